@@ -1,0 +1,130 @@
+/*
+ * zcgvs_sm100.h - C ABI of the B200 (sm_100a) search hot path.
+ *
+ * This library replaces the reference engine's src/cuda/ directory (the brute-force scan,
+ * multi-pass top-k, gather-rescore, BM25 and converter launchers) with fused sm_100a kernels
+ * behind a plain C interface: pointers, sizes and an opaque stream handle, no C++ or torch
+ * types. The C++ declarations of the reference (include/zcgvs/cuda/*.cuh, Searcher) are
+ * re-implemented on top of this ABI in include/zcgvs/.
+ *
+ * Conventions shared by every entry point:
+ *   - All device memory is owned by the caller. Entry points never allocate, never
+ *     synchronise the stream and can be captured into a CUDA graph. Scratch is passed in as
+ *     an explicit workspace whose size comes from the matching *_workspace_bytes() query.
+ *   - A workspace must be zero-filled once before its first use (zcgvs_workspace_init or a
+ *     cudaMemset); every call leaves its counters at zero again, so it can be reused by the
+ *     next call on the same stream without re-initialisation.
+ *   - `stream` is a cudaStream_t passed as void*; NULL is the legacy default stream.
+ *   - Zero-sized problems (doc_count, batch or dim <= 0) are silent no-ops returning
+ *     ZCGVS_OK, as in the reference launchers (src/cuda/similarity.cu:356-358).
+ *   - Errors are reported as zcgvs_status codes; zcgvs_last_error_message() returns a
+ *     thread-local description of the last failure on the calling thread.
+ *   - Top-k order is the total order (score descending, document id ascending), identical to
+ *     the reference CPU oracle's std::stable_sort (tests/cpp/cpu_reference.hpp:26-34). Padding
+ *     slots hold id -1 and score -FLT_MAX. Masked documents score exactly -FLT_MAX
+ *     (src/cuda/similarity.cu:109-113) and therefore rank after every unmasked document.
+ */
+#ifndef ZCGVS_SM100_H
+#define ZCGVS_SM100_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* Status codes. ZCGVS_ERR_INVALID_ARG mirrors the reference's std::invalid_argument
+ * (src/cuda/topk.cu:146-153, src/cuda/similarity.cu:326-329), ZCGVS_ERR_CUDA its CudaError
+ * (include/zcgvs/core/cuda_check.hpp:10-37). ZCGVS_ERR_DEVICE_STATUS means a kernel gave up a
+ * bounded wait and recorded it in the workspace status word. */
+typedef enum zcgvs_status {
+    ZCGVS_OK = 0,
+    ZCGVS_ERR_INVALID_ARG = 1,
+    ZCGVS_ERR_CUDA = 2,
+    ZCGVS_ERR_UNSUPPORTED = 3,
+    ZCGVS_ERR_DEVICE_STATUS = 4
+} zcgvs_status;
+
+/* Storage precision of a corpus. Codes 0-3 equal the reference ScalarType
+ * (include/zcgvs/core/scalar_type.hpp:12-17) and the ZCVE dtype field
+ * (include/zcgvs/data/binary_format.hpp:59-62). ZCGVS_DTYPE_I8_ROW is an extension: int8 rows
+ * with one fp32 scale per row, scored as an exact int32 dot of the int8 query and row times
+ * the two scales. */
+typedef enum zcgvs_dtype {
+    ZCGVS_DTYPE_F32 = 0,
+    ZCGVS_DTYPE_F16 = 1,
+    ZCGVS_DTYPE_I8 = 2,
+    ZCGVS_DTYPE_BINARY = 3,
+    ZCGVS_DTYPE_I8_ROW = 4
+} zcgvs_dtype;
+
+/* Similarity metric; codes equal the reference Metric (include/zcgvs/core/metric.hpp:8-12).
+ * Cosine is the dot product of pre-normalised rows (include/zcgvs/cuda/decode.cuh:30-42). */
+typedef enum zcgvs_metric {
+    ZCGVS_METRIC_COSINE = 0,
+    ZCGVS_METRIC_DOT = 1,
+    ZCGVS_METRIC_L2 = 2
+} zcgvs_metric;
+
+/* Largest k / candidate count any selection supports; equals topKMaxK() of the reference
+ * (src/cuda/topk.cu:117). */
+#define ZCGVS_MAX_K 1024
+
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+int zcgvs_version(void);
+
+/* Thread-local description of the last error returned on this thread ("" if none). */
+const char* zcgvs_last_error_message(void);
+
+/* Zero-fills `bytes` of a workspace on `stream` (a cudaMemsetAsync). */
+int zcgvs_workspace_init(void* workspace, size_t bytes, void* stream);
+
+/* Copies the device status word of a workspace to *status and synchronises `stream`.
+ * 0 means every bounded wait of every call that used the workspace completed. */
+int zcgvs_workspace_status(const void* workspace, size_t bytes, uint32_t* status, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Fused scan + top-k. Replaces the launchSimilarity -> launchTopK chain of
+ * Searcher::recordPipeline (src/search/searcher.cpp:230-232, :281-284): scores are kept on
+ * chip and only the final [batch, k] selection is written.
+ *
+ *   corpus      : [doc_count, row] in `dtype` storage, row-major, rows of rowBytes(dtype, dim)
+ *                 bytes (binary rows are ceil(dim/32) uint32 words).
+ *   scale       : per-matrix dequantisation scale for ZCGVS_DTYPE_I8 (ignored otherwise).
+ *   row_scales  : [doc_count] fp32 per-row scales for ZCGVS_DTYPE_I8_ROW (NULL otherwise).
+ *   queries     : [batch, dim] fp32 on the device. The kernel widens (fp16/int8 paths, which
+ *                 score against the fp32 query exactly as src/cuda/similarity.cu:83-164 does),
+ *                 quantises per row (I8_ROW: s = max|x|/127, q = clamp(rint(x/s), +-127)) or
+ *                 packs sign bits (BINARY, bit b of word w = dim 32w+b, set when x >= 0).
+ *   mask        : optional [doc_count] uint8 allow-mask; 0 = excluded (scores -FLT_MAX).
+ *   metric      : ZCGVS_METRIC_*; L2 scores -sum((q-x)^2). Ignored for BINARY, whose score is
+ *                 (dim - 2*hamming)/dim (include/zcgvs/cuda/decode.cuh:45-47). L2 is
+ *                 unsupported for I8_ROW.
+ *   k           : 1..min(ZCGVS_MAX_K, doc_count).
+ *   id_base     : added to every row index (global ids of a row shard); 0 for a whole corpus.
+ *   out_indices : [batch, k] int32 document ids, descending by score.
+ *   out_scores  : [batch, k] fp32 scores.
+ * --------------------------------------------------------------------------------------- */
+size_t zcgvs_scan_topk_workspace_bytes(int dtype, int64_t doc_count, int dim, int batch, int k);
+
+int zcgvs_scan_topk(const void* corpus, int dtype, float scale, const float* row_scales,
+                    int64_t doc_count, int dim, const float* queries, int batch,
+                    const uint8_t* mask, int metric, int k, int id_base, int* out_indices,
+                    float* out_scores, void* workspace, size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Score matrix. Same contract as the reference launchSimilarity
+ * (include/zcgvs/cuda/similarity.cuh:20-30): writes [batch, doc_count] fp32 scores. Float
+ * storage takes fp32 queries; binary storage takes packed query words [batch, ceil(dim/32)]
+ * (as produced by zcgvs_pack_binary), like the reference.
+ * --------------------------------------------------------------------------------------- */
+int zcgvs_similarity(const void* corpus, int dtype, float scale, const float* row_scales,
+                     int64_t doc_count, int dim, const void* queries, int batch,
+                     const uint8_t* mask, int metric, float* scores, void* stream);
+
+#ifdef __cplusplus
+}  /* extern "C" */
+#endif
+
+#endif /* ZCGVS_SM100_H */

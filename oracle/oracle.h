@@ -1,0 +1,48 @@
+/*
+ * oracle.h - CPU restatement of the reference search path. TEST INFRASTRUCTURE ONLY:
+ * called by tests/, __graft_entry__.smoke() and bench.py's cpu_baseline leg as the checker,
+ * never by the product library.
+ */
+#ifndef ZCGVS_ORACLE_H
+#define ZCGVS_ORACLE_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+enum { ORC_DTYPE_F32 = 0, ORC_DTYPE_F16 = 1, ORC_DTYPE_I8 = 2, ORC_DTYPE_BINARY = 3, ORC_DTYPE_I8_ROW = 4 };
+enum { ORC_METRIC_COSINE = 0, ORC_METRIC_DOT = 1, ORC_METRIC_L2 = 2 };
+
+uint16_t orc_f32_to_f16(float value);
+float orc_f16_to_f32(uint16_t h);
+void orc_convert_f16(const float* src, size_t count, uint16_t* dst);
+float orc_matrix_scale(const float* src, size_t count);
+void orc_quantize_i8(const float* src, size_t count, float scale, int8_t* dst);
+void orc_quantize_rows_i8(const float* src, int64_t rows, int dim, int8_t* dst, float* scales);
+void orc_pack_binary(const float* src, int64_t rows, int dim, uint32_t* dst);
+int orc_hamming(const uint32_t* a, const uint32_t* b, int words);
+void orc_scores(int dtype, const void* corpus, float scale, const float* row_scales, int64_t n,
+                int dim, const float* queries, int batch, const uint8_t* mask, int metric,
+                float* out);
+void orc_topk(const float* scores, int64_t n, int batch, int k, int id_base, int32_t* out_idx,
+              float* out_scores);
+void orc_scan_topk(int dtype, const void* corpus, float scale, const float* row_scales, int64_t n,
+                   int dim, const float* queries, int batch, const uint8_t* mask, int metric,
+                   int k, int id_base, int32_t* out_idx, float* out_scores);
+
+/* Seeded inputs identical to the reference harnesses' randomMatrix
+ * (tests/cpp/test_pipeline.cu:20-31): std::mt19937(seed), std::normal_distribution<float>(0,1),
+ * then each row L2-normalised in fp32 (tests/cpp/cpu_reference.hpp:36-49). */
+void orc_gen_normal_rows(int64_t rows, int dim, uint32_t seed, int normalize, float* out);
+/* std::mt19937(seed) + std::uniform_real_distribution<float>(lo, hi), the generator of
+ * tests/cpp/test_topk.cu:14-20 and test_metrics_filter.cu:27-37. */
+void orc_gen_uniform(size_t count, uint32_t seed, float lo, float hi, float* out);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif

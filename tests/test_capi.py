@@ -1,0 +1,59 @@
+"""CPU tier: the C-ABI library loads, exports every symbol include/*.h declares, and rejects
+invalid arguments before touching a device (mirroring the reference's std::invalid_argument
+cases, src/cuda/topk.cu:146-153 and src/search/searcher.cpp:91-135)."""
+
+from __future__ import annotations
+
+import ctypes
+import re
+
+import pytest
+
+from conftest import ROOT
+
+
+def declared_functions():
+    names = set()
+    for header in (ROOT / "include").glob("*.h"):
+        text = re.sub(r"/\*.*?\*/", "", header.read_text(), flags=re.S)
+        names.update(re.findall(r"\b(zcgvs_[a-z0-9_]+)\s*\(", text))
+    return sorted(names)
+
+
+def test_header_declares_entry_points():
+    names = declared_functions()
+    assert "zcgvs_scan_topk" in names and "zcgvs_similarity" in names
+
+
+def test_library_exports_every_declared_symbol(zc):
+    lib = zc.lib()
+    for name in declared_functions():
+        assert hasattr(lib, name), f"{name} declared in include/ but not exported"
+        assert name in zc.SIGNATURES, f"{name} has no ctypes signature"
+
+
+def test_version(zc):
+    assert zc.lib().zcgvs_version() >= 100
+
+
+@pytest.mark.parametrize("k,n,expect", [(0, 100, "k must be positive"), (1025, 5000, "exceeds kernel capacity"),
+                                        (101, 100, "exceeds corpus size")])
+def test_scan_topk_rejects_bad_k(zc, k, n, expect):
+    fake = ctypes.c_void_p(16)
+    status = zc.lib().zcgvs_scan_topk(fake, zc.DTYPE_F32, 1.0, None, n, 8, fake, 1, None, zc.METRIC_DOT, k, 0,
+                                      fake, fake, fake, 1 << 20, None)
+    assert status == zc.ERR_INVALID_ARG
+    assert expect in zc.lib().zcgvs_last_error_message().decode()
+
+
+def test_zero_sized_problem_is_a_noop(zc):
+    assert zc.lib().zcgvs_scan_topk(None, zc.DTYPE_F32, 1.0, None, 0, 8, None, 1, None, 0, 10, 0,
+                                    None, None, None, 0, None) == zc.OK
+    assert zc.lib().zcgvs_similarity(None, zc.DTYPE_F32, 1.0, None, 10, 8, None, 0, None, 0, None, None) == zc.OK
+
+
+def test_per_row_int8_needs_scales(zc):
+    fake = ctypes.c_void_p(16)
+    status = zc.lib().zcgvs_scan_topk(fake, zc.DTYPE_I8_ROW, 1.0, None, 100, 8, fake, 1, None, zc.METRIC_DOT, 10, 0,
+                                      fake, fake, fake, 1 << 20, None)
+    assert status == zc.ERR_INVALID_ARG

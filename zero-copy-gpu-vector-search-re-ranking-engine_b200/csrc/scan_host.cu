@@ -1,0 +1,325 @@
+// Host side of the streaming scan: launch planning (tile size, stage depth, query pass width,
+// grid), workspace layout, argument validation and the C-ABI entry points zcgvs_scan_topk and
+// zcgvs_similarity.
+#include <algorithm>
+#include <climits>
+#include <string>
+
+#include "host_common.h"
+#include "scan_instances.h"
+#include "zcgvs_sm100.h"
+
+namespace zc {
+
+namespace {
+
+constexpr int kTileTargetBytes = 32 * 1024;
+constexpr int kMaxStages = 8;
+constexpr int kMaxTileRows = 512;
+constexpr size_t kWorkspaceAlign = 256;
+
+struct ScanPlan {
+    int mode = 0;
+    int qb = 1;
+    int jc = 0;
+    bool l2 = false;
+    bool emit = false;
+    int row_bytes = 0;
+    int stride = 0;
+    int nch = 0;
+    int elems_per_row = 0;
+    bool use_tma = false;
+    int rows_per_tile = 0;
+    long long ntiles = 0;
+    int grid_rows = 0;  // CTAs along the corpus (gridDim.y)
+    int passes = 0;     // query passes (gridDim.x)
+    int cap = 0;
+    int stages = 1;
+    int query_bytes = 0;
+    int smem_query_off = 0;
+    int smem_topk_off = 0;
+    int smem_bar_off = 0;
+    int smem_total = 0;
+    size_t ws_header = 0;
+    size_t ws_total = 0;
+};
+
+int mode_of(int dtype) {
+    switch (dtype) {
+        case ZCGVS_DTYPE_F32: return kModeF32;
+        case ZCGVS_DTYPE_F16: return kModeF16;
+        case ZCGVS_DTYPE_I8: return kModeI8M;
+        case ZCGVS_DTYPE_BINARY: return kModeBin;
+        case ZCGVS_DTYPE_I8_ROW: return kModeI8R;
+        default: return -1;
+    }
+}
+
+int query_bytes_of(int mode, int stride) {
+    switch (mode) {
+        case kModeF32: return stride;       // 4 fp32 per 16-byte chunk
+        case kModeF16: return 2 * stride;   // 8 fp32 per chunk
+        case kModeI8M: return 4 * stride;   // 16 fp32 per chunk
+        default: return stride;             // int8 values / packed words, like the rows
+    }
+}
+
+// Fills the shared-memory layout for a given pass width / tile size; false if it cannot fit.
+bool layout(ScanPlan& plan, int budget) {
+    const int tile_bytes = plan.rows_per_tile * plan.stride;
+    const int query = plan.qb * plan.query_bytes;
+    const int topk = plan.emit ? 0 : plan.qb * (plan.cap * 8 + 16);
+    const int fixed = static_cast<int>(round_up(query, 128)) + static_cast<int>(round_up(topk, 128)) +
+                      kMaxStages * 8 + 128;
+    int stages = 1;
+    if (plan.use_tma) {
+        stages = std::min(kMaxStages, (budget - fixed) / std::max(tile_bytes, 1));
+        if (stages < 2) return false;
+    } else if (fixed + tile_bytes > budget) {
+        return false;
+    }
+    plan.stages = stages;
+    plan.smem_query_off = static_cast<int>(round_up(static_cast<size_t>(stages) * tile_bytes, 128));
+    plan.smem_topk_off = plan.smem_query_off + static_cast<int>(round_up(query, 128));
+    plan.smem_bar_off = plan.smem_topk_off + static_cast<int>(round_up(topk, 128));
+    plan.smem_total = plan.smem_bar_off + kMaxStages * 8;
+    return plan.smem_total <= budget;
+}
+
+// Builds the launch plan. Returns ZCGVS_OK or an error status (message recorded).
+int make_plan(int dtype, long long n, int dim, int batch, int k, int metric, bool emit,
+              bool aligned, ScanPlan& plan) {
+    plan.mode = mode_of(dtype);
+    if (plan.mode < 0) return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: unknown storage dtype " + std::to_string(dtype));
+    if (metric < ZCGVS_METRIC_COSINE || metric > ZCGVS_METRIC_L2) {
+        return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: unknown metric " + std::to_string(metric));
+    }
+    plan.l2 = (metric == ZCGVS_METRIC_L2) && plan.mode != kModeBin;
+    if (plan.l2 && plan.mode == kModeI8R) {
+        return fail(ZCGVS_ERR_UNSUPPORTED, "zcgvs: the per-row int8 store scores dot/cosine only");
+    }
+    plan.emit = emit;
+    const long long rb = row_bytes_of(dtype, dim);
+    plan.row_bytes = static_cast<int>(rb);
+    plan.stride = static_cast<int>(round_up(static_cast<size_t>(rb), 16));
+    plan.nch = plan.stride / 16;
+    plan.elems_per_row = (plan.mode == kModeBin) ? (dim + 31) / 32 : dim;
+    plan.use_tma = aligned && (rb % 16 == 0);
+    plan.query_bytes = query_bytes_of(plan.mode, plan.stride);
+
+    const int budget = device_max_smem() - 2048;
+    int rows = std::max(1, kTileTargetBytes / plan.stride);
+    rows = std::min(rows, kMaxTileRows);
+    if (rows >= 16) rows &= ~15;
+    int qb = emit ? 8 : (batch <= 1 ? 1 : std::min(8, next_pow2(batch)));
+    const int sms = device_sm_count();
+
+    for (;;) {
+        plan.qb = qb;
+        plan.rows_per_tile = rows;
+        plan.ntiles = (n + rows - 1) / rows;
+        plan.grid_rows = static_cast<int>(std::min<long long>(plan.ntiles, sms));
+        plan.cap = emit ? 0 : next_pow2(k + std::max(rows, plan.grid_rows));
+        if (layout(plan, budget)) break;
+        if (rows > 1) {
+            rows = std::max(1, rows / 2);
+            continue;
+        }
+        if (qb > 1) {
+            qb /= 2;
+            rows = std::min(std::max(1, kTileTargetBytes / plan.stride), kMaxTileRows);
+            if (rows >= 16) rows &= ~15;
+            continue;
+        }
+        return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs similarity: embedding dim " + std::to_string(dim) +
+                                               " needs more shared memory than a block can stage");
+    }
+    plan.passes = (batch + plan.qb - 1) / plan.qb;
+    plan.jc = 0;
+    if (!emit && plan.qb == 1 && !plan.l2 && plan.mode != kModeBin && plan.nch <= 128) {
+        plan.jc = (plan.nch + 31) / 32;
+    }
+    plan.ws_header = round_up(16 + 4 * static_cast<size_t>(plan.passes), kWorkspaceAlign);
+    plan.ws_total = emit ? 0
+                         : plan.ws_header + static_cast<size_t>(batch) * plan.grid_rows *
+                                                static_cast<size_t>(k) * 8;
+    return ZCGVS_OK;
+}
+
+ScanKernelFn lookup(const ScanPlan& plan) {
+    switch (plan.mode) {
+        case kModeF32: return scan_lookup_f32(plan.qb, plan.jc, plan.l2, plan.emit);
+        case kModeF16: return scan_lookup_f16(plan.qb, plan.jc, plan.l2, plan.emit);
+        case kModeI8M:
+        case kModeI8R: return scan_lookup_i8(plan.mode, plan.qb, plan.jc, plan.l2, plan.emit);
+        case kModeBin: return scan_lookup_bin(plan.qb, plan.emit);
+        default: return nullptr;
+    }
+}
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15u) == 0; }
+
+bool aligned_to(const void* p, uintptr_t bytes) {
+    return (reinterpret_cast<uintptr_t>(p) & (bytes - 1u)) == 0;
+}
+
+// Every device pointer must be aligned to its element type (the plain-copy staging path reads
+// whole elements); fp32 / int32 buffers to 4 bytes, fp16 rows to 2.
+int check_alignment(int dtype, const void* corpus, const void* row_scales, const void* queries,
+                    const void* out_a, const void* out_b) {
+    const uintptr_t elem = (dtype == ZCGVS_DTYPE_F32 || dtype == ZCGVS_DTYPE_BINARY) ? 4u
+                           : (dtype == ZCGVS_DTYPE_F16)                               ? 2u
+                                                                                      : 1u;
+    if (!aligned_to(corpus, elem) || !aligned_to(row_scales, 4) || !aligned_to(queries, 4) ||
+        !aligned_to(out_a, 4) || !aligned_to(out_b, 4)) {
+        return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: a device pointer is not aligned to its element size");
+    }
+    return ZCGVS_OK;
+}
+
+int launch(const ScanPlan& plan, ScanParams& params, cudaStream_t stream) {
+    const ScanKernelFn kernel = lookup(plan);
+    if (kernel == nullptr) {
+        return fail(ZCGVS_ERR_UNSUPPORTED, "zcgvs: no scan kernel variant for this configuration");
+    }
+    cudaError_t status = ensure_smem_optin(reinterpret_cast<const void*>(kernel));
+    if (status != cudaSuccess) return fail_cuda(status, "cudaFuncSetAttribute(scan_kernel)");
+    params.rows_per_tile = plan.rows_per_tile;
+    params.ntiles = plan.ntiles;
+    params.use_tma = plan.use_tma ? 1 : 0;
+    params.stages = plan.stages;
+    params.cap = plan.cap;
+    params.row_bytes = plan.row_bytes;
+    params.stride = plan.stride;
+    params.nch = plan.nch;
+    params.elems_per_row = plan.elems_per_row;
+    params.query_bytes = plan.query_bytes;
+    params.smem_query_off = plan.smem_query_off;
+    params.smem_topk_off = plan.smem_topk_off;
+    params.smem_bar_off = plan.smem_bar_off;
+    const dim3 grid(static_cast<unsigned>(plan.passes), static_cast<unsigned>(plan.grid_rows));
+    kernel<<<grid, kScanThreads, plan.smem_total, stream>>>(params);
+    status = cudaGetLastError();
+    if (status != cudaSuccess) return fail_cuda(status, "scan_kernel launch");
+    return ok();
+}
+
+}  // namespace
+
+}  // namespace zc
+
+extern "C" {
+
+size_t zcgvs_scan_topk_workspace_bytes(int dtype, int64_t doc_count, int dim, int batch, int k) {
+    if (doc_count <= 0 || dim <= 0 || batch <= 0 || k <= 0) return 0;
+    // The plan may differ with the corpus alignment (bulk-copy vs plain staging) and the
+    // metric, so report the largest workspace any of them needs.
+    size_t bytes = 0;
+    const int metrics[2] = {ZCGVS_METRIC_DOT, ZCGVS_METRIC_L2};
+    for (const int metric : metrics) {
+        for (const bool aligned : {true, false}) {
+            zc::ScanPlan plan;
+            if (zc::make_plan(dtype, doc_count, dim, batch, std::min(k, ZCGVS_MAX_K), metric,
+                              false, aligned, plan) == ZCGVS_OK) {
+                bytes = std::max(bytes, plan.ws_total);
+            }
+        }
+    }
+    zc::ok();
+    return bytes;
+}
+
+int zcgvs_scan_topk(const void* corpus, int dtype, float scale, const float* row_scales,
+                    int64_t doc_count, int dim, const float* queries, int batch,
+                    const uint8_t* mask, int metric, int k, int id_base, int* out_indices,
+                    float* out_scores, void* workspace, size_t workspace_bytes, void* stream) {
+    using namespace zc;
+    if (doc_count <= 0 || batch <= 0 || dim <= 0) return ok();
+    if (k <= 0) return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: k must be positive");
+    if (k > ZCGVS_MAX_K) {
+        return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: k=" + std::to_string(k) + " exceeds kernel capacity " +
+                                               std::to_string(ZCGVS_MAX_K));
+    }
+    if (doc_count > INT_MAX) {
+        return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: corpus exceeds the supported document count");
+    }
+    if (k > doc_count) {
+        return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: k=" + std::to_string(k) + " exceeds corpus size " +
+                                               std::to_string(doc_count));
+    }
+    if (id_base < 0 || static_cast<long long>(id_base) + doc_count - 1 > INT_MAX) {
+        return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: id_base + doc_count exceeds the int32 id range");
+    }
+    if (corpus == nullptr || queries == nullptr || out_indices == nullptr || out_scores == nullptr) {
+        return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: null corpus, query or output pointer");
+    }
+    if (dtype == ZCGVS_DTYPE_I8_ROW && row_scales == nullptr) {
+        return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: the per-row int8 store needs row_scales");
+    }
+    int status = check_alignment(dtype, corpus, row_scales, queries, out_indices, out_scores);
+    if (status != ZCGVS_OK) return status;
+    ScanPlan plan;
+    status = make_plan(dtype, doc_count, dim, batch, k, metric, false, aligned16(corpus), plan);
+    if (status != ZCGVS_OK) return status;
+    if (workspace == nullptr || workspace_bytes < plan.ws_total) {
+        return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: workspace smaller than zcgvs_scan_topk_workspace_bytes()");
+    }
+    if (!aligned16(workspace)) return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: workspace must be 16-byte aligned");
+
+    ScanParams params{};
+    params.corpus = static_cast<const uint8_t*>(corpus);
+    params.row_scales = row_scales;
+    params.scale = scale;
+    params.n = doc_count;
+    params.dim = dim;
+    params.queries = queries;
+    params.query_packed = 0;
+    params.batch = batch;
+    params.mask = mask;
+    params.k = k;
+    params.id_base = static_cast<unsigned int>(id_base);
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    params.status = reinterpret_cast<unsigned int*>(ws);
+    params.counters = reinterpret_cast<unsigned int*>(ws + 16);
+    params.lists = reinterpret_cast<unsigned long long*>(ws + plan.ws_header);
+    params.out_idx = out_indices;
+    params.out_scores = out_scores;
+    params.out_matrix = nullptr;
+    return launch(plan, params, static_cast<cudaStream_t>(stream));
+}
+
+int zcgvs_similarity(const void* corpus, int dtype, float scale, const float* row_scales,
+                     int64_t doc_count, int dim, const void* queries, int batch,
+                     const uint8_t* mask, int metric, float* scores, void* stream) {
+    using namespace zc;
+    if (doc_count <= 0 || batch <= 0 || dim <= 0) return ok();
+    if (doc_count > INT_MAX) {
+        return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: corpus exceeds the supported document count");
+    }
+    if (corpus == nullptr || queries == nullptr || scores == nullptr) {
+        return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: null corpus, query or score pointer");
+    }
+    if (dtype == ZCGVS_DTYPE_I8_ROW && row_scales == nullptr) {
+        return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: the per-row int8 store needs row_scales");
+    }
+    int status = check_alignment(dtype, corpus, row_scales, queries, scores, nullptr);
+    if (status != ZCGVS_OK) return status;
+    ScanPlan plan;
+    status = make_plan(dtype, doc_count, dim, batch, 1, metric, true, aligned16(corpus), plan);
+    if (status != ZCGVS_OK) return status;
+    ScanParams params{};
+    params.corpus = static_cast<const uint8_t*>(corpus);
+    params.row_scales = row_scales;
+    params.scale = scale;
+    params.n = doc_count;
+    params.dim = dim;
+    params.queries = queries;
+    params.query_packed = (dtype == ZCGVS_DTYPE_BINARY) ? 1 : 0;
+    params.batch = batch;
+    params.mask = mask;
+    params.k = 1;
+    params.out_matrix = scores;
+    return launch(plan, params, static_cast<cudaStream_t>(stream));
+}
+
+}  // extern "C"

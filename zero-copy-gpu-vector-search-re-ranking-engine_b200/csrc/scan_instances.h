@@ -1,0 +1,46 @@
+// Kernel lookup tables of the streaming scan. Each scan_<mode>.cu instantiates the variants
+// of one storage mode; the launcher picks one by (query pass width, register chunk count,
+// metric, output form).
+#pragma once
+
+#include "scan_kernel.cuh"
+
+namespace zc {
+
+using ScanKernelFn = void (*)(const ScanParams);
+
+ScanKernelFn scan_lookup_f32(int qb, int jc, bool l2, bool emit);
+ScanKernelFn scan_lookup_f16(int qb, int jc, bool l2, bool emit);
+ScanKernelFn scan_lookup_i8(int mode, int qb, int jc, bool l2, bool emit);
+ScanKernelFn scan_lookup_bin(int qb, bool emit);
+
+}  // namespace zc
+
+// Instantiation helpers: the top-k variants for query pass widths 1/2/4/8 (generic chunk loop)
+// plus the register-resident single-query fast path for 1-4 chunks per lane, and one
+// score-matrix variant (8 queries per pass).
+#define ZC_SCAN_TOPK_TABLE(MODE, L2)                                          \
+    if (emit) {                                                               \
+        if (qb == 8 && jc == 0) return &scan_kernel<MODE, 8, 0, L2, true>;    \
+        return nullptr;                                                       \
+    }                                                                         \
+    if (jc == 0) {                                                            \
+        switch (qb) {                                                         \
+            case 1: return &scan_kernel<MODE, 1, 0, L2, false>;               \
+            case 2: return &scan_kernel<MODE, 2, 0, L2, false>;               \
+            case 4: return &scan_kernel<MODE, 4, 0, L2, false>;               \
+            case 8: return &scan_kernel<MODE, 8, 0, L2, false>;               \
+            default: return nullptr;                                          \
+        }                                                                     \
+    }
+
+#define ZC_SCAN_FAST_TABLE(MODE)                                              \
+    if (!emit && qb == 1) {                                                   \
+        switch (jc) {                                                         \
+            case 1: return &scan_kernel<MODE, 1, 1, false, false>;            \
+            case 2: return &scan_kernel<MODE, 1, 2, false, false>;            \
+            case 3: return &scan_kernel<MODE, 1, 3, false, false>;            \
+            case 4: return &scan_kernel<MODE, 1, 4, false, false>;            \
+            default: break;                                                   \
+        }                                                                     \
+    }

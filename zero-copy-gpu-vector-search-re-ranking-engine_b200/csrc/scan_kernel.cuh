@@ -1,0 +1,500 @@
+// Streaming corpus scan with fused top-k for single- and small-batch queries.
+//
+// Replaces the reference pipeline `similarityScanKernel`/`hammingScanKernel`
+// (src/cuda/similarity.cu:83-238) -> [batch, N] fp32 score matrix in HBM -> `launchTopK`
+// (src/cuda/topk.cu:132-189) with one kernel per call:
+//
+//   * Work split: the corpus is cut into tiles of R whole rows; CTA y of the grid owns a
+//     contiguous range of tiles, CTA x a pass of QB queries (x varies fastest, so the passes
+//     that read the same rows run side by side and share L2).
+//   * Staging: when rows are 16-byte multiples, one thread moves each tile global -> shared
+//     with a single bulk async copy (cp.async.bulk, the TMA engine's 1-D form) into an
+//     S-deep ring of stages tracked by mbarriers; otherwise all threads copy rows into a
+//     zero-padded 16-byte stride (the reference's scalar fallback, :273-287).
+//   * Scoring: warp per row for fp32 / fp16 / int8 rows, lanes striding 16-byte chunks;
+//     partial sums of the QB queries are combined with one transposing warp reduction.
+//     Binary rows are thread per row (XOR + popc), like the reference's Hamming kernel.
+//   * Selection: scores go straight into the CTA's on-chip top-k (topk_cta.cuh); at the end
+//     each CTA writes k keys per query to the workspace and the last CTA to finish a pass
+//     merges them and writes the final [QB, k] ids and scores.
+//
+// Numerics follow the reference: fp16 and int8 rows are widened to fp32 and multiplied by the
+// fp32 query (decode.cuh:22-43); L2 is -sum((q - x)^2); Hamming scores are
+// (dim - 2 h) / dim. The per-row int8 mode scores float(int32 dot) * s_q * s_row exactly.
+#pragma once
+
+#include <type_traits>
+
+#include "common.cuh"
+#include "topk_cta.cuh"
+
+namespace zc {
+
+enum ScanMode : int { kModeF32 = 0, kModeF16 = 1, kModeI8M = 2, kModeBin = 3, kModeI8R = 4 };
+
+constexpr int kScanThreads = 512;
+constexpr int kScanWarps = kScanThreads / 32;
+
+struct ScanParams {
+    const uint8_t* corpus;
+    const float* row_scales;       // kModeI8R: [n]
+    float scale;                   // kModeI8M
+    long long n;                   // rows
+    int dim;
+    int row_bytes;                 // bytes of one row in global memory
+    int stride;                    // bytes of one row in shared memory (multiple of 16)
+    int nch;                       // stride / 16
+    int elems_per_row;             // storage elements per global row (dim, or words)
+    const void* queries;           // fp32 [batch, dim], or packed words when query_packed
+    int query_packed;
+    int batch;
+    const uint8_t* mask;
+    int k;
+    int cap;                       // top-k buffer capacity (power of two)
+    int rows_per_tile;
+    long long ntiles;
+    int use_tma;
+    int stages;
+    unsigned int id_base;
+    unsigned long long* lists;     // [batch][gridDim.y][k]
+    unsigned int* counters;        // [gridDim.x]
+    unsigned int* status;
+    int* out_idx;                  // [batch][k]
+    float* out_scores;             // [batch][k]
+    float* out_matrix;             // score-matrix mode: [batch][n]
+    int query_bytes;               // bytes of one staged query
+    int smem_query_off;
+    int smem_topk_off;
+    int smem_bar_off;
+};
+
+template <int MODE>
+struct ModeTraits;
+template <>
+struct ModeTraits<kModeF32> {
+    static constexpr int kEpc = 4;  // fp32 query values per 16-byte chunk
+    static constexpr int kElemBytes = 4;
+};
+template <>
+struct ModeTraits<kModeF16> {
+    static constexpr int kEpc = 8;
+    static constexpr int kElemBytes = 2;
+};
+template <>
+struct ModeTraits<kModeI8M> {
+    static constexpr int kEpc = 16;
+    static constexpr int kElemBytes = 1;
+};
+template <>
+struct ModeTraits<kModeI8R> {
+    static constexpr int kEpc = 4;  // four packed int8x4 words per chunk
+    static constexpr int kElemBytes = 1;
+};
+template <>
+struct ModeTraits<kModeBin> {
+    static constexpr int kEpc = 4;  // four 32-bit words per chunk
+    static constexpr int kElemBytes = 4;
+};
+
+__device__ __forceinline__ uint4 lds128(const void* p) {
+    return *reinterpret_cast<const uint4*>(p);
+}
+
+// Accumulates one 16-byte corpus chunk against one query's matching values.
+template <int MODE, bool L2>
+__device__ __forceinline__ void accumulate_chunk(const uint4 raw, const float* qv, float scale,
+                                                 float& acc) {
+    auto step = [&](float x, float q) {
+        if constexpr (L2) {
+            const float d = q - x;
+            acc = fmaf(d, d, acc);
+        } else {
+            acc = fmaf(q, x, acc);
+        }
+    };
+    if constexpr (MODE == kModeF32) {
+        step(__uint_as_float(raw.x), qv[0]);
+        step(__uint_as_float(raw.y), qv[1]);
+        step(__uint_as_float(raw.z), qv[2]);
+        step(__uint_as_float(raw.w), qv[3]);
+    } else if constexpr (MODE == kModeF16) {
+        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            const float2 f = __half22float2(*reinterpret_cast<const __half2*>(&w[i]));
+            step(f.x, qv[2 * i]);
+            step(f.y, qv[2 * i + 1]);
+        }
+    } else if constexpr (MODE == kModeI8M) {
+        const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+#pragma unroll
+            for (int b = 0; b < 4; ++b) {
+                const int8_t v = static_cast<int8_t>((w[i] >> (8 * b)) & 0xffu);
+                step(static_cast<float>(v) * scale, qv[4 * i + b]);
+            }
+        }
+    }
+}
+
+__device__ __forceinline__ int dp4a_chunk(const uint4 raw, const int* qw, int acc) {
+    acc = __dp4a(static_cast<int>(raw.x), qw[0], acc);
+    acc = __dp4a(static_cast<int>(raw.y), qw[1], acc);
+    acc = __dp4a(static_cast<int>(raw.z), qw[2], acc);
+    acc = __dp4a(static_cast<int>(raw.w), qw[3], acc);
+    return acc;
+}
+
+// Stages the query pass into shared memory in the form the row loop consumes: fp32 values
+// zero-padded to whole chunks, per-row int8 quantisation (I8R) or packed sign bits (Bin).
+template <int MODE, int QB>
+__device__ void stage_queries(const ScanParams& p, uint8_t* qsmem, float* qscale, int q0,
+                              int nq, float* red /* [kScanWarps * QB] */) {
+    const int tid = threadIdx.x;
+    if constexpr (MODE == kModeF32 || MODE == kModeF16 || MODE == kModeI8M) {
+        const int qf = p.query_bytes / 4;
+        float* dst = reinterpret_cast<float*>(qsmem);
+        const float* src = static_cast<const float*>(p.queries);
+        for (int e = tid; e < QB * qf; e += kScanThreads) {
+            const int q = e / qf;
+            const int j = e - q * qf;
+            dst[e] = (q < nq && j < p.dim) ? src[static_cast<size_t>(q0 + q) * p.dim + j] : 0.0f;
+        }
+    } else if constexpr (MODE == kModeI8R) {
+        // s = max|x| / 127 (1 when the row is all zero), q = clamp(rint(x * (1/s)), -127, 127):
+        // the reference quantiser (src/cuda/convert.cu:25-32) applied with a per-row scale.
+        const float* src = static_cast<const float*>(p.queries);
+        float amax[QB];
+#pragma unroll
+        for (int q = 0; q < QB; ++q) amax[q] = 0.0f;
+        for (int j = tid; j < p.dim; j += kScanThreads) {
+#pragma unroll
+            for (int q = 0; q < QB; ++q) {
+                if (q < nq) amax[q] = fmaxf(amax[q], fabsf(src[static_cast<size_t>(q0 + q) * p.dim + j]));
+            }
+        }
+#pragma unroll
+        for (int q = 0; q < QB; ++q) {
+            const float m = warp_max_f32(amax[q]);
+            if ((tid & 31) == 0) red[q * kScanWarps + (tid >> 5)] = m;
+        }
+        __syncthreads();
+        if (tid < QB) {
+            float m = 0.0f;
+            for (int w = 0; w < kScanWarps; ++w) m = fmaxf(m, red[tid * kScanWarps + w]);
+            qscale[tid] = (m > 0.0f) ? __fdiv_rn(m, 127.0f) : 1.0f;
+        }
+        __syncthreads();
+        int8_t* dst = reinterpret_cast<int8_t*>(qsmem);
+        for (int e = tid; e < QB * p.query_bytes; e += kScanThreads) {
+            const int q = e / p.query_bytes;
+            const int j = e - q * p.query_bytes;
+            int8_t v = 0;
+            if (q < nq && j < p.dim) {
+                const float inv = __fdiv_rn(1.0f, qscale[q]);
+                const float r = rintf(__fmul_rn(src[static_cast<size_t>(q0 + q) * p.dim + j], inv));
+                v = static_cast<int8_t>(fminf(fmaxf(r, -127.0f), 127.0f));
+            }
+            dst[e] = v;
+        }
+    } else {  // kModeBin
+        const int qw = p.query_bytes / 4;
+        const int words = (p.dim + 31) / 32;
+        uint32_t* dst = reinterpret_cast<uint32_t*>(qsmem);
+        for (int e = tid; e < QB * qw; e += kScanThreads) {
+            const int q = e / qw;
+            const int w = e - q * qw;
+            uint32_t bits = 0u;
+            if (q < nq && w < words) {
+                if (p.query_packed) {
+                    bits = static_cast<const uint32_t*>(p.queries)[static_cast<size_t>(q0 + q) * words + w];
+                } else {
+                    const float* row = static_cast<const float*>(p.queries) + static_cast<size_t>(q0 + q) * p.dim;
+                    for (int b = 0; b < 32; ++b) {
+                        const int d = 32 * w + b;
+                        if (d < p.dim && row[d] >= 0.0f) bits |= (1u << b);
+                    }
+                }
+            }
+            dst[e] = bits;
+        }
+    }
+}
+
+// Copies `rows` rows into a stage with the 16-byte padded stride (non-TMA path).
+template <int ELEM_BYTES>
+__device__ void fill_stage_plain(const ScanParams& p, uint8_t* stage, long long row0, int rows) {
+    using Elem = typename std::conditional<ELEM_BYTES == 4, uint32_t,
+                 typename std::conditional<ELEM_BYTES == 2, uint16_t, uint8_t>::type>::type;
+    const int epr = p.elems_per_row;
+    const int spr = p.stride / ELEM_BYTES;
+    const Elem* src = reinterpret_cast<const Elem*>(p.corpus) + row0 * epr;
+    Elem* dst = reinterpret_cast<Elem*>(stage);
+    const int total = rows * spr;
+    for (int i = threadIdx.x; i < total; i += kScanThreads) {
+        const int r = i / spr;
+        const int e = i - r * spr;
+        dst[i] = (e < epr) ? src[static_cast<size_t>(r) * epr + e] : Elem(0);
+    }
+}
+
+template <int MODE, int QB, int JC, bool L2, bool EMIT>
+__global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams p) {
+    using Traits = ModeTraits<MODE>;
+    constexpr int EPC = Traits::kEpc;
+    constexpr bool kInt = (MODE == kModeI8R);
+    constexpr int kQbLog = Log2<QB>::value;
+
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ float s_red[kScanWarps * QB];
+    __shared__ float s_qscale[QB];
+    __shared__ u64 s_scratch[32];
+    __shared__ int s_last;
+
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const int pass = blockIdx.x;
+    const int cta = blockIdx.y;
+    const int G = gridDim.y;
+    const int q0 = pass * QB;
+    const int nq = min(QB, p.batch - q0);
+
+    const int R = p.rows_per_tile;
+    const int tile_bytes = R * p.stride;
+    uint8_t* stages = smem;
+    uint8_t* qsmem = smem + p.smem_query_off;
+    u64* bars = reinterpret_cast<u64*>(smem + p.smem_bar_off);
+
+    TopkSmem tk;
+    tk.buf = reinterpret_cast<u64*>(smem + p.smem_topk_off);
+    tk.count = reinterpret_cast<int*>(tk.buf + QB * p.cap);
+    tk.thr = reinterpret_cast<u64*>(tk.count + 2 * QB);  // 8-byte aligned
+    tk.cap = p.cap;
+    tk.k = p.k;
+
+    const long long t_begin = (p.ntiles * cta) / G;
+    const long long t_end = (p.ntiles * (cta + 1)) / G;
+    const int my_tiles = static_cast<int>(t_end - t_begin);
+    const int S = p.use_tma ? p.stages : 1;
+
+    auto issue = [&](int i) {
+        const long long tile = t_begin + i;
+        const long long row0 = tile * R;
+        const long long left = p.n - row0;
+        const int rows = static_cast<int>(left < R ? left : R);
+        const uint32_t bytes = static_cast<uint32_t>(rows) * static_cast<uint32_t>(p.row_bytes);
+        u64* bar = &bars[i % S];
+        mbar_arrive_expect_tx(bar, bytes);
+        bulk_copy_g2s(stages + (i % S) * tile_bytes, p.corpus + row0 * p.row_bytes, bytes, bar);
+    };
+
+    if (p.use_tma) {
+        if (tid == 0) {
+            for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
+            fence_mbarrier_init();
+        }
+        __syncthreads();
+        if (tid == 0) {
+            for (int i = 0; i < S && i < my_tiles; ++i) issue(i);
+        }
+    }
+
+    stage_queries<MODE, QB>(p, qsmem, s_qscale, q0, nq, s_red);
+    if (!EMIT && tid < QB) {
+        tk.count[tid] = 0;
+        tk.thr[tid] = 0ull;
+    }
+    __syncthreads();
+
+    // Register-resident query slices for the fast path (JC chunks per lane, lane + 32 j).
+    using QElem = typename std::conditional<kInt, int, float>::type;
+    QElem qreg[JC > 0 ? JC : 1][QB][EPC];
+    if constexpr (JC > 0 && MODE != kModeBin) {
+#pragma unroll
+        for (int j = 0; j < JC; ++j) {
+            const int c = lane + 32 * j;
+#pragma unroll
+            for (int q = 0; q < QB; ++q) {
+#pragma unroll
+                for (int e = 0; e < EPC; ++e) {
+                    if (c < p.nch) {
+                        qreg[j][q][e] = reinterpret_cast<const QElem*>(qsmem + q * p.query_bytes)[c * EPC + e];
+                    } else {
+                        qreg[j][q][e] = QElem(0);
+                    }
+                }
+            }
+        }
+    }
+
+    bool aborted = false;
+    int i = 0;
+    for (; i < my_tiles; ++i) {
+        const long long tile = t_begin + i;
+        const long long row0 = tile * R;
+        const long long left = p.n - row0;
+        const int rows = static_cast<int>(left < R ? left : R);
+        bool failed = false;
+        int s = 0;
+        if (p.use_tma) {
+            s = i % S;
+            failed = !mbar_wait_bounded(&bars[s], static_cast<uint32_t>((i / S) & 1), p.status,
+                                        kStatusTileWaitTimeout);
+        } else {
+            fill_stage_plain<Traits::kElemBytes>(p, stages, row0, rows);
+            __syncthreads();
+        }
+        const uint8_t* st = stages + s * tile_bytes;
+
+        if constexpr (MODE == kModeBin) {
+            // Thread per row. Each thread starts its chunk walk at a row-dependent offset so a
+            // quarter-warp's 16-byte reads fall in distinct bank groups.
+            for (int r = tid; r < rows; r += kScanThreads) {
+                const uint8_t* rowp = st + r * p.stride;
+                int h[QB];
+#pragma unroll
+                for (int q = 0; q < QB; ++q) h[q] = 0;
+                int u = r % p.nch;
+                for (int c = 0; c < p.nch; ++c) {
+                    const uint4 w = lds128(rowp + u * 16);
+#pragma unroll
+                    for (int q = 0; q < QB; ++q) {
+                        const uint4 qw = lds128(qsmem + q * p.query_bytes + u * 16);
+                        h[q] += __popc(w.x ^ qw.x) + __popc(w.y ^ qw.y) + __popc(w.z ^ qw.z) +
+                                __popc(w.w ^ qw.w);
+                    }
+                    u = (u + 1 == p.nch) ? 0 : u + 1;
+                }
+                const long long row = row0 + r;
+                const bool masked = (p.mask != nullptr) && (__ldg(p.mask + row) == 0);
+#pragma unroll
+                for (int q = 0; q < QB; ++q) {
+                    if (q < nq) {
+                        float score = __fdiv_rn(static_cast<float>(p.dim - 2 * h[q]),
+                                                static_cast<float>(p.dim));
+                        if (masked) score = -FLT_MAX;
+                        if constexpr (EMIT) {
+                            p.out_matrix[static_cast<size_t>(q0 + q) * p.n + row] = score;
+                        } else {
+                            topk_offer(tk, q, make_key(score, p.id_base + static_cast<uint32_t>(row)));
+                        }
+                    }
+                }
+            }
+        } else {
+            for (int r = warp; r < rows; r += kScanWarps) {
+                const uint8_t* rowp = st + r * p.stride;
+                QElem acc[QB];
+#pragma unroll
+                for (int q = 0; q < QB; ++q) acc[q] = QElem(0);
+                if constexpr (JC > 0) {
+#pragma unroll
+                    for (int j = 0; j < JC; ++j) {
+                        const int c = lane + 32 * j;
+                        if (c < p.nch) {
+                            const uint4 raw = lds128(rowp + c * 16);
+#pragma unroll
+                            for (int q = 0; q < QB; ++q) {
+                                if constexpr (kInt) {
+                                    acc[q] = dp4a_chunk(raw, qreg[j][q], acc[q]);
+                                } else {
+                                    accumulate_chunk<MODE, L2>(raw, qreg[j][q], p.scale, acc[q]);
+                                }
+                            }
+                        }
+                    }
+                } else {
+                    for (int c = lane; c < p.nch; c += 32) {
+                        const uint4 raw = lds128(rowp + c * 16);
+#pragma unroll
+                        for (int q = 0; q < QB; ++q) {
+                            const uint8_t* qrow = qsmem + q * p.query_bytes + c * EPC * sizeof(QElem);
+                            QElem qv[EPC];
+#pragma unroll
+                            for (int e = 0; e < EPC; e += 4) {
+                                const uint4 v = lds128(qrow + e * sizeof(QElem));
+                                qv[e] = *reinterpret_cast<const QElem*>(&v.x);
+                                qv[e + 1] = *reinterpret_cast<const QElem*>(&v.y);
+                                qv[e + 2] = *reinterpret_cast<const QElem*>(&v.z);
+                                qv[e + 3] = *reinterpret_cast<const QElem*>(&v.w);
+                            }
+                            if constexpr (kInt) {
+                                acc[q] = dp4a_chunk(raw, qv, acc[q]);
+                            } else {
+                                accumulate_chunk<MODE, L2>(raw, qv, p.scale, acc[q]);
+                            }
+                        }
+                    }
+                }
+                transpose_reduce<QB>(acc, lane);
+                constexpr int kGroup = 32 >> kQbLog;
+                const int q = lane >> (5 - kQbLog);
+                if ((lane & (kGroup - 1)) == 0 && q < nq) {
+                    const long long row = row0 + r;
+                    float score;
+                    if constexpr (kInt) {
+                        score = __fmul_rn(__fmul_rn(__int2float_rn(acc[0]), s_qscale[q]),
+                                          __ldg(p.row_scales + row));
+                    } else {
+                        score = L2 ? -acc[0] : acc[0];
+                    }
+                    if (p.mask != nullptr && __ldg(p.mask + row) == 0) score = -FLT_MAX;
+                    if constexpr (EMIT) {
+                        p.out_matrix[static_cast<size_t>(q0 + q) * p.n + row] = score;
+                    } else {
+                        topk_offer(tk, q, make_key(score, p.id_base + static_cast<uint32_t>(row)));
+                    }
+                }
+            }
+        }
+
+        aborted = __syncthreads_or(failed);
+        if constexpr (!EMIT) topk_maybe_flush(tk, nq, R, kScanThreads);
+        if (aborted) break;
+        if (p.use_tma && tid == 0 && i + S < my_tiles) {
+            fence_proxy_async_shared();
+            issue(i + S);
+        }
+    }
+
+    // A wait ran out: make sure no bulk copy into this CTA's shared memory is still pending
+    // before the CTA can retire (bounded as well), then finish normally so the workspace
+    // counters stay consistent; the status word tells the host the results are invalid.
+    if (aborted && p.use_tma && tid == 0) {
+        const int last = min(i + S - 1, my_tiles - 1);
+        for (int j = i; j <= last; ++j) {
+            mbar_wait_bounded(&bars[j % S], static_cast<uint32_t>((j / S) & 1), p.status,
+                              kStatusDrainTimeout);
+        }
+    }
+    if constexpr (EMIT) return;
+
+    __syncthreads();
+    topk_flush_all(tk, nq, kScanThreads);
+    for (int q = 0; q < nq; ++q) {
+        unsigned long long* dst = p.lists + (static_cast<size_t>(q0 + q) * G + cta) * p.k;
+        const int n = tk.count[q];
+        for (int j = tid; j < p.k; j += kScanThreads) dst[j] = j < n ? tk.buf[q * p.cap + j] : 0ull;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const unsigned int ticket = atomicAdd(&p.counters[pass], 1u);
+        s_last = (ticket == static_cast<unsigned int>(G - 1)) ? 1 : 0;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    for (int q = 0; q < nq; ++q) {
+        const unsigned long long* src = p.lists + static_cast<size_t>(q0 + q) * G * p.k;
+        topk_merge_lists(tk, q, src, G, kScanThreads, s_scratch);
+        topk_write(tk, q, p.out_idx + static_cast<size_t>(q0 + q) * p.k,
+                   p.out_scores + static_cast<size_t>(q0 + q) * p.k, kScanThreads);
+        __syncthreads();
+    }
+    if (tid == 0) p.counters[pass] = 0u;
+}
+
+}  // namespace zc

@@ -1,0 +1,154 @@
+"""ctypes binding of libzcgvs_sm100.so, the C ABI declared in include/zcgvs_sm100.h.
+
+This is the host-side mirror of the reference's launcher surface for Python callers (tests,
+bench.py, services): device buffers are torch CUDA tensors used as plain memory, and every
+call goes straight to the CUDA library. There is no CPU fallback: importing this module on a
+machine without the built library raises, and a call without a GPU fails with the CUDA error.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import subprocess
+from pathlib import Path
+
+HERE = Path(__file__).resolve().parent
+LIB_PATH = HERE / "libzcgvs_sm100.so"
+HEADER_PATH = HERE.parent / "include" / "zcgvs_sm100.h"
+
+OK, ERR_INVALID_ARG, ERR_CUDA, ERR_UNSUPPORTED, ERR_DEVICE_STATUS = 0, 1, 2, 3, 4
+DTYPE_F32, DTYPE_F16, DTYPE_I8, DTYPE_BINARY, DTYPE_I8_ROW = 0, 1, 2, 3, 4
+METRIC_COSINE, METRIC_DOT, METRIC_L2 = 0, 1, 2
+MAX_K = 1024
+
+_P = ctypes.c_void_p
+_i32, _i64, _f32, _sz = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_size_t
+
+# Every exported function: name -> (restype, argtypes). Kept in the order of the header.
+SIGNATURES = {
+    "zcgvs_version": (_i32, []),
+    "zcgvs_last_error_message": (ctypes.c_char_p, []),
+    "zcgvs_workspace_init": (_i32, [_P, _sz, _P]),
+    "zcgvs_workspace_status": (_i32, [_P, _sz, _P, _P]),
+    "zcgvs_scan_topk_workspace_bytes": (_sz, [_i32, _i64, _i32, _i32, _i32]),
+    "zcgvs_scan_topk": (_i32, [_P, _i32, _f32, _P, _i64, _i32, _P, _i32, _P, _i32, _i32, _i32,
+                               _P, _P, _P, _sz, _P]),
+    "zcgvs_similarity": (_i32, [_P, _i32, _f32, _P, _i64, _i32, _P, _i32, _P, _i32, _P, _P]),
+}
+
+
+class ZcgvsError(RuntimeError):
+    def __init__(self, status: int, message: str):
+        super().__init__(f"[status {status}] {message}")
+        self.status = status
+
+
+class InvalidArgument(ZcgvsError, ValueError):
+    pass
+
+
+_lib = None
+
+
+def build() -> None:
+    subprocess.run(["make", "-s", "-j8", "-C", str(HERE)], check=True)
+
+
+def lib():
+    """Loads the CUDA library; raises if it has not been built."""
+    global _lib
+    if _lib is None:
+        if not LIB_PATH.exists():
+            raise RuntimeError(f"{LIB_PATH} is not built; run `make -C {HERE}` or __graft_entry__.build()")
+        handle = ctypes.CDLL(str(LIB_PATH))
+        for name, (restype, argtypes) in SIGNATURES.items():
+            fn = getattr(handle, name)
+            fn.restype = restype
+            fn.argtypes = argtypes
+        _lib = handle
+    return _lib
+
+
+def check(status: int) -> None:
+    if status == OK:
+        return
+    message = lib().zcgvs_last_error_message().decode("utf-8", "replace")
+    if status == ERR_INVALID_ARG:
+        raise InvalidArgument(status, message)
+    raise ZcgvsError(status, message)
+
+
+# ----------------------------------------------------------------------------------------
+# torch helpers (torch is plumbing: device memory and streams only)
+# ----------------------------------------------------------------------------------------
+def _ptr(t):
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _stream(stream):
+    import torch
+
+    s = torch.cuda.current_stream() if stream is None else stream
+    return ctypes.c_void_p(s.cuda_stream)
+
+
+class Workspace:
+    """A zero-initialised device workspace that grows on demand (re-zeroed when it grows)."""
+
+    def __init__(self, device=None):
+        self.device = device
+        self.buffer = None
+
+    def get(self, nbytes: int, stream=None):
+        import torch
+
+        if self.buffer is None or self.buffer.numel() < nbytes:
+            self.buffer = torch.zeros(max(nbytes, 256), dtype=torch.uint8, device=self.device or "cuda")
+        return self.buffer
+
+    def status(self, stream=None) -> int:
+        if self.buffer is None:
+            return 0
+        value = ctypes.c_uint32(0)
+        check(lib().zcgvs_workspace_status(_ptr(self.buffer), self.buffer.numel(), ctypes.byref(value),
+                                           _stream(stream)))
+        return int(value.value)
+
+
+def scan_topk_workspace_bytes(dtype: int, doc_count: int, dim: int, batch: int, k: int) -> int:
+    return int(lib().zcgvs_scan_topk_workspace_bytes(dtype, doc_count, dim, batch, k))
+
+
+def scan_topk(corpus, dtype: int, dim: int, queries, k: int, *, scale: float = 1.0,
+              row_scales=None, mask=None, metric: int = METRIC_DOT, id_base: int = 0,
+              workspace: Workspace | None = None, out=None, stream=None):
+    """Fused scan + top-k on device tensors. Returns (indices int32 [B,k], scores fp32 [B,k])."""
+    import torch
+
+    doc_count = corpus.shape[0]
+    queries = queries.reshape(-1, dim)
+    batch = queries.shape[0]
+    if out is None:
+        out = (torch.empty((batch, k), dtype=torch.int32, device=queries.device),
+               torch.empty((batch, k), dtype=torch.float32, device=queries.device))
+    ws = workspace or Workspace(queries.device)
+    nbytes = scan_topk_workspace_bytes(dtype, doc_count, dim, batch, k)
+    buf = ws.get(nbytes, stream)
+    check(lib().zcgvs_scan_topk(_ptr(corpus), dtype, scale, _ptr(row_scales), doc_count, dim,
+                                _ptr(queries), batch, _ptr(mask), metric, k, id_base,
+                                _ptr(out[0]), _ptr(out[1]), _ptr(buf), buf.numel(), _stream(stream)))
+    return out
+
+
+def similarity(corpus, dtype: int, dim: int, queries, *, scale: float = 1.0, row_scales=None,
+               mask=None, metric: int = METRIC_DOT, out=None, stream=None):
+    """Score matrix [B, N] (the reference launchSimilarity contract)."""
+    import torch
+
+    doc_count = corpus.shape[0]
+    batch = queries.shape[0]
+    if out is None:
+        out = torch.empty((batch, doc_count), dtype=torch.float32, device=queries.device)
+    check(lib().zcgvs_similarity(_ptr(corpus), dtype, scale, _ptr(row_scales), doc_count, dim,
+                                 _ptr(queries), batch, _ptr(mask), metric, _ptr(out), _stream(stream)))
+    return out
