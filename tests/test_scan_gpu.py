@@ -171,3 +171,43 @@ def test_similarity_matrix_sweep(zc, orc, name, dim, metric, mask_every):
         np.testing.assert_array_equal(got, ref)
     else:
         np.testing.assert_allclose(got, ref, rtol=0, atol=1e-4)
+
+
+FAST_CASES = [(name, dim) for name, dims in (("i8row", (512, 768, 1024, 1536, 2048)),
+                                             ("f32", (384, 512)),
+                                             ("f16", (384, 768, 1024)),
+                                             ("i8", (512, 768, 1024)))
+              for dim in dims]
+
+
+@pytest.mark.parametrize("name,dim", FAST_CASES)
+@pytest.mark.parametrize("n,k,mask_every", [(100000, 100, 0), (33333, 256, 5), (4097, 1, 0), (70001, 10, 3)])
+def test_single_query_warp_specialised_path(zc, orc, name, dim, n, k, mask_every):
+    """Batch 1 over 16-byte-multiple rows takes the warp-specialised kernel (scan_fast.cuh):
+    every storage, sweep depth 2-8, ragged corpus sizes, masks and k from 1 to 256."""
+    idx, val, ref, exact = run_topk(zc, orc, name, n, dim, 1, k, 1, mask_every, seed=dim + k)
+    assert_topk_parity(idx, val, ref, k, exact=exact)
+
+
+@pytest.mark.parametrize("order", ["ascending", "descending", "constant"])
+def test_single_query_adversarial_orders_spill_and_ties(zc, orc, order):
+    """Ascending scores make every row beat the running threshold, so every CTA overflows its
+    shared candidate buffer into the global spill area; constant scores make every row tie and
+    the order is decided by id alone."""
+    import torch
+
+    n, dim, k = 600_000, 128, 100
+    q = orc.normal_rows(1, dim, 4242)
+    if order == "constant":
+        t = np.ones(n, dtype=np.float32)
+    else:
+        t = np.linspace(0.0, 1.0, n, dtype=np.float32)
+        if order == "descending":
+            t = t[::-1].copy()
+    corpus = (t[:, None] * q).astype(np.float32)
+    d_idx, d_val = zc.scan_topk(to_dev(corpus), zc.DTYPE_F32, dim, to_dev(q), k)
+    torch.cuda.synchronize()
+    ref = orc.scores(corpus, orc.DTYPE_F32, dim, q)
+    assert_topk_parity(d_idx.cpu().numpy(), d_val.cpu().numpy(), ref, k, exact=False)
+    if order == "constant":
+        assert d_idx.cpu().numpy()[0].tolist() == list(range(k))

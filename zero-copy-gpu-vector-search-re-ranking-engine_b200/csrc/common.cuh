@@ -92,6 +92,10 @@ __device__ __forceinline__ void mbar_arrive_expect_tx(u64* bar, uint32_t bytes) 
                  : "memory");
 }
 
+__device__ __forceinline__ void mbar_arrive_cta(u64* bar) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity) {
     uint32_t done;
     asm volatile(
@@ -134,14 +138,16 @@ __device__ __forceinline__ void bulk_copy_g2s(void* dst_smem, const void* src_gm
 // Warp reductions.
 // ---------------------------------------------------------------------------------------
 
-// Transposing reduction of V per-lane partial sums across all 32 lanes, V a power of two
-// <= 32. Each exchange halves the values a lane holds, so reducing V sums costs
-// (V - 1) + (5 - log2 V) shuffles instead of 5 V. On return v[0] of lane l holds the full
-// sum of value index (l >> (5 - log2 V)), replicated across 32 / V lanes.
-template <int V, typename T>
+// Transposing reduction of V per-lane partial sums across each aligned segment of W lanes
+// (V <= W, both powers of two). Each exchange halves the values a lane holds, so reducing V
+// sums costs (V - 1) + (log2 W - log2 V) shuffles instead of V log2 W. On return v[0] of lane
+// l holds the full segment sum of value index (l % W) >> (log2 W - log2 V), replicated across
+// W / V lanes.
+template <int V, int W, typename T>
 __device__ __forceinline__ void transpose_reduce(T (&v)[V], int lane) {
+    static_assert(V <= W, "segment narrower than the value count");
 #pragma unroll
-    for (int step = 0, nv = V, offset = 16; offset >= 1; ++step, offset >>= 1) {
+    for (int nv = V, offset = W / 2; offset >= 1; offset >>= 1) {
         if (nv > 1) {
             const int half = nv >> 1;
             const bool upper = (lane & offset) != 0;

@@ -1,0 +1,341 @@
+// Warp-specialised streaming scan for one query per pass (the HBM-bound single-query case).
+//
+// Same contract and numerics as scan_kernel (scan_kernel.cuh); different schedule, with no
+// CTA-wide barrier anywhere between the first and the last tile:
+//
+//   * Producer warp: keeps an S-deep ring of stages full with bulk copies (rows + per-row
+//     scales / mask), waiting on each stage's "empty" mbarrier.
+//   * kFastConsumers consumer warps: wait on the stage's "full" mbarrier, score their rows (16
+//     lanes per row, two rows per lane group), then one lane arrives on "empty". Scores that
+//     beat the CTA threshold are appended to one CTA candidate buffer with a single
+//     ballot-aggregated shared atomic per warp iteration. The buffer is zero-initialised
+//     shared memory; appends beyond its capacity spill to a per-CTA global area sized for every
+//     row the CTA owns, so no score can ever be lost.
+//   * Selector warp: follows the buffer as it fills, keeps its own top-k of the keys it has
+//     seen (warp bitonic sort) and publishes their k-th key as the CTA threshold. Keys it reads
+//     before they are written read as 0, so its threshold is computed from a subset of the
+//     candidates and is always a valid lower bound of the CTA's true k-th key.
+//   * After the last tile: every candidate at or above the threshold is selected into the CTA
+//     list (workspace), and the last CTA of the pass merges the CTA lists (as scan_kernel).
+#pragma once
+
+#include "scan_kernel.cuh"
+
+namespace zc {
+
+constexpr int kFastConsumers = 16;
+constexpr int kFastProducerWarp = kFastConsumers;
+constexpr int kFastSelectorWarp = kFastConsumers + 1;
+constexpr int kFastThreads = (kFastConsumers + 2) * 32;
+
+// Selector buffer: 32 lanes x kSelE registers.
+constexpr int kSelE = 8;
+constexpr int kSelCap = 32 * kSelE;
+
+template <int MODE, int JC>
+__global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanParams p) {
+    using Traits = ModeTraits<MODE>;
+    constexpr int EPC = Traits::kEpc;
+    constexpr bool kInt = (MODE == kModeI8R);
+    constexpr int LPR = 16;
+    constexpr int RPW = 2;                        // lane groups per warp
+    constexpr int RW = 2;                         // rows per lane group per iteration
+    constexpr int kRowsPerWarp = RPW * RW;
+    constexpr int kRowsPerStep = kFastConsumers * kRowsPerWarp;
+    constexpr int kGroupShift = 3;                // log2(LPR) - log2(RW)
+    constexpr int kWarpsAll = kFastThreads / 32;
+    using QElem = typename std::conditional<kInt, int, float>::type;
+
+    extern __shared__ __align__(128) uint8_t smem[];
+    __shared__ float s_red[kWarpsAll];
+    __shared__ float s_qscale[1];
+    __shared__ u64 s_scratch[32];
+    __shared__ u64 s_thr;
+    __shared__ u64 s_merge_thr;
+    __shared__ int s_abort;
+    __shared__ int s_done;
+    __shared__ int s_last;
+    __shared__ int s_count;
+    __shared__ int s_merge_count;
+
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const int pass = blockIdx.x;                  // one query per pass
+    const int cta = blockIdx.y;
+    const int G = gridDim.y;
+    const int R = p.rows_per_tile;
+    const int S = p.stages;
+    const int stage_bytes = p.stage_bytes;
+    const int ccap = p.cap;                       // shared candidate buffer capacity
+    const int k = p.k;
+
+    uint8_t* stages = smem;
+    uint8_t* qsmem = smem + p.smem_query_off;
+    u64* cbuf = reinterpret_cast<u64*>(smem + p.smem_topk_off);
+    u64* sbuf = cbuf + ccap;                      // selector buffer, kSelCap keys
+    u64* full = reinterpret_cast<u64*>(smem + p.smem_bar_off);
+    u64* empty = full + S;
+    volatile int* abort_flag = &s_abort;
+    volatile u64* cta_thr = &s_thr;
+    volatile int* vcount = &s_count;
+
+    const int t_begin = static_cast<int>((p.ntiles * cta) / G);
+    const int t_end = static_cast<int>((p.ntiles * (cta + 1)) / G);
+    const int my_tiles = t_end - t_begin;
+    const bool need_side = p.side_scales || p.mask != nullptr;
+    // Spill area for this (pass, CTA): one slot per row the CTA owns.
+    const long long spill_cap = static_cast<long long>(my_tiles) * R;
+    unsigned long long* spill = p.spill + (static_cast<size_t>(pass) * G + cta) * p.spill_stride;
+
+    if (tid == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], kFastConsumers);
+        }
+        fence_mbarrier_init();
+        s_thr = 0ull;
+        s_abort = 0;
+        s_done = 0;
+        s_count = 0;
+    }
+    for (int i = tid; i < ccap; i += kFastThreads) cbuf[i] = 0ull;
+    stage_queries<MODE, 1, kFastThreads>(p, qsmem, s_qscale, pass, 1, s_red);
+    __syncthreads();
+
+    if (warp == kFastProducerWarp) {
+        // ---------------- producer warp ----------------
+        int issued = 0;
+        for (int i = 0; i < my_tiles; ++i) {
+            const int s = i % S;
+            if (i >= S) {
+                bool ok = true;
+                if (lane == 0) {
+                    ok = !*abort_flag &&
+                         mbar_wait_bounded(&empty[s], static_cast<uint32_t>(((i / S) - 1) & 1), p.status,
+                                           kStatusTileWaitTimeout);
+                    if (!ok) *abort_flag = 1;
+                }
+                if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+            }
+            const int row0 = (t_begin + i) * R;
+            const int rows = min(R, static_cast<int>(p.n - row0));
+            uint8_t* st = stages + s * stage_bytes;
+            const bool side_bulk = p.side_tma && rows == R;
+            if (need_side && !side_bulk) {
+                for (int r = lane; r < rows; r += 32) {
+                    if (p.side_scales) reinterpret_cast<float*>(st + p.side_off_scales)[r] = __ldg(p.row_scales + row0 + r);
+                    if (p.mask != nullptr) st[p.side_off_mask + r] = __ldg(p.mask + row0 + r);
+                }
+                __syncwarp();
+            }
+            if (lane == 0) {
+                const uint32_t bytes = static_cast<uint32_t>(rows) * static_cast<uint32_t>(p.row_bytes);
+                uint32_t total = bytes;
+                if (side_bulk) {
+                    if (p.side_scales) total += 4u * R;
+                    if (p.mask != nullptr) total += R;
+                }
+                fence_proxy_async_shared();
+                mbar_arrive_expect_tx(&full[s], total);
+                bulk_copy_g2s(st, p.corpus + static_cast<size_t>(row0) * p.row_bytes, bytes, &full[s]);
+                if (side_bulk) {
+                    if (p.side_scales) bulk_copy_g2s(st + p.side_off_scales, p.row_scales + row0, 4u * R, &full[s]);
+                    if (p.mask != nullptr) bulk_copy_g2s(st + p.side_off_mask, p.mask + row0, R, &full[s]);
+                }
+            }
+            issued = i + 1;
+            __syncwarp();
+        }
+        // If the ring was abandoned, wait (bounded) for every copy still in flight before the
+        // CTA can retire.
+        if (lane == 0 && *abort_flag) {
+            for (int i = max(0, issued - S); i < issued; ++i) {
+                mbar_wait_bounded(&full[i % S], static_cast<uint32_t>((i / S) & 1), p.status, kStatusDrainTimeout);
+            }
+        }
+    } else if (warp == kFastSelectorWarp) {
+        // ---------------- selector warp ----------------
+        // Follows the shared buffer and keeps the best keys it has seen in sbuf (kSelCap
+        // slots). When sbuf fills it sorts it in registers, keeps k and publishes the k-th key.
+        // Polling is bounded in time; giving up only leaves the threshold lower (the result
+        // stays exact).
+        int processed = 0;
+        int scount = 0;
+        u64 sthr = 0ull;
+        const u64 start = global_timer_ns();
+        for (uint32_t spin = 0;; ++spin) {
+            const int done = *reinterpret_cast<volatile int*>(&s_done);
+            const int n = min(*vcount, ccap);
+            if (processed < n) {
+                for (int base = processed; base < n; base += 32) {
+                    const int i = base + lane;
+                    const u64 key = i < n ? cbuf[i] : 0ull;
+                    const bool take = key > sthr;
+                    const uint32_t ballot = __ballot_sync(0xffffffffu, take);
+                    if (take) sbuf[scount + __popc(ballot & ((1u << lane) - 1u))] = key;
+                    scount += __popc(ballot);
+                    if (scount > kSelCap - 32) {
+                        __syncwarp();
+                        u64 v[kSelE];
+#pragma unroll
+                        for (int e = 0; e < kSelE; ++e) {
+                            const int at = lane * kSelE + e;
+                            v[e] = at < scount ? sbuf[at] : 0ull;
+                        }
+                        warp_sort_desc_regs<kSelE>(v, lane);
+                        __syncwarp();
+#pragma unroll
+                        for (int e = 0; e < kSelE; ++e) sbuf[lane * kSelE + e] = v[e];
+                        __syncwarp();
+                        if (scount >= k) {
+                            sthr = sbuf[k - 1];
+                            if (lane == 0) *cta_thr = sthr;
+                        }
+                        scount = min(scount, k);
+                    }
+                }
+                processed = n;
+            } else if (done == kFastConsumers || n >= ccap) {
+                break;
+            } else {
+                __nanosleep(128);
+                if ((spin & 63u) == 0u && global_timer_ns() - start > kWaitBudgetNs) break;
+            }
+        }
+    } else {
+        // ---------------- consumer warps ----------------
+        const int grp = lane / LPR;
+        const int gl = lane % LPR;
+        QElem qreg[JC][EPC];
+#pragma unroll
+        for (int j = 0; j < JC; ++j) {
+#pragma unroll
+            for (int e = 0; e < EPC; ++e) {
+                qreg[j][e] = reinterpret_cast<const QElem*>(qsmem)[(gl + LPR * j) * EPC + e];
+            }
+        }
+        const float qscale = s_qscale[0];
+
+        for (int i = 0; i < my_tiles; ++i) {
+            const int s = i % S;
+            const int row0 = (t_begin + i) * R;
+            const int rows = min(R, static_cast<int>(p.n - row0));
+            bool ok = true;
+            if (lane == 0) {
+                ok = !*abort_flag && mbar_wait_bounded(&full[s], static_cast<uint32_t>((i / S) & 1),
+                                                       p.status, kStatusTileWaitTimeout);
+                if (!ok) *abort_flag = 1;
+            }
+            if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
+            const uint8_t* st = stages + s * stage_bytes;
+            const float* side_scale = reinterpret_cast<const float*>(st + p.side_off_scales);
+            const uint8_t* side_mask = st + p.side_off_mask;
+            const uint32_t id0 = p.id_base + static_cast<uint32_t>(row0);
+
+            for (int rb = warp * kRowsPerWarp; rb < rows; rb += kRowsPerStep) {
+                QElem acc[RW];
+#pragma unroll
+                for (int rr = 0; rr < RW; ++rr) {
+                    acc[rr] = QElem(0);
+                    const int r = rb + rr * RPW + grp;
+                    if (r < rows) {
+                        const uint8_t* rowp = st + r * p.stride;
+#pragma unroll
+                        for (int j = 0; j < JC; ++j) {
+                            const uint4 raw = lds128(rowp + (gl + LPR * j) * 16);
+                            if constexpr (kInt) {
+                                acc[rr] = dp4a_chunk(raw, qreg[j], acc[rr]);
+                            } else {
+                                accumulate_chunk<MODE, false>(raw, qreg[j], p.scale, acc[rr]);
+                            }
+                        }
+                    }
+                }
+                transpose_reduce<RW, LPR>(acc, lane);
+                const int r = rb + (gl >> kGroupShift) * RPW + grp;
+                const bool leader = (gl & ((1 << kGroupShift) - 1)) == 0 && r < rows;
+                u64 key = 0ull;
+                if (leader) {
+                    float score;
+                    if constexpr (kInt) {
+                        score = __fmul_rn(__fmul_rn(__int2float_rn(acc[0]), qscale), side_scale[r]);
+                    } else {
+                        score = acc[0];
+                    }
+                    if (p.mask != nullptr && side_mask[r] == 0) score = -FLT_MAX;
+                    key = make_key(score, id0 + r);
+                }
+                const bool take = leader && key > *cta_thr;
+                const uint32_t ballot = __ballot_sync(0xffffffffu, take);
+                if (ballot != 0u) {
+                    int base = 0;
+                    if (lane == 0) base = atomicAdd(&s_count, __popc(ballot));
+                    base = __shfl_sync(0xffffffffu, base, 0);
+                    if (take) {
+                        const int slot = base + __popc(ballot & ((1u << lane) - 1u));
+                        if (slot < ccap) {
+                            cbuf[slot] = key;
+                        } else if (slot - ccap < spill_cap) {
+                            spill[slot - ccap] = key;
+                        }
+                    }
+                }
+            }
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cta(&empty[s]);
+        }
+        if (lane == 0) atomicAdd(&s_done, 1);
+    }
+    __syncthreads();
+
+    // Select this CTA's top-k from every candidate at or above the selector's threshold: the
+    // shared buffer first, then any spill. The stage ring (free now) holds the merge buffer;
+    // offers run in lock-step rounds of at most kFastThreads keys between flush checks.
+    TopkSmem mt;
+    mt.buf = reinterpret_cast<u64*>(stages);
+    mt.count = &s_merge_count;
+    mt.thr = &s_merge_thr;
+    mt.cap = p.cap_final;
+    mt.k = k;
+    const u64 floor_key = s_thr;
+    if (tid == 0) {
+        s_merge_count = 0;
+        s_merge_thr = floor_key > 0ull ? floor_key - 1ull : 0ull;
+    }
+    __syncthreads();
+    const int total = min(s_count, static_cast<int>(ccap + spill_cap));
+    for (int base = 0; base < total; base += kFastThreads) {
+        const int i = base + tid;
+        if (i < total) {
+            const u64 key = i < ccap ? cbuf[i] : __ldcg(spill + (i - ccap));
+            if (key != 0ull) topk_offer(mt, 0, key);
+        }
+        __syncthreads();
+        topk_maybe_flush_one(mt, 0, kFastThreads, kFastThreads);
+    }
+    __syncthreads();
+    topk_flush_mask(mt, 1u, kFastThreads);
+    {
+        unsigned long long* dst = p.lists + (static_cast<size_t>(pass) * G + cta) * k;
+        const int n = s_merge_count;
+        for (int j = tid; j < k; j += kFastThreads) dst[j] = j < n ? mt.buf[j] : 0ull;
+    }
+    __threadfence();
+    __syncthreads();
+    if (tid == 0) {
+        const unsigned int ticket = atomicAdd(&p.counters[pass], 1u);
+        s_last = (ticket == static_cast<unsigned int>(G - 1)) ? 1 : 0;
+    }
+    __syncthreads();
+    if (!s_last) return;
+    __threadfence();
+    const unsigned long long* src = p.lists + static_cast<size_t>(pass) * G * k;
+    topk_merge_lists(mt, 0, src, G, kFastThreads, s_scratch);
+    topk_write(mt, 0, p.out_idx + static_cast<size_t>(pass) * k, p.out_scores + static_cast<size_t>(pass) * k,
+               kFastThreads);
+    __syncthreads();
+    if (tid == 0) p.counters[pass] = 0u;
+}
+
+}  // namespace zc

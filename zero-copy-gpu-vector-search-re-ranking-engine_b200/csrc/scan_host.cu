@@ -6,6 +6,7 @@
 #include <string>
 
 #include "host_common.h"
+#include "scan_fast.cuh"
 #include "scan_instances.h"
 #include "zcgvs_sm100.h"
 
@@ -13,7 +14,7 @@ namespace zc {
 
 namespace {
 
-constexpr int kTileTargetBytes = 32 * 1024;
+constexpr int kTileTargetBytes = 48 * 1024;
 constexpr int kMaxStages = 8;
 constexpr int kMaxTileRows = 512;
 constexpr size_t kWorkspaceAlign = 256;
@@ -36,12 +37,29 @@ struct ScanPlan {
     int cap = 0;
     int stages = 1;
     int query_bytes = 0;
+    bool side_scales = false;
+    bool side_mask = false;
+    int stage_bytes = 0;
+    int side_off_scales = 0;
+    int side_off_mask = 0;
     int smem_query_off = 0;
     int smem_topk_off = 0;
     int smem_bar_off = 0;
     int smem_total = 0;
     size_t ws_header = 0;
+    size_t ws_lists = 0;
     size_t ws_total = 0;
+    // Warp-specialised single-query variant (scan_fast.cuh), same tiles, grid and workspace.
+    bool fast = false;
+    int fast_stages = 0;
+    int fast_ccap = 0;
+    int fast_scap = 0;
+    int fast_cap_final = 0;
+    long long fast_spill_stride = 0;
+    int fast_query_off = 0;
+    int fast_topk_off = 0;
+    int fast_bar_off = 0;
+    int fast_smem = 0;
 };
 
 int mode_of(int dtype) {
@@ -66,7 +84,12 @@ int query_bytes_of(int mode, int stride) {
 
 // Fills the shared-memory layout for a given pass width / tile size; false if it cannot fit.
 bool layout(ScanPlan& plan, int budget) {
-    const int tile_bytes = plan.rows_per_tile * plan.stride;
+    const int R = plan.rows_per_tile;
+    plan.side_off_scales = R * plan.stride;
+    plan.side_off_mask = plan.side_off_scales + (plan.side_scales ? static_cast<int>(round_up(4 * R, 16)) : 0);
+    const int tile_bytes = static_cast<int>(
+        round_up(plan.side_off_mask + (plan.side_mask ? static_cast<int>(round_up(R, 16)) : 0), 128));
+    plan.stage_bytes = tile_bytes;
     const int query = plan.qb * plan.query_bytes;
     const int topk = plan.emit ? 0 : plan.qb * (plan.cap * 8 + 16);
     const int fixed = static_cast<int>(round_up(query, 128)) + static_cast<int>(round_up(topk, 128)) +
@@ -88,7 +111,7 @@ bool layout(ScanPlan& plan, int budget) {
 
 // Builds the launch plan. Returns ZCGVS_OK or an error status (message recorded).
 int make_plan(int dtype, long long n, int dim, int batch, int k, int metric, bool emit,
-              bool aligned, ScanPlan& plan) {
+              bool aligned, bool has_mask, ScanPlan& plan) {
     plan.mode = mode_of(dtype);
     if (plan.mode < 0) return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: unknown storage dtype " + std::to_string(dtype));
     if (metric < ZCGVS_METRIC_COSINE || metric > ZCGVS_METRIC_L2) {
@@ -99,6 +122,8 @@ int make_plan(int dtype, long long n, int dim, int batch, int k, int metric, boo
         return fail(ZCGVS_ERR_UNSUPPORTED, "zcgvs: the per-row int8 store scores dot/cosine only");
     }
     plan.emit = emit;
+    plan.side_scales = (plan.mode == kModeI8R);
+    plan.side_mask = has_mask;
     const long long rb = row_bytes_of(dtype, dim);
     plan.row_bytes = static_cast<int>(rb);
     plan.stride = static_cast<int>(round_up(static_cast<size_t>(rb), 16));
@@ -108,10 +133,27 @@ int make_plan(int dtype, long long n, int dim, int batch, int k, int metric, boo
     plan.query_bytes = query_bytes_of(plan.mode, plan.stride);
 
     const int budget = device_max_smem() - 2048;
-    int rows = std::max(1, kTileTargetBytes / plan.stride);
-    rows = std::min(rows, kMaxTileRows);
-    if (rows >= 16) rows &= ~15;
+    // Fast path: a single query held in registers, 16 lanes per row, two rows per lane group,
+    // planned when the row is exactly 2/3/4/6/8 sweeps of 16 lanes x 16 bytes.
+    const int fast_jc = (plan.nch % 16 == 0) ? plan.nch / 16 : 0;
+    const bool fast_ok = !emit && !plan.l2 && plan.mode != kModeBin &&
+                         (fast_jc == 2 || fast_jc == 3 || fast_jc == 4 || fast_jc == 6 || fast_jc == 8);
+    // Rows per tile: about kTileTargetBytes, rounded to whole CTA steps so no warp idles at the
+    // tile barrier (64 rows for the fast path, 16 for warp-per-row, 32 for thread-per-row).
+    auto rows_for = [&](int qb) {
+        const int step = (qb == 1 && fast_ok) ? 64 : (plan.mode == kModeBin ? 32 : 16);
+        int r = std::max(1, kTileTargetBytes / plan.stride);
+        if (r >= step) {
+            r = r / step * step;
+        } else if (step * plan.stride <= 2 * kTileTargetBytes) {
+            r = step;
+        } else if (r >= 16) {
+            r &= ~15;
+        }
+        return std::min(r, kMaxTileRows);
+    };
     int qb = emit ? 8 : (batch <= 1 ? 1 : std::min(8, next_pow2(batch)));
+    int rows = rows_for(qb);
     const int sms = device_sm_count();
 
     for (;;) {
@@ -127,22 +169,44 @@ int make_plan(int dtype, long long n, int dim, int batch, int k, int metric, boo
         }
         if (qb > 1) {
             qb /= 2;
-            rows = std::min(std::max(1, kTileTargetBytes / plan.stride), kMaxTileRows);
-            if (rows >= 16) rows &= ~15;
+            rows = rows_for(qb);
             continue;
         }
         return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs similarity: embedding dim " + std::to_string(dim) +
                                                " needs more shared memory than a block can stage");
     }
     plan.passes = (batch + plan.qb - 1) / plan.qb;
-    plan.jc = 0;
-    if (!emit && plan.qb == 1 && !plan.l2 && plan.mode != kModeBin && plan.nch <= 128) {
-        plan.jc = (plan.nch + 31) / 32;
+    plan.jc = (plan.qb == 1 && fast_ok) ? fast_jc : 0;
+
+    // The warp-specialised kernel needs the bulk-copy ring and k <= 192. Its shared memory
+    // holds the stage ring, the query, the CTA candidate buffer and the selector's buffer; the
+    // ring must also fit the final merge buffer once the scan is over.
+    if (plan.jc > 0 && plan.use_tma && k <= kSelCap - 64 && !(plan.mode == kModeI8M && plan.jc > 4)) {
+        plan.fast_ccap = 2048;
+        plan.fast_scap = kSelCap;
+        plan.fast_cap_final = next_pow2(k + std::max(kFastThreads, plan.grid_rows));
+        const int query = static_cast<int>(round_up(plan.query_bytes, 128));
+        const int bufs = 8 * (plan.fast_ccap + plan.fast_scap);
+        const int fixed = query + bufs + 2 * kMaxStages * 8 + 128;
+        const int stages = std::min(kMaxStages, (budget - fixed) / plan.stage_bytes);
+        const long long ring = static_cast<long long>(stages) * plan.stage_bytes;
+        if (stages >= 2 && ring >= 8LL * plan.fast_cap_final) {
+            plan.fast = true;
+            plan.fast_stages = stages;
+            plan.fast_query_off = static_cast<int>(round_up(static_cast<size_t>(ring), 128));
+            plan.fast_topk_off = plan.fast_query_off + query;
+            plan.fast_bar_off = plan.fast_topk_off + bufs;
+            plan.fast_smem = plan.fast_bar_off + 2 * kMaxStages * 8;
+            plan.fast_spill_stride = (plan.ntiles + plan.grid_rows - 1) / plan.grid_rows * plan.rows_per_tile;
+        }
     }
     plan.ws_header = round_up(16 + 4 * static_cast<size_t>(plan.passes), kWorkspaceAlign);
-    plan.ws_total = emit ? 0
-                         : plan.ws_header + static_cast<size_t>(batch) * plan.grid_rows *
-                                                static_cast<size_t>(k) * 8;
+    plan.ws_lists = static_cast<size_t>(batch) * plan.grid_rows * static_cast<size_t>(k) * 8;
+    plan.ws_total = emit ? 0 : plan.ws_header + plan.ws_lists;
+    if (plan.fast) {
+        plan.ws_total += static_cast<size_t>(plan.passes) * plan.grid_rows *
+                         static_cast<size_t>(plan.fast_spill_stride) * 8;
+    }
     return ZCGVS_OK;
 }
 
@@ -178,7 +242,7 @@ int check_alignment(int dtype, const void* corpus, const void* row_scales, const
 }
 
 int launch(const ScanPlan& plan, ScanParams& params, cudaStream_t stream) {
-    const ScanKernelFn kernel = lookup(plan);
+    const ScanKernelFn kernel = plan.fast ? scan_lookup_fast(plan.mode, plan.jc) : lookup(plan);
     if (kernel == nullptr) {
         return fail(ZCGVS_ERR_UNSUPPORTED, "zcgvs: no scan kernel variant for this configuration");
     }
@@ -187,18 +251,32 @@ int launch(const ScanPlan& plan, ScanParams& params, cudaStream_t stream) {
     params.rows_per_tile = plan.rows_per_tile;
     params.ntiles = plan.ntiles;
     params.use_tma = plan.use_tma ? 1 : 0;
-    params.stages = plan.stages;
-    params.cap = plan.cap;
+    params.stages = plan.fast ? plan.fast_stages : plan.stages;
+    params.cap = plan.fast ? plan.fast_ccap : plan.cap;
+    params.merge_cap = plan.fast_scap;
+    params.cap_final = plan.fast_cap_final;
+    params.spill_stride = plan.fast_spill_stride;
     params.row_bytes = plan.row_bytes;
     params.stride = plan.stride;
     params.nch = plan.nch;
     params.elems_per_row = plan.elems_per_row;
     params.query_bytes = plan.query_bytes;
-    params.smem_query_off = plan.smem_query_off;
-    params.smem_topk_off = plan.smem_topk_off;
-    params.smem_bar_off = plan.smem_bar_off;
+    params.stage_bytes = plan.stage_bytes;
+    params.side_scales = plan.side_scales ? 1 : 0;
+    params.side_off_scales = plan.side_off_scales;
+    params.side_off_mask = plan.side_off_mask;
+    params.side_tma = (plan.use_tma && plan.rows_per_tile % 16 == 0 &&
+                       (!plan.side_scales || aligned16(params.row_scales)) &&
+                       (params.mask == nullptr || aligned16(params.mask)))
+                          ? 1
+                          : 0;
+    params.smem_query_off = plan.fast ? plan.fast_query_off : plan.smem_query_off;
+    params.smem_topk_off = plan.fast ? plan.fast_topk_off : plan.smem_topk_off;
+    params.smem_bar_off = plan.fast ? plan.fast_bar_off : plan.smem_bar_off;
     const dim3 grid(static_cast<unsigned>(plan.passes), static_cast<unsigned>(plan.grid_rows));
-    kernel<<<grid, kScanThreads, plan.smem_total, stream>>>(params);
+    const int threads = plan.fast ? kFastThreads : kScanThreads;
+    const int smem = plan.fast ? plan.fast_smem : plan.smem_total;
+    kernel<<<grid, threads, smem, stream>>>(params);
     status = cudaGetLastError();
     if (status != cudaSuccess) return fail_cuda(status, "scan_kernel launch");
     return ok();
@@ -218,10 +296,12 @@ size_t zcgvs_scan_topk_workspace_bytes(int dtype, int64_t doc_count, int dim, in
     const int metrics[2] = {ZCGVS_METRIC_DOT, ZCGVS_METRIC_L2};
     for (const int metric : metrics) {
         for (const bool aligned : {true, false}) {
-            zc::ScanPlan plan;
-            if (zc::make_plan(dtype, doc_count, dim, batch, std::min(k, ZCGVS_MAX_K), metric,
-                              false, aligned, plan) == ZCGVS_OK) {
-                bytes = std::max(bytes, plan.ws_total);
+            for (const bool has_mask : {true, false}) {
+                zc::ScanPlan plan;
+                if (zc::make_plan(dtype, doc_count, dim, batch, std::min(k, ZCGVS_MAX_K), metric,
+                                  false, aligned, has_mask, plan) == ZCGVS_OK) {
+                    bytes = std::max(bytes, plan.ws_total);
+                }
             }
         }
     }
@@ -259,7 +339,8 @@ int zcgvs_scan_topk(const void* corpus, int dtype, float scale, const float* row
     int status = check_alignment(dtype, corpus, row_scales, queries, out_indices, out_scores);
     if (status != ZCGVS_OK) return status;
     ScanPlan plan;
-    status = make_plan(dtype, doc_count, dim, batch, k, metric, false, aligned16(corpus), plan);
+    status = make_plan(dtype, doc_count, dim, batch, k, metric, false, aligned16(corpus),
+                       mask != nullptr, plan);
     if (status != ZCGVS_OK) return status;
     if (workspace == nullptr || workspace_bytes < plan.ws_total) {
         return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: workspace smaller than zcgvs_scan_topk_workspace_bytes()");
@@ -282,6 +363,7 @@ int zcgvs_scan_topk(const void* corpus, int dtype, float scale, const float* row
     params.status = reinterpret_cast<unsigned int*>(ws);
     params.counters = reinterpret_cast<unsigned int*>(ws + 16);
     params.lists = reinterpret_cast<unsigned long long*>(ws + plan.ws_header);
+    params.spill = reinterpret_cast<unsigned long long*>(ws + plan.ws_header + plan.ws_lists);
     params.out_idx = out_indices;
     params.out_scores = out_scores;
     params.out_matrix = nullptr;
@@ -305,7 +387,8 @@ int zcgvs_similarity(const void* corpus, int dtype, float scale, const float* ro
     int status = check_alignment(dtype, corpus, row_scales, queries, scores, nullptr);
     if (status != ZCGVS_OK) return status;
     ScanPlan plan;
-    status = make_plan(dtype, doc_count, dim, batch, 1, metric, true, aligned16(corpus), plan);
+    status = make_plan(dtype, doc_count, dim, batch, 1, metric, true, aligned16(corpus),
+                       mask != nullptr, plan);
     if (status != ZCGVS_OK) return status;
     ScanParams params{};
     params.corpus = static_cast<const uint8_t*>(corpus);

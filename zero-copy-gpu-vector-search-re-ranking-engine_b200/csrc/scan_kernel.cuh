@@ -63,6 +63,15 @@ struct ScanParams {
     float* out_scores;             // [batch][k]
     float* out_matrix;             // score-matrix mode: [batch][n]
     int query_bytes;               // bytes of one staged query
+    int stage_bytes;               // one pipeline stage: rows, then per-row side data
+    int side_scales;               // stage the per-row scales (kModeI8R)
+    int side_tma;                  // side data may ride the tile's bulk copies (aligned)
+    int side_off_scales;           // offsets of the side data inside a stage
+    int side_off_mask;
+    int merge_cap;                 // warp-specialised kernel: selector buffer capacity
+    int cap_final;                 // warp-specialised kernel: merge buffer capacity
+    unsigned long long* spill;     // warp-specialised kernel: [passes][G][spill_stride]
+    long long spill_stride;
     int smem_query_off;
     int smem_topk_off;
     int smem_bar_off;
@@ -148,15 +157,16 @@ __device__ __forceinline__ int dp4a_chunk(const uint4 raw, const int* qw, int ac
 
 // Stages the query pass into shared memory in the form the row loop consumes: fp32 values
 // zero-padded to whole chunks, per-row int8 quantisation (I8R) or packed sign bits (Bin).
-template <int MODE, int QB>
+template <int MODE, int QB, int NT = kScanThreads>
 __device__ void stage_queries(const ScanParams& p, uint8_t* qsmem, float* qscale, int q0,
-                              int nq, float* red /* [kScanWarps * QB] */) {
+                              int nq, float* red /* [(NT / 32) * QB] */) {
+    constexpr int kWarps = NT / 32;
     const int tid = threadIdx.x;
     if constexpr (MODE == kModeF32 || MODE == kModeF16 || MODE == kModeI8M) {
         const int qf = p.query_bytes / 4;
         float* dst = reinterpret_cast<float*>(qsmem);
         const float* src = static_cast<const float*>(p.queries);
-        for (int e = tid; e < QB * qf; e += kScanThreads) {
+        for (int e = tid; e < QB * qf; e += NT) {
             const int q = e / qf;
             const int j = e - q * qf;
             dst[e] = (q < nq && j < p.dim) ? src[static_cast<size_t>(q0 + q) * p.dim + j] : 0.0f;
@@ -168,7 +178,7 @@ __device__ void stage_queries(const ScanParams& p, uint8_t* qsmem, float* qscale
         float amax[QB];
 #pragma unroll
         for (int q = 0; q < QB; ++q) amax[q] = 0.0f;
-        for (int j = tid; j < p.dim; j += kScanThreads) {
+        for (int j = tid; j < p.dim; j += NT) {
 #pragma unroll
             for (int q = 0; q < QB; ++q) {
                 if (q < nq) amax[q] = fmaxf(amax[q], fabsf(src[static_cast<size_t>(q0 + q) * p.dim + j]));
@@ -177,17 +187,17 @@ __device__ void stage_queries(const ScanParams& p, uint8_t* qsmem, float* qscale
 #pragma unroll
         for (int q = 0; q < QB; ++q) {
             const float m = warp_max_f32(amax[q]);
-            if ((tid & 31) == 0) red[q * kScanWarps + (tid >> 5)] = m;
+            if ((tid & 31) == 0) red[q * kWarps + (tid >> 5)] = m;
         }
         __syncthreads();
         if (tid < QB) {
             float m = 0.0f;
-            for (int w = 0; w < kScanWarps; ++w) m = fmaxf(m, red[tid * kScanWarps + w]);
+            for (int w = 0; w < kWarps; ++w) m = fmaxf(m, red[tid * kWarps + w]);
             qscale[tid] = (m > 0.0f) ? __fdiv_rn(m, 127.0f) : 1.0f;
         }
         __syncthreads();
         int8_t* dst = reinterpret_cast<int8_t*>(qsmem);
-        for (int e = tid; e < QB * p.query_bytes; e += kScanThreads) {
+        for (int e = tid; e < QB * p.query_bytes; e += NT) {
             const int q = e / p.query_bytes;
             const int j = e - q * p.query_bytes;
             int8_t v = 0;
@@ -202,7 +212,7 @@ __device__ void stage_queries(const ScanParams& p, uint8_t* qsmem, float* qscale
         const int qw = p.query_bytes / 4;
         const int words = (p.dim + 31) / 32;
         uint32_t* dst = reinterpret_cast<uint32_t*>(qsmem);
-        for (int e = tid; e < QB * qw; e += kScanThreads) {
+        for (int e = tid; e < QB * qw; e += NT) {
             const int q = e / qw;
             const int w = e - q * qw;
             uint32_t bits = 0u;
@@ -225,6 +235,7 @@ __device__ void stage_queries(const ScanParams& p, uint8_t* qsmem, float* qscale
 // Copies `rows` rows into a stage with the 16-byte padded stride (non-TMA path).
 template <int ELEM_BYTES>
 __device__ void fill_stage_plain(const ScanParams& p, uint8_t* stage, long long row0, int rows) {
+    // Rows only; per-row side data is loaded by the caller.
     using Elem = typename std::conditional<ELEM_BYTES == 4, uint32_t,
                  typename std::conditional<ELEM_BYTES == 2, uint16_t, uint8_t>::type>::type;
     const int epr = p.elems_per_row;
@@ -239,18 +250,29 @@ __device__ void fill_stage_plain(const ScanParams& p, uint8_t* stage, long long 
     }
 }
 
-template <int MODE, int QB, int JC, bool L2, bool EMIT>
+// MODE: storage; QB: queries per pass; JC: chunks per lane held in registers (0 = generic
+// loop, query read from shared memory); LPR: lanes per row (32 / LPR lane groups per warp);
+// RW: rows each lane group scores per iteration; L2: metric; EMIT: write the score matrix
+// instead of selecting. One warp iteration scores (32 / LPR) * RW rows and shares a single
+// reduction and epilogue among them.
+template <int MODE, int QB, int JC, int LPR, int RW, bool L2, bool EMIT>
 __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams p) {
     using Traits = ModeTraits<MODE>;
     constexpr int EPC = Traits::kEpc;
     constexpr bool kInt = (MODE == kModeI8R);
-    constexpr int kQbLog = Log2<QB>::value;
+    constexpr int RPW = 32 / LPR;              // lane groups per warp
+    constexpr int kRowsPerWarp = RPW * RW;     // rows per warp iteration
+    constexpr int kRowsPerStep = kScanWarps * kRowsPerWarp;
+    constexpr int V = RW * QB;                 // partial sums per lane
+    static_assert(V <= LPR, "more partial sums than lanes in a row group");
+    constexpr int kGroupShift = Log2<LPR>::value - Log2<V>::value;
 
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float s_red[kScanWarps * QB];
     __shared__ float s_qscale[QB];
     __shared__ u64 s_scratch[32];
     __shared__ int s_last;
+    __shared__ int s_abort;
 
     const int tid = threadIdx.x;
     const int lane = tid & 31;
@@ -262,10 +284,11 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
     const int nq = min(QB, p.batch - q0);
 
     const int R = p.rows_per_tile;
-    const int tile_bytes = R * p.stride;
+    const int stage_bytes = p.stage_bytes;
     uint8_t* stages = smem;
     uint8_t* qsmem = smem + p.smem_query_off;
     u64* bars = reinterpret_cast<u64*>(smem + p.smem_bar_off);
+    const bool need_side = p.side_scales || p.mask != nullptr;
 
     TopkSmem tk;
     tk.buf = reinterpret_cast<u64*>(smem + p.smem_topk_off);
@@ -274,22 +297,34 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
     tk.cap = p.cap;
     tk.k = p.k;
 
-    const long long t_begin = (p.ntiles * cta) / G;
-    const long long t_end = (p.ntiles * (cta + 1)) / G;
-    const int my_tiles = static_cast<int>(t_end - t_begin);
+    const int t_begin = static_cast<int>((p.ntiles * cta) / G);
+    const int t_end = static_cast<int>((p.ntiles * (cta + 1)) / G);
+    const int my_tiles = t_end - t_begin;
     const int S = p.use_tma ? p.stages : 1;
 
-    auto issue = [&](int i) {
-        const long long tile = t_begin + i;
-        const long long row0 = tile * R;
-        const long long left = p.n - row0;
-        const int rows = static_cast<int>(left < R ? left : R);
+    // One bulk copy per tile for the rows, plus (full tiles only) one each for the per-row
+    // scales and allow-mask bytes, all completing on the stage's mbarrier.
+    auto issue = [&](int i, int s) {
+        const int row0 = (t_begin + i) * R;
+        const int rows = min(R, static_cast<int>(p.n - row0));
         const uint32_t bytes = static_cast<uint32_t>(rows) * static_cast<uint32_t>(p.row_bytes);
-        u64* bar = &bars[i % S];
-        mbar_arrive_expect_tx(bar, bytes);
-        bulk_copy_g2s(stages + (i % S) * tile_bytes, p.corpus + row0 * p.row_bytes, bytes, bar);
+        const bool side_bulk = p.side_tma && rows == R;
+        uint32_t total = bytes;
+        if (side_bulk) {
+            if (p.side_scales) total += 4u * R;
+            if (p.mask != nullptr) total += R;
+        }
+        uint8_t* st = stages + s * stage_bytes;
+        u64* bar = &bars[s];
+        mbar_arrive_expect_tx(bar, total);
+        bulk_copy_g2s(st, p.corpus + static_cast<size_t>(row0) * p.row_bytes, bytes, bar);
+        if (side_bulk) {
+            if (p.side_scales) bulk_copy_g2s(st + p.side_off_scales, p.row_scales + row0, 4u * R, bar);
+            if (p.mask != nullptr) bulk_copy_g2s(st + p.side_off_mask, p.mask + row0, R, bar);
+        }
     };
 
+    if (tid == 0) s_abort = 0;
     if (p.use_tma) {
         if (tid == 0) {
             for (int s = 0; s < S; ++s) mbar_init(&bars[s], 1);
@@ -297,7 +332,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
         }
         __syncthreads();
         if (tid == 0) {
-            for (int i = 0; i < S && i < my_tiles; ++i) issue(i);
+            for (int i = 0; i < S && i < my_tiles; ++i) issue(i, i);
         }
     }
 
@@ -308,22 +343,25 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
     }
     __syncthreads();
 
-    // Register-resident query slices for the fast path (JC chunks per lane, lane + 32 j).
+    // Warp-mode lane roles: lane group `grp` scores row (step base + grp); lane `gl` of the
+    // group owns 16-byte chunks gl, gl + LPR, ...
+    const int grp = lane / LPR;
+    const int gl = lane % LPR;
+
+    // Register-resident query slices for the fast path (JC chunks per lane).
     using QElem = typename std::conditional<kInt, int, float>::type;
     QElem qreg[JC > 0 ? JC : 1][QB][EPC];
     if constexpr (JC > 0 && MODE != kModeBin) {
 #pragma unroll
         for (int j = 0; j < JC; ++j) {
-            const int c = lane + 32 * j;
+            const int c = gl + LPR * j;
 #pragma unroll
             for (int q = 0; q < QB; ++q) {
 #pragma unroll
                 for (int e = 0; e < EPC; ++e) {
-                    if (c < p.nch) {
-                        qreg[j][q][e] = reinterpret_cast<const QElem*>(qsmem + q * p.query_bytes)[c * EPC + e];
-                    } else {
-                        qreg[j][q][e] = QElem(0);
-                    }
+                    qreg[j][q][e] = (c < p.nch)
+                        ? reinterpret_cast<const QElem*>(qsmem + q * p.query_bytes)[c * EPC + e]
+                        : QElem(0);
                 }
             }
         }
@@ -331,22 +369,30 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
 
     bool aborted = false;
     int i = 0;
+    int s = 0;
+    uint32_t phase = 0;
     for (; i < my_tiles; ++i) {
-        const long long tile = t_begin + i;
-        const long long row0 = tile * R;
-        const long long left = p.n - row0;
-        const int rows = static_cast<int>(left < R ? left : R);
+        const int row0 = (t_begin + i) * R;
+        const int rows = min(R, static_cast<int>(p.n - row0));
         bool failed = false;
-        int s = 0;
         if (p.use_tma) {
-            s = i % S;
-            failed = !mbar_wait_bounded(&bars[s], static_cast<uint32_t>((i / S) & 1), p.status,
-                                        kStatusTileWaitTimeout);
+            failed = !mbar_wait_bounded(&bars[s], phase, p.status, kStatusTileWaitTimeout);
         } else {
             fill_stage_plain<Traits::kElemBytes>(p, stages, row0, rows);
-            __syncthreads();
         }
-        const uint8_t* st = stages + s * tile_bytes;
+        uint8_t* st = stages + s * stage_bytes;
+        const bool side_plain = need_side && !(p.use_tma && p.side_tma && rows == R);
+        if (side_plain) {
+            for (int r = tid; r < rows; r += kScanThreads) {
+                if (p.side_scales) reinterpret_cast<float*>(st + p.side_off_scales)[r] = __ldg(p.row_scales + row0 + r);
+                if (p.mask != nullptr) st[p.side_off_mask + r] = __ldg(p.mask + row0 + r);
+            }
+        }
+        if (!p.use_tma || side_plain) __syncthreads();
+        const float* side_scale = reinterpret_cast<const float*>(st + p.side_off_scales);
+        const uint8_t* side_mask = st + p.side_off_mask;
+        const uint32_t id0 = p.id_base + static_cast<uint32_t>(row0);
+        bool need_flush = false;
 
         if constexpr (MODE == kModeBin) {
             // Thread per row. Each thread starts its chunk walk at a row-dependent offset so a
@@ -367,8 +413,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
                     }
                     u = (u + 1 == p.nch) ? 0 : u + 1;
                 }
-                const long long row = row0 + r;
-                const bool masked = (p.mask != nullptr) && (__ldg(p.mask + row) == 0);
+                const bool masked = (p.mask != nullptr) && side_mask[r] == 0;
 #pragma unroll
                 for (int q = 0; q < QB; ++q) {
                     if (q < nq) {
@@ -376,86 +421,105 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
                                                 static_cast<float>(p.dim));
                         if (masked) score = -FLT_MAX;
                         if constexpr (EMIT) {
-                            p.out_matrix[static_cast<size_t>(q0 + q) * p.n + row] = score;
+                            p.out_matrix[static_cast<size_t>(q0 + q) * p.n + row0 + r] = score;
                         } else {
-                            topk_offer(tk, q, make_key(score, p.id_base + static_cast<uint32_t>(row)));
+                            need_flush |= topk_offer_check(tk, q, make_key(score, id0 + r), R);
                         }
                     }
                 }
             }
         } else {
-            for (int r = warp; r < rows; r += kScanWarps) {
-                const uint8_t* rowp = st + r * p.stride;
-                QElem acc[QB];
+            for (int rb = warp * kRowsPerWarp; rb < rows; rb += kRowsPerStep) {
+                QElem acc[V];
 #pragma unroll
-                for (int q = 0; q < QB; ++q) acc[q] = QElem(0);
-                if constexpr (JC > 0) {
+                for (int v = 0; v < V; ++v) acc[v] = QElem(0);
 #pragma unroll
-                    for (int j = 0; j < JC; ++j) {
-                        const int c = lane + 32 * j;
-                        if (c < p.nch) {
+                for (int rr = 0; rr < RW; ++rr) {
+                    const int r = rb + rr * RPW + grp;    // uniform within the lane group
+                    if (r >= rows) continue;
+                    const uint8_t* rowp = st + r * p.stride;
+                    if constexpr (JC > 0) {
+                        // The fast path is only planned when the row is exactly JC sweeps of
+                        // the group, so every chunk index is in range.
+#pragma unroll
+                        for (int j = 0; j < JC; ++j) {
+                            const int c = gl + LPR * j;
                             const uint4 raw = lds128(rowp + c * 16);
 #pragma unroll
                             for (int q = 0; q < QB; ++q) {
                                 if constexpr (kInt) {
-                                    acc[q] = dp4a_chunk(raw, qreg[j][q], acc[q]);
+                                    acc[rr * QB + q] = dp4a_chunk(raw, qreg[j][q], acc[rr * QB + q]);
                                 } else {
-                                    accumulate_chunk<MODE, L2>(raw, qreg[j][q], p.scale, acc[q]);
+                                    accumulate_chunk<MODE, L2>(raw, qreg[j][q], p.scale, acc[rr * QB + q]);
+                                }
+                            }
+                        }
+                    } else {
+                        for (int c = gl; c < p.nch; c += LPR) {
+                            const uint4 raw = lds128(rowp + c * 16);
+#pragma unroll
+                            for (int q = 0; q < QB; ++q) {
+                                const uint8_t* qrow = qsmem + q * p.query_bytes + c * EPC * sizeof(QElem);
+                                QElem qv[EPC];
+#pragma unroll
+                                for (int e = 0; e < EPC; e += 4) {
+                                    const uint4 v = lds128(qrow + e * sizeof(QElem));
+                                    qv[e] = *reinterpret_cast<const QElem*>(&v.x);
+                                    qv[e + 1] = *reinterpret_cast<const QElem*>(&v.y);
+                                    qv[e + 2] = *reinterpret_cast<const QElem*>(&v.z);
+                                    qv[e + 3] = *reinterpret_cast<const QElem*>(&v.w);
+                                }
+                                if constexpr (kInt) {
+                                    acc[rr * QB + q] = dp4a_chunk(raw, qv, acc[rr * QB + q]);
+                                } else {
+                                    accumulate_chunk<MODE, L2>(raw, qv, p.scale, acc[rr * QB + q]);
                                 }
                             }
                         }
                     }
-                } else {
-                    for (int c = lane; c < p.nch; c += 32) {
-                        const uint4 raw = lds128(rowp + c * 16);
-#pragma unroll
-                        for (int q = 0; q < QB; ++q) {
-                            const uint8_t* qrow = qsmem + q * p.query_bytes + c * EPC * sizeof(QElem);
-                            QElem qv[EPC];
-#pragma unroll
-                            for (int e = 0; e < EPC; e += 4) {
-                                const uint4 v = lds128(qrow + e * sizeof(QElem));
-                                qv[e] = *reinterpret_cast<const QElem*>(&v.x);
-                                qv[e + 1] = *reinterpret_cast<const QElem*>(&v.y);
-                                qv[e + 2] = *reinterpret_cast<const QElem*>(&v.z);
-                                qv[e + 3] = *reinterpret_cast<const QElem*>(&v.w);
-                            }
-                            if constexpr (kInt) {
-                                acc[q] = dp4a_chunk(raw, qv, acc[q]);
-                            } else {
-                                accumulate_chunk<MODE, L2>(raw, qv, p.scale, acc[q]);
-                            }
-                        }
-                    }
                 }
-                transpose_reduce<QB>(acc, lane);
-                constexpr int kGroup = 32 >> kQbLog;
-                const int q = lane >> (5 - kQbLog);
-                if ((lane & (kGroup - 1)) == 0 && q < nq) {
-                    const long long row = row0 + r;
+                transpose_reduce<V, LPR>(acc, lane);
+                const int idx = gl >> kGroupShift;
+                const int q = idx % QB;
+                const int r = rb + (idx / QB) * RPW + grp;
+                if ((gl & ((1 << kGroupShift) - 1)) == 0 && q < nq && r < rows) {
                     float score;
                     if constexpr (kInt) {
-                        score = __fmul_rn(__fmul_rn(__int2float_rn(acc[0]), s_qscale[q]),
-                                          __ldg(p.row_scales + row));
+                        score = __fmul_rn(__fmul_rn(__int2float_rn(acc[0]), s_qscale[q]), side_scale[r]);
                     } else {
                         score = L2 ? -acc[0] : acc[0];
                     }
-                    if (p.mask != nullptr && __ldg(p.mask + row) == 0) score = -FLT_MAX;
+                    if (p.mask != nullptr && side_mask[r] == 0) score = -FLT_MAX;
                     if constexpr (EMIT) {
-                        p.out_matrix[static_cast<size_t>(q0 + q) * p.n + row] = score;
+                        p.out_matrix[static_cast<size_t>(q0 + q) * p.n + row0 + r] = score;
                     } else {
-                        topk_offer(tk, q, make_key(score, p.id_base + static_cast<uint32_t>(row)));
+                        need_flush |= topk_offer_check(tk, q, make_key(score, id0 + r), R);
                     }
                 }
             }
         }
 
-        aborted = __syncthreads_or(failed);
-        if constexpr (!EMIT) topk_maybe_flush(tk, nq, R, kScanThreads);
-        if (aborted) break;
+        // One barrier per tile. It both releases the stage for the next bulk copy and tells
+        // every thread whether some buffer needs a flush or some wait ran out (rare paths).
+        if (failed) s_abort = 1;
+        if (__syncthreads_or(failed || need_flush)) {
+            aborted = s_abort != 0;
+            if constexpr (!EMIT) {
+                uint32_t mask = 0;
+                for (int q = 0; q < nq; ++q) {
+                    if (tk.count[q] > tk.cap - R) mask |= 1u << q;
+                }
+                topk_flush_mask(tk, mask, kScanThreads);
+            }
+            if (aborted) break;
+        }
         if (p.use_tma && tid == 0 && i + S < my_tiles) {
             fence_proxy_async_shared();
-            issue(i + S);
+            issue(i + S, s);
+        }
+        if (++s == S) {
+            s = 0;
+            phase ^= 1u;
         }
     }
 

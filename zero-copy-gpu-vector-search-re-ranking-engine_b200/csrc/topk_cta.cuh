@@ -31,39 +31,57 @@ __device__ __forceinline__ void topk_offer(const TopkSmem& t, int q, u64 key) {
     }
 }
 
+// Offer that also reports whether this append filled the buffer past `cap - max_new`, i.e.
+// whether the CTA must flush before the next `max_new` offers.
+__device__ __forceinline__ bool topk_offer_check(const TopkSmem& t, int q, u64 key, int max_new) {
+    if (key > t.thr[q]) {
+        const int slot = atomicAdd(&t.count[q], 1);
+        t.buf[q * t.cap + slot] = key;
+        return slot >= t.cap - max_new;
+    }
+    return false;
+}
+
 // Sorts the buffers of the queries selected by `mask` (bit q) descending and truncates them
-// to k. Must be called by every thread of the CTA, after a __syncthreads() that follows the
-// last offer. Ends with a __syncthreads().
+// to k. Only the filled prefix is sorted (rounded up to a power of two), with shift-only index
+// arithmetic. Must be called by every thread of the CTA, after a __syncthreads() that follows
+// the last offer. Ends with a __syncthreads() when anything was flushed.
 __device__ inline void topk_flush_mask(const TopkSmem& t, uint32_t mask, int nthreads) {
+    if (mask == 0u) return;
     const int tid = threadIdx.x;
     int segs[32];
     int nseg = 0;
-#pragma unroll 1
-    for (int q = 0; q < 32; ++q) {
-        if (mask & (1u << q)) segs[nseg++] = q;
+    int longest = 2;
+    for (uint32_t m = mask; m != 0u; m &= m - 1u) {
+        const int q = __ffs(m) - 1;
+        segs[nseg++] = q;
+        longest = max(longest, t.count[q]);
     }
-    if (nseg == 0) return;
-    // Every thread must have read the counts it used for the decision before padding starts.
+    // Every thread must have read the counts it used before padding starts.
     __syncthreads();
+    int size = 2;
+    while (size < longest) size <<= 1;
     const int cap = t.cap;
     for (int s = 0; s < nseg; ++s) {
         const int q = segs[s];
-        for (int i = t.count[q] + tid; i < cap; i += nthreads) t.buf[q * cap + i] = 0ull;
+        for (int i = t.count[q] + tid; i < size; i += nthreads) t.buf[q * cap + i] = 0ull;
     }
     __syncthreads();
-    const int half = cap >> 1;
+    const int half = size >> 1;
+    const int half_log = __ffs(half) - 1;
     const int pairs = nseg * half;
-    for (int size = 2; size <= cap; size <<= 1) {
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+    for (int sz = 2; sz <= size; sz <<= 1) {
+        for (int stride = sz >> 1; stride > 0; stride >>= 1) {
+            const int stride_log = __ffs(stride) - 1;
             for (int p = tid; p < pairs; p += nthreads) {
-                const int seg = p / half;
-                const int i = p - seg * half;
-                const int lo = 2 * stride * (i / stride) + (i % stride);
+                const int seg = p >> half_log;
+                const int i = p & (half - 1);
+                const int lo = ((i >> stride_log) << (stride_log + 1)) | (i & (stride - 1));
                 const int hi = lo + stride;
                 u64* b = t.buf + segs[seg] * cap;
                 const u64 a = b[lo];
                 const u64 c = b[hi];
-                const bool descending = (lo & size) == 0;
+                const bool descending = (lo & sz) == 0;
                 if (descending ? (a < c) : (a > c)) {
                     b[lo] = c;
                     b[hi] = a;
@@ -79,6 +97,46 @@ __device__ inline void topk_flush_mask(const TopkSmem& t, uint32_t mask, int nth
         t.thr[q] = (n >= t.k) ? t.buf[q * cap + t.k - 1] : 0ull;
     }
     __syncthreads();
+}
+
+// Warp-cooperative descending bitonic sort of 32 * E keys held in registers, element index
+// lane * E + i. Strides below E swap registers inside a lane; larger strides exchange the
+// same register with the partner lane (lane ^ stride / E).
+template <int E>
+__device__ __forceinline__ void warp_sort_desc_regs(u64 (&v)[E], int lane) {
+#pragma unroll
+    for (int size = 2; size <= 32 * E; size <<= 1) {
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            if (stride < E) {
+#pragma unroll
+                for (int i = 0; i < E; ++i) {
+                    const int j = i ^ stride;
+                    if (j > i) {
+                        const int e = lane * E + i;
+                        const bool descending = (e & size) == 0;
+                        const u64 a = v[i];
+                        const u64 b = v[j];
+                        const bool swap = descending ? (a < b) : (a > b);
+                        v[i] = swap ? b : a;
+                        v[j] = swap ? a : b;
+                    }
+                }
+            } else {
+                const int lane_mask = stride / E;
+                const bool lower = (lane & lane_mask) == 0;
+#pragma unroll
+                for (int i = 0; i < E; ++i) {
+                    const int e = lane * E + i;
+                    const bool descending = (e & size) == 0;
+                    const u64 other = __shfl_xor_sync(0xffffffffu, v[i], lane_mask);
+                    const u64 hi = v[i] > other ? v[i] : other;
+                    const u64 lo = v[i] > other ? other : v[i];
+                    v[i] = (lower == descending) ? hi : lo;
+                }
+            }
+        }
+    }
 }
 
 // Flushes every query whose buffer could overflow on the next `max_new` offers. Called by
