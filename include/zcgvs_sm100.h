@@ -114,6 +114,26 @@ int zcgvs_scan_topk(const void* corpus, int dtype, float scale, const float* row
                     float* out_scores, void* workspace, size_t workspace_bytes, void* stream);
 
 /* ---------------------------------------------------------------------------------------
+ * Fused scan + top-k without a workspace, for callers that cannot allocate device memory
+ * (hosts that own every byte of GPU memory and forbid plug-ins from calling cudaMalloc, or
+ * paths where an allocation's implicit device synchronisation is not allowed). No
+ * counterpart in the reference: it has no entry point that runs without caller scratch.
+ *
+ * Same arguments, results and errors as zcgvs_scan_topk, minus the workspace. Scratch is a
+ * fixed 32 MiB __device__ array inside this library, reserved on every GPU that loads it until
+ * the process exits; searches needing more (zcgvs_scan_topk_workspace_bytes() > 32 MiB, e.g. a
+ * single query over more than ~4M rows) return ZCGVS_ERR_INVALID_ARG. The first call on a
+ * device looks up the array's device address (cudaGetSymbolAddress) and should come before any
+ * stream capture. All calls on a device share the array: each clears its header on `stream`,
+ * and calls whose kernels overlap on the GPU race, so callers must serialise them. Allocates
+ * nothing (no cudaMalloc / cudaFree).
+ * --------------------------------------------------------------------------------------- */
+int zcgvs_scan_topk_noalloc(const void* corpus, int dtype, float scale, const float* row_scales,
+                            int64_t doc_count, int dim, const float* queries, int batch,
+                            const uint8_t* mask, int metric, int k, int id_base, int* out_indices,
+                            float* out_scores, void* stream);
+
+/* ---------------------------------------------------------------------------------------
  * Score matrix. Same contract as the reference launchSimilarity
  * (include/zcgvs/cuda/similarity.cuh:20-30): writes [batch, doc_count] fp32 scores. Float
  * storage takes fp32 queries; binary storage takes packed query words [batch, ceil(dim/32)]

@@ -33,6 +33,8 @@ SIGNATURES = {
     "zcgvs_scan_topk_workspace_bytes": (_sz, [_i32, _i64, _i32, _i32, _i32]),
     "zcgvs_scan_topk": (_i32, [_P, _i32, _f32, _P, _i64, _i32, _P, _i32, _P, _i32, _i32, _i32,
                                _P, _P, _P, _sz, _P]),
+    "zcgvs_scan_topk_noalloc": (_i32, [_P, _i32, _f32, _P, _i64, _i32, _P, _i32, _P, _i32, _i32,
+                                       _i32, _P, _P, _P]),
     "zcgvs_similarity": (_i32, [_P, _i32, _f32, _P, _i64, _i32, _P, _i32, _P, _i32, _P, _P]),
 }
 
@@ -137,6 +139,25 @@ def scan_topk(corpus, dtype: int, dim: int, queries, k: int, *, scale: float = 1
     check(lib().zcgvs_scan_topk(_ptr(corpus), dtype, scale, _ptr(row_scales), doc_count, dim,
                                 _ptr(queries), batch, _ptr(mask), metric, k, id_base,
                                 _ptr(out[0]), _ptr(out[1]), _ptr(buf), buf.numel(), _stream(stream)))
+    return out
+
+
+def scan_topk_noalloc(corpus, dtype: int, dim: int, queries, k: int, *, scale: float = 1.0,
+                      row_scales=None, mask=None, metric: int = METRIC_DOT, id_base: int = 0,
+                      out=None, stream=None):
+    """zcgvs_scan_topk_noalloc: the fused search with the library's static scratch (no
+    workspace). Returns (indices int32 [B,k], scores fp32 [B,k])."""
+    import torch
+
+    doc_count = corpus.shape[0]
+    queries = queries.reshape(-1, dim)
+    batch = queries.shape[0]
+    if out is None:
+        out = (torch.empty((batch, k), dtype=torch.int32, device=queries.device),
+               torch.empty((batch, k), dtype=torch.float32, device=queries.device))
+    check(lib().zcgvs_scan_topk_noalloc(_ptr(corpus), dtype, scale, _ptr(row_scales), doc_count, dim,
+                                        _ptr(queries), batch, _ptr(mask), metric, k, id_base,
+                                        _ptr(out[0]), _ptr(out[1]), _stream(stream)))
     return out
 
 
