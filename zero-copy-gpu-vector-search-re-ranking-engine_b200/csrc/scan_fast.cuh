@@ -27,6 +27,9 @@ constexpr int kFastConsumers = 16;
 constexpr int kFastProducerWarp = kFastConsumers;
 constexpr int kFastSelectorWarp = kFastConsumers + 1;
 constexpr int kFastThreads = (kFastConsumers + 2) * 32;
+// Shared append region per consumer warp (keys), and the whole candidate buffer.
+constexpr int kRegionCap = 128;
+constexpr int kCandCap = kFastConsumers * kRegionCap;
 
 // Selector buffer: 32 lanes x kSelE registers.
 constexpr int kSelE = 8;
@@ -55,8 +58,8 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
     __shared__ int s_abort;
     __shared__ int s_done;
     __shared__ int s_last;
-    __shared__ int s_count;
     __shared__ int s_merge_count;
+    __shared__ int s_wcount[kFastConsumers];
 
     const int tid = threadIdx.x;
     const int lane = tid & 31;
@@ -67,25 +70,25 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
     const int R = p.rows_per_tile;
     const int S = p.stages;
     const int stage_bytes = p.stage_bytes;
-    const int ccap = p.cap;                       // shared candidate buffer capacity
     const int k = p.k;
 
     uint8_t* stages = smem;
     uint8_t* qsmem = smem + p.smem_query_off;
     u64* cbuf = reinterpret_cast<u64*>(smem + p.smem_topk_off);
-    u64* sbuf = cbuf + ccap;                      // selector buffer, kSelCap keys
+    u64* sbuf = cbuf + kCandCap;                  // selector buffer, kSelCap keys
     u64* full = reinterpret_cast<u64*>(smem + p.smem_bar_off);
     u64* empty = full + S;
     volatile int* abort_flag = &s_abort;
     volatile u64* cta_thr = &s_thr;
-    volatile int* vcount = &s_count;
 
     const int t_begin = static_cast<int>((p.ntiles * cta) / G);
     const int t_end = static_cast<int>((p.ntiles * (cta + 1)) / G);
     const int my_tiles = t_end - t_begin;
     const bool need_side = p.side_scales || p.mask != nullptr;
-    // Spill area for this (pass, CTA): one slot per row the CTA owns.
-    const long long spill_cap = static_cast<long long>(my_tiles) * R;
+    // Spill area for this (pass, CTA), one slice per consumer warp with a slot for every row the
+    // warp can score.
+    const long long warp_rows = static_cast<long long>(my_tiles) * kRowsPerWarp *
+                                ((R + kRowsPerStep - 1) / kRowsPerStep);
     unsigned long long* spill = p.spill + (static_cast<size_t>(pass) * G + cta) * p.spill_stride;
 
     if (tid == 0) {
@@ -97,23 +100,22 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
         s_thr = 0ull;
         s_abort = 0;
         s_done = 0;
-        s_count = 0;
     }
-    for (int i = tid; i < ccap; i += kFastThreads) cbuf[i] = 0ull;
+    for (int i = tid; i < kCandCap; i += kFastThreads) cbuf[i] = 0ull;
     stage_queries<MODE, 1, kFastThreads>(p, qsmem, s_qscale, pass, 1, s_red);
     __syncthreads();
 
     if (warp == kFastProducerWarp) {
         // ---------------- producer warp ----------------
         int issued = 0;
+        int s = 0;
+        uint32_t empty_phase = 0;
         for (int i = 0; i < my_tiles; ++i) {
-            const int s = i % S;
             if (i >= S) {
                 bool ok = true;
                 if (lane == 0) {
                     ok = !*abort_flag &&
-                         mbar_wait_bounded(&empty[s], static_cast<uint32_t>(((i / S) - 1) & 1), p.status,
-                                           kStatusTileWaitTimeout);
+                         mbar_wait_bounded(&empty[s], empty_phase, p.status, kStatusTileWaitTimeout);
                     if (!ok) *abort_flag = 1;
                 }
                 if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
@@ -146,6 +148,10 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
             }
             issued = i + 1;
             __syncwarp();
+            if (++s == S) {
+                s = 0;
+                if (i >= S) empty_phase ^= 1u;
+            }
         }
         // If the ring was abandoned, wait (bounded) for every copy still in flight before the
         // CTA can retire.
@@ -160,48 +166,48 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
         // slots). When sbuf fills it sorts it in registers, keeps k and publishes the k-th key.
         // Polling is bounded in time; giving up only leaves the threshold lower (the result
         // stays exact).
-        int processed = 0;
         int scount = 0;
         u64 sthr = 0ull;
         const u64 start = global_timer_ns();
+        volatile u64* vbuf = cbuf;
+        int pos = 0;                              // lane w < kFastConsumers follows region w
         for (uint32_t spin = 0;; ++spin) {
             const int done = *reinterpret_cast<volatile int*>(&s_done);
-            const int n = min(*vcount, ccap);
-            if (processed < n) {
-                for (int base = processed; base < n; base += 32) {
-                    const int i = base + lane;
-                    const u64 key = i < n ? cbuf[i] : 0ull;
-                    const bool take = key > sthr;
-                    const uint32_t ballot = __ballot_sync(0xffffffffu, take);
-                    if (take) sbuf[scount + __popc(ballot & ((1u << lane) - 1u))] = key;
-                    scount += __popc(ballot);
-                    if (scount > kSelCap - 32) {
-                        __syncwarp();
-                        u64 v[kSelE];
+            bool progress = false;
+            for (;;) {
+                const u64 key = (lane < kFastConsumers && pos < kRegionCap) ? vbuf[lane * kRegionCap + pos] : 0ull;
+                const bool ready = key != 0ull;
+                const uint32_t any = __ballot_sync(0xffffffffu, ready);
+                if (any == 0u) break;
+                progress = true;
+                pos += ready ? 1 : 0;
+                const bool take = ready && key > sthr;
+                const uint32_t ballot = __ballot_sync(0xffffffffu, take);
+                if (take) sbuf[scount + __popc(ballot & ((1u << lane) - 1u))] = key;
+                scount += __popc(ballot);
+                if (scount > kSelCap - 32 || (sthr == 0ull && scount >= k + 32)) {
+                    __syncwarp();
+                    u64 v[kSelE];
 #pragma unroll
-                        for (int e = 0; e < kSelE; ++e) {
-                            const int at = lane * kSelE + e;
-                            v[e] = at < scount ? sbuf[at] : 0ull;
-                        }
-                        warp_sort_desc_regs<kSelE>(v, lane);
-                        __syncwarp();
-#pragma unroll
-                        for (int e = 0; e < kSelE; ++e) sbuf[lane * kSelE + e] = v[e];
-                        __syncwarp();
-                        if (scount >= k) {
-                            sthr = sbuf[k - 1];
-                            if (lane == 0) *cta_thr = sthr;
-                        }
-                        scount = min(scount, k);
+                    for (int e = 0; e < kSelE; ++e) {
+                        const int at = lane * kSelE + e;
+                        v[e] = at < scount ? sbuf[at] : 0ull;
                     }
+                    warp_sort_desc_regs<kSelE>(v, lane);
+                    __syncwarp();
+#pragma unroll
+                    for (int e = 0; e < kSelE; ++e) sbuf[lane * kSelE + e] = v[e];
+                    __syncwarp();
+                    if (scount >= k) {
+                        sthr = sbuf[k - 1];
+                        if (lane == 0) *cta_thr = sthr;
+                    }
+                    scount = min(scount, k);
                 }
-                processed = n;
-            } else if (done == kFastConsumers || n >= ccap) {
-                break;
-            } else {
-                __nanosleep(128);
-                if ((spin & 63u) == 0u && global_timer_ns() - start > kWaitBudgetNs) break;
             }
+            if (done == kFastConsumers && !progress) break;
+            __nanosleep(128);
+            if ((spin & 63u) == 0u && global_timer_ns() - start > kWaitBudgetNs) break;
         }
     } else {
         // ---------------- consumer warps ----------------
@@ -216,15 +222,18 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
             }
         }
         const float qscale = s_qscale[0];
+        u64* region = cbuf + warp * kRegionCap;
+        unsigned long long* wspill = spill + warp * warp_rows;
+        int wcount = 0;         // keys this warp appended (replicated in every lane)
 
+        int s = 0;
+        uint32_t full_phase = 0;
         for (int i = 0; i < my_tiles; ++i) {
-            const int s = i % S;
             const int row0 = (t_begin + i) * R;
             const int rows = min(R, static_cast<int>(p.n - row0));
             bool ok = true;
             if (lane == 0) {
-                ok = !*abort_flag && mbar_wait_bounded(&full[s], static_cast<uint32_t>((i / S) & 1),
-                                                       p.status, kStatusTileWaitTimeout);
+                ok = !*abort_flag && mbar_wait_bounded(&full[s], full_phase, p.status, kStatusTileWaitTimeout);
                 if (!ok) *abort_flag = 1;
             }
             if (!__shfl_sync(0xffffffffu, ok ? 1 : 0, 0)) break;
@@ -232,6 +241,10 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
             const float* side_scale = reinterpret_cast<const float*>(st + p.side_off_scales);
             const uint8_t* side_mask = st + p.side_off_mask;
             const uint32_t id0 = p.id_base + static_cast<uint32_t>(row0);
+            // The threshold only rises; reading it once per tile keeps it off the row path.
+            const u64 thr = *cta_thr;
+            const float thr_score = score_from_bits(static_cast<uint32_t>(thr >> 32));
+            const bool full_tile = rows == R;
 
             for (int rb = warp * kRowsPerWarp; rb < rows; rb += kRowsPerStep) {
                 QElem acc[RW];
@@ -239,11 +252,11 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
                 for (int rr = 0; rr < RW; ++rr) {
                     acc[rr] = QElem(0);
                     const int r = rb + rr * RPW + grp;
-                    if (r < rows) {
-                        const uint8_t* rowp = st + r * p.stride;
+                    if (full_tile || r < rows) {
+                        const uint8_t* rowp = st + r * p.stride + gl * 16;
 #pragma unroll
                         for (int j = 0; j < JC; ++j) {
-                            const uint4 raw = lds128(rowp + (gl + LPR * j) * 16);
+                            const uint4 raw = lds128(rowp + LPR * 16 * j);
                             if constexpr (kInt) {
                                 acc[rr] = dp4a_chunk(raw, qreg[j], acc[rr]);
                             } else {
@@ -254,7 +267,8 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
                 }
                 transpose_reduce<RW, LPR>(acc, lane);
                 const int r = rb + (gl >> kGroupShift) * RPW + grp;
-                const bool leader = (gl & ((1 << kGroupShift) - 1)) == 0 && r < rows;
+                const bool leader = (gl & ((1 << kGroupShift) - 1)) == 0 && (full_tile || r < rows);
+                bool take = false;
                 u64 key = 0ull;
                 if (leader) {
                     float score;
@@ -264,28 +278,36 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
                         score = acc[0];
                     }
                     if (p.mask != nullptr && side_mask[r] == 0) score = -FLT_MAX;
-                    key = make_key(score, id0 + r);
-                }
-                const bool take = leader && key > *cta_thr;
-                const uint32_t ballot = __ballot_sync(0xffffffffu, take);
-                if (ballot != 0u) {
-                    int base = 0;
-                    if (lane == 0) base = atomicAdd(&s_count, __popc(ballot));
-                    base = __shfl_sync(0xffffffffu, base, 0);
-                    if (take) {
-                        const int slot = base + __popc(ballot & ((1u << lane) - 1u));
-                        if (slot < ccap) {
-                            cbuf[slot] = key;
-                        } else if (slot - ccap < spill_cap) {
-                            spill[slot - ccap] = key;
-                        }
+                    // Cheap float pre-check; only candidates at or above the threshold's score
+                    // pay for the exact 64-bit key comparison.
+                    if (!(score < thr_score) || thr == 0ull) {
+                        key = make_key(score, id0 + r);
+                        take = key > thr;
                     }
                 }
+                const uint32_t ballot = __ballot_sync(0xffffffffu, take);
+                if (take) {
+                    const int slot = wcount + __popc(ballot & ((1u << lane) - 1u));
+                    if (slot < kRegionCap) {
+                        region[slot] = key;
+                    } else if (slot - kRegionCap < warp_rows) {
+                        wspill[slot - kRegionCap] = key;
+                    }
+                }
+                wcount += __popc(ballot);
             }
             __syncwarp();
             if (lane == 0) mbar_arrive_cta(&empty[s]);
+            if (++s == S) {
+                s = 0;
+                full_phase ^= 1u;
+            }
         }
-        if (lane == 0) atomicAdd(&s_done, 1);
+        if (lane == 0) {
+            s_wcount[warp] = wcount;
+            __threadfence_block();
+            atomicAdd(&s_done, 1);
+        }
     }
     __syncthreads();
 
@@ -304,15 +326,15 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
         s_merge_thr = floor_key > 0ull ? floor_key - 1ull : 0ull;
     }
     __syncthreads();
-    const int total = min(s_count, static_cast<int>(ccap + spill_cap));
-    for (int base = 0; base < total; base += kFastThreads) {
-        const int i = base + tid;
-        if (i < total) {
-            const u64 key = i < ccap ? cbuf[i] : __ldcg(spill + (i - ccap));
-            if (key != 0ull) topk_offer(mt, 0, key);
-        }
-        __syncthreads();
-        topk_maybe_flush_one(mt, 0, kFastThreads, kFastThreads);
+    // All shared regions in one wide round, then any warp's spill slice (rare).
+    topk_offer_all<4>(mt, 0, kCandCap, floor_key, [&](int i) {
+        const int w = i / kRegionCap;
+        return (i - w * kRegionCap) < s_wcount[w] ? cbuf[i] : 0ull;
+    }, kFastThreads);
+    for (int w = 0; w < kFastConsumers; ++w) {
+        const int extra = static_cast<int>(min(static_cast<long long>(s_wcount[w]) - kRegionCap, warp_rows));
+        topk_offer_all<4>(mt, 0, extra, floor_key,
+                          [&](int i) { return __ldcg(spill + w * warp_rows + i); }, kFastThreads);
     }
     __syncthreads();
     topk_flush_mask(mt, 1u, kFastThreads);

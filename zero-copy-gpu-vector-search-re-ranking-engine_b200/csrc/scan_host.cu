@@ -21,6 +21,7 @@ constexpr size_t kWorkspaceAlign = 256;
 
 struct ScanPlan {
     int mode = 0;
+    int k = 1;
     int qb = 1;
     int jc = 0;
     bool l2 = false;
@@ -55,6 +56,7 @@ struct ScanPlan {
     int fast_ccap = 0;
     int fast_scap = 0;
     int fast_cap_final = 0;
+    int cap_final = 0;
     long long fast_spill_stride = 0;
     int fast_query_off = 0;
     int fast_topk_off = 0;
@@ -102,7 +104,15 @@ bool layout(ScanPlan& plan, int budget) {
         return false;
     }
     plan.stages = stages;
-    plan.smem_query_off = static_cast<int>(round_up(static_cast<size_t>(stages) * tile_bytes, 128));
+    // After the scan the ring hosts the cross-CTA merge buffer: at least k + kScanThreads keys.
+    size_t ring = static_cast<size_t>(stages) * tile_bytes;
+    if (!plan.emit) {
+        ring = std::max(ring, 8 * static_cast<size_t>(next_pow2(plan.k + kScanThreads)));
+        size_t cap = 1;
+        while (cap * 2 * 8 <= ring) cap *= 2;
+        plan.cap_final = static_cast<int>(cap);
+    }
+    plan.smem_query_off = static_cast<int>(round_up(ring, 128));
     plan.smem_topk_off = plan.smem_query_off + static_cast<int>(round_up(query, 128));
     plan.smem_bar_off = plan.smem_topk_off + static_cast<int>(round_up(topk, 128));
     plan.smem_total = plan.smem_bar_off + kMaxStages * 8;
@@ -122,6 +132,7 @@ int make_plan(int dtype, long long n, int dim, int batch, int k, int metric, boo
         return fail(ZCGVS_ERR_UNSUPPORTED, "zcgvs: the per-row int8 store scores dot/cosine only");
     }
     plan.emit = emit;
+    plan.k = k;
     plan.side_scales = (plan.mode == kModeI8R);
     plan.side_mask = has_mask;
     const long long rb = row_bytes_of(dtype, dim);
@@ -182,9 +193,9 @@ int make_plan(int dtype, long long n, int dim, int batch, int k, int metric, boo
     // holds the stage ring, the query, the CTA candidate buffer and the selector's buffer; the
     // ring must also fit the final merge buffer once the scan is over.
     if (plan.jc > 0 && plan.use_tma && k <= kSelCap - 64 && !(plan.mode == kModeI8M && plan.jc > 4)) {
-        plan.fast_ccap = 2048;
+        plan.fast_ccap = kCandCap;
         plan.fast_scap = kSelCap;
-        plan.fast_cap_final = next_pow2(k + std::max(kFastThreads, plan.grid_rows));
+        plan.fast_cap_final = next_pow2(k + 8 * kFastThreads);
         const int query = static_cast<int>(round_up(plan.query_bytes, 128));
         const int bufs = 8 * (plan.fast_ccap + plan.fast_scap);
         const int fixed = query + bufs + 2 * kMaxStages * 8 + 128;
@@ -197,7 +208,9 @@ int make_plan(int dtype, long long n, int dim, int batch, int k, int metric, boo
             plan.fast_topk_off = plan.fast_query_off + query;
             plan.fast_bar_off = plan.fast_topk_off + bufs;
             plan.fast_smem = plan.fast_bar_off + 2 * kMaxStages * 8;
-            plan.fast_spill_stride = (plan.ntiles + plan.grid_rows - 1) / plan.grid_rows * plan.rows_per_tile;
+            // Per consumer warp: a slot for every row it can score (whole 64-row CTA steps).
+            const long long steps = (plan.rows_per_tile + 63) / 64;
+            plan.fast_spill_stride = (plan.ntiles + plan.grid_rows - 1) / plan.grid_rows * steps * 64;
         }
     }
     plan.ws_header = round_up(16 + 4 * static_cast<size_t>(plan.passes), kWorkspaceAlign);
@@ -254,7 +267,7 @@ int launch(const ScanPlan& plan, ScanParams& params, cudaStream_t stream) {
     params.stages = plan.fast ? plan.fast_stages : plan.stages;
     params.cap = plan.fast ? plan.fast_ccap : plan.cap;
     params.merge_cap = plan.fast_scap;
-    params.cap_final = plan.fast_cap_final;
+    params.cap_final = plan.fast ? plan.fast_cap_final : plan.cap_final;
     params.spill_stride = plan.fast_spill_stride;
     params.row_bytes = plan.row_bytes;
     params.stride = plan.stride;

@@ -551,10 +551,19 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
     __syncthreads();
     if (!s_last) return;
     __threadfence();
+    // The stage ring is idle now: it holds the merge buffer (p.cap_final keys).
+    __shared__ int s_merge_count;
+    __shared__ u64 s_merge_thr;
+    TopkSmem mt;
+    mt.buf = reinterpret_cast<u64*>(stages);
+    mt.count = &s_merge_count;
+    mt.thr = &s_merge_thr;
+    mt.cap = p.cap_final;
+    mt.k = p.k;
     for (int q = 0; q < nq; ++q) {
         const unsigned long long* src = p.lists + static_cast<size_t>(q0 + q) * G * p.k;
-        topk_merge_lists(tk, q, src, G, kScanThreads, s_scratch);
-        topk_write(tk, q, p.out_idx + static_cast<size_t>(q0 + q) * p.k,
+        topk_merge_lists(mt, 0, src, G, kScanThreads, s_scratch);
+        topk_write(mt, 0, p.out_idx + static_cast<size_t>(q0 + q) * p.k,
                    p.out_scores + static_cast<size_t>(q0 + q) * p.k, kScanThreads);
         __syncthreads();
     }

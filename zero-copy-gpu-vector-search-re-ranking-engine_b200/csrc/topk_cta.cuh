@@ -164,48 +164,84 @@ __device__ __forceinline__ void topk_flush_all(const TopkSmem& t, int nq, int nt
     topk_flush_mask(t, nq >= 32 ? 0xffffffffu : ((1u << nq) - 1u), nthreads);
 }
 
-// Merges `lists` sorted descending lists of k keys each (list c of query q at
-// src[(q * lists + c) * k]) into the accumulator slot `q_local`, which must be empty.
+// Offers every key >= floor_key among `total` keys, key i fetched by get(i), into slot q.
+// Each thread holds U independent fetches in flight per round, so a round costs one memory
+// latency however many keys it covers; the buffer is flushed between rounds when needed.
+// Requires t.cap >= t.k + U * nthreads. Called by every thread of the CTA.
+template <int U, typename Get>
+__device__ void topk_offer_all(const TopkSmem& t, int q, int total, u64 floor_key, Get get,
+                               int nthreads) {
+    const int lane = threadIdx.x & 31;
+    for (int base = 0; base < total; base += nthreads * U) {
+        u64 v[U];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const int i = base + u * nthreads + static_cast<int>(threadIdx.x);
+            v[u] = i < total ? get(i) : 0ull;
+        }
+        // Keep every fetch of the round ahead of the first offer: without this the compiler
+        // sinks each load next to its (atomic) offer and the round pays one memory latency
+        // per key instead of one in total.
+        asm volatile("" ::: "memory");
+        const u64 thr = t.thr[q];
+#pragma unroll
+        for (int u = 0; u < U; ++u) {
+            const bool take = v[u] != 0ull && v[u] >= floor_key && v[u] > thr;
+            const uint32_t ballot = __ballot_sync(0xffffffffu, take);
+            if (ballot != 0u) {
+                int slot = 0;
+                if (lane == 0) slot = atomicAdd(&t.count[q], __popc(ballot));
+                slot = __shfl_sync(0xffffffffu, slot, 0) + __popc(ballot & ((1u << lane) - 1u));
+                if (take) t.buf[q * t.cap + slot] = v[u];
+            }
+        }
+        __syncthreads();
+        topk_maybe_flush_one(t, q, U * nthreads, nthreads);
+    }
+}
+
+// Merges `lists` sorted descending lists of k keys each (list c at src[c * k]) into slot
+// q_local of the accumulator, which must be empty and have cap >= k + nthreads and
+// cap >= next_pow2(lists) (rounds are 8, 2 or 1 keys per thread wide, whichever the capacity
+// allows).
 //
-// Prefilter: every list holds k keys >= its own k-th key, so the global k-th key is at least
-// T = max over lists of their k-th key. Only the prefix of each list that is >= T can reach
-// the result, and it is usually a handful of entries, so the merge touches ~k keys instead of
-// lists * k. Lists are walked in lock-step rounds with at most `lists` offers per round.
-__device__ inline void topk_merge_lists(const TopkSmem& t, int q_local,
-                                        const u64* src, int lists, int nthreads,
-                                        u64* s_scratch /* >= 32 entries */) {
+// Floor: pick j with lists * (j + 1) >= k and let m = ceil(k / (j + 1)). The m-th largest of
+// the lists' j-th keys, F, has m lists each holding j + 1 keys >= F, i.e. at least k keys, so
+// the merged k-th key is >= F and only keys >= F are offered. For many short lists (one per
+// CTA) j = 0: F is the k-th largest list head, which leaves a few hundred candidates out of
+// lists * k.
+__device__ inline void topk_merge_lists(const TopkSmem& t, int q_local, const u64* src, int lists,
+                                        int nthreads, u64* s_scratch /* >= 32 entries */) {
+    (void)s_scratch;
     const int tid = threadIdx.x;
     const int k = t.k;
-    u64 local_max = 0ull;
-    for (int c = tid; c < lists; c += nthreads) {
-        const u64 kth = __ldcg(src + static_cast<size_t>(c) * k + (k - 1));
-        local_max = kth > local_max ? kth : local_max;
+    const int j = (k + lists - 1) / lists - 1;
+    const int m = (k + j) / (j + 1);
+    int width = 2;
+    while (width < lists) width <<= 1;
+    // Sort the lists' j-th keys (descending) in the front of the buffer; F = entry m - 1.
+    u64* heads = t.buf + q_local * t.cap;
+    for (int c = tid; c < width; c += nthreads) {
+        heads[c] = c < lists ? __ldcg(src + static_cast<size_t>(c) * k + j) : 0ull;
     }
-    local_max = warp_max_u64(local_max);
-    if ((tid & 31) == 0) s_scratch[tid >> 5] = local_max;
+    if (tid == 0) t.count[q_local] = width;
     __syncthreads();
-    u64 floor_key = 0ull;
-    for (int w = 0; w < (nthreads + 31) / 32; ++w) {
-        floor_key = s_scratch[w] > floor_key ? s_scratch[w] : floor_key;
-    }
+    topk_flush_mask(t, 1u << q_local, nthreads);    // sorts `width` keys; keeps min(width, k)
+    const u64 floor_key = heads[m - 1];
+    __syncthreads();
     if (tid == 0) {
         t.count[q_local] = 0;
         t.thr[q_local] = floor_key > 0ull ? floor_key - 1ull : 0ull;
     }
     __syncthreads();
-    for (int j = 0; j < k; ++j) {
-        bool active = false;
-        for (int c = tid; c < lists; c += nthreads) {
-            const u64 key = __ldcg(src + static_cast<size_t>(c) * k + j);
-            if (key != 0ull && key >= floor_key) {
-                active = true;
-                topk_offer(t, q_local, key);
-            }
-        }
-        if (!__syncthreads_or(active)) break;
-        topk_maybe_flush_one(t, q_local, lists, nthreads);
+    auto fetch = [&](int i) { return __ldcg(src + i); };
+    if (t.cap >= k + 8 * nthreads) {
+        topk_offer_all<8>(t, q_local, lists * k, floor_key, fetch, nthreads);
+    } else if (t.cap >= k + 2 * nthreads) {
+        topk_offer_all<2>(t, q_local, lists * k, floor_key, fetch, nthreads);
+    } else {
+        topk_offer_all<1>(t, q_local, lists * k, floor_key, fetch, nthreads);
     }
-    __syncthreads();
     topk_flush_mask(t, 1u << q_local, nthreads);
 }
 
