@@ -134,6 +134,26 @@ __device__ __forceinline__ void bulk_copy_g2s(void* dst_smem, const void* src_gm
         : "memory");
 }
 
+// L2 policy for data read exactly once (the corpus stream): its lines are evicted first, so
+// the kernel's own code, candidate lists and counters stay in L2 while hundreds of MB stream
+// through it. Without it the one-shot tail of the kernel (CTA selection, last-CTA merge)
+// fetches its instructions from DRAM.
+__device__ __forceinline__ u64 l2_policy_evict_first() {
+    u64 policy;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));
+    return policy;
+}
+
+// bulk_copy_g2s with an L2 cache policy from createpolicy.
+__device__ __forceinline__ void bulk_copy_g2s_hint(void* dst_smem, const void* src_gmem, uint32_t bytes,
+                                                   u64* bar, u64 policy) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1], %2, "
+        "[%3], %4;" ::"r"(smem_u32(dst_smem)),
+        "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar)), "l"(policy)
+        : "memory");
+}
+
 // ---------------------------------------------------------------------------------------
 // Warp reductions.
 // ---------------------------------------------------------------------------------------

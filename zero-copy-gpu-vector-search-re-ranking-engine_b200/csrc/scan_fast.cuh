@@ -59,6 +59,7 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
     __shared__ int s_done;
     __shared__ int s_last;
     __shared__ int s_merge_count;
+    __shared__ int s_sel_complete;
     __shared__ int s_wcount[kFastConsumers];
 
     const int tid = threadIdx.x;
@@ -100,6 +101,7 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
         s_thr = 0ull;
         s_abort = 0;
         s_done = 0;
+        s_sel_complete = 0;
     }
     for (int i = tid; i < kCandCap; i += kFastThreads) cbuf[i] = 0ull;
     stage_queries<MODE, 1, kFastThreads>(p, qsmem, s_qscale, pass, 1, s_red);
@@ -107,6 +109,7 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
 
     if (warp == kFastProducerWarp) {
         // ---------------- producer warp ----------------
+        const u64 stream_policy = l2_policy_evict_first();
         int issued = 0;
         int s = 0;
         uint32_t empty_phase = 0;
@@ -140,10 +143,16 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
                 }
                 fence_proxy_async_shared();
                 mbar_arrive_expect_tx(&full[s], total);
-                bulk_copy_g2s(st, p.corpus + static_cast<size_t>(row0) * p.row_bytes, bytes, &full[s]);
+                bulk_copy_g2s_hint(st, p.corpus + static_cast<size_t>(row0) * p.row_bytes, bytes, &full[s],
+                                   stream_policy);
                 if (side_bulk) {
-                    if (p.side_scales) bulk_copy_g2s(st + p.side_off_scales, p.row_scales + row0, 4u * R, &full[s]);
-                    if (p.mask != nullptr) bulk_copy_g2s(st + p.side_off_mask, p.mask + row0, R, &full[s]);
+                    if (p.side_scales) {
+                        bulk_copy_g2s_hint(st + p.side_off_scales, p.row_scales + row0, 4u * R, &full[s],
+                                           stream_policy);
+                    }
+                    if (p.mask != nullptr) {
+                        bulk_copy_g2s_hint(st + p.side_off_mask, p.mask + row0, R, &full[s], stream_policy);
+                    }
                 }
             }
             issued = i + 1;
@@ -173,6 +182,8 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
         int pos = 0;                              // lane w < kFastConsumers follows region w
         for (uint32_t spin = 0;; ++spin) {
             const int done = *reinterpret_cast<volatile int*>(&s_done);
+            // Keys appended before a consumer counted itself done are visible after this fence.
+            __threadfence_block();
             bool progress = false;
             for (;;) {
                 const u64 key = (lane < kFastConsumers && pos < kRegionCap) ? vbuf[lane * kRegionCap + pos] : 0ull;
@@ -205,9 +216,28 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
                     scount = min(scount, k);
                 }
             }
-            if (done == kFastConsumers && !progress) break;
+            if (done == kFastConsumers && !progress) {
+                if (lane == 0) s_sel_complete = 1;
+                break;
+            }
             __nanosleep(128);
             if ((spin & 63u) == 0u && global_timer_ns() - start > kWaitBudgetNs) break;
+        }
+        // Keep the selector's state for the end of the kernel: sort it once more so sbuf holds
+        // the exact top of every key it saw.
+        __syncwarp();
+        {
+            u64 v[kSelE];
+#pragma unroll
+            for (int e = 0; e < kSelE; ++e) {
+                const int at = lane * kSelE + e;
+                v[e] = at < scount ? sbuf[at] : 0ull;
+            }
+            warp_sort_desc_regs<kSelE>(v, lane);
+            __syncwarp();
+#pragma unroll
+            for (int e = 0; e < kSelE; ++e) sbuf[lane * kSelE + e] = v[e];
+            if (lane == 0) s_merge_count = min(scount, k);
         }
     } else {
         // ---------------- consumer warps ----------------
@@ -311,15 +341,24 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
     }
     __syncthreads();
 
-    // Select this CTA's top-k from every candidate at or above the selector's threshold: the
-    // shared buffer first, then any spill. The stage ring (free now) holds the merge buffer;
-    // offers run in lock-step rounds of at most kFastThreads keys between flush checks.
+    // The stage ring (free now) holds the merge buffer.
     TopkSmem mt;
     mt.buf = reinterpret_cast<u64*>(stages);
     mt.count = &s_merge_count;
     mt.thr = &s_merge_thr;
     mt.cap = p.cap_final;
     mt.k = k;
+    // When no warp spilled and the selector followed every region to the end, it has seen
+    // every candidate: its sorted buffer already is this CTA's list.
+    bool spilled = false;
+    for (int w = 0; w < kFastConsumers; ++w) spilled |= s_wcount[w] > kRegionCap;
+    if (!spilled && s_sel_complete) {
+        unsigned long long* dst = p.lists + (static_cast<size_t>(pass) * G + cta) * k;
+        const int n = s_merge_count;
+        for (int j = tid; j < k; j += kFastThreads) dst[j] = j < n ? sbuf[j] : 0ull;
+    } else {
+    // Otherwise select this CTA's top-k from every candidate at or above the selector's
+    // threshold: the shared regions first, then any spill.
     const u64 floor_key = s_thr;
     if (tid == 0) {
         s_merge_count = 0;
@@ -342,6 +381,7 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
         unsigned long long* dst = p.lists + (static_cast<size_t>(pass) * G + cta) * k;
         const int n = s_merge_count;
         for (int j = tid; j < k; j += kFastThreads) dst[j] = j < n ? mt.buf[j] : 0ull;
+    }
     }
     __threadfence();
     __syncthreads();

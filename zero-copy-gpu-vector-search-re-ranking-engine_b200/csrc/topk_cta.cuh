@@ -42,6 +42,46 @@ __device__ __forceinline__ bool topk_offer_check(const TopkSmem& t, int q, u64 k
     return false;
 }
 
+// Warp-cooperative descending bitonic sort of 32 * E keys held in registers, element index
+// lane * E + i. Strides below E swap registers inside a lane; larger strides exchange the
+// same register with the partner lane (lane ^ stride / E).
+template <int E>
+__device__ __forceinline__ void warp_sort_desc_regs(u64 (&v)[E], int lane) {
+#pragma unroll
+    for (int size = 2; size <= 32 * E; size <<= 1) {
+#pragma unroll
+        for (int stride = size >> 1; stride > 0; stride >>= 1) {
+            if (stride < E) {
+#pragma unroll
+                for (int i = 0; i < E; ++i) {
+                    const int j = i ^ stride;
+                    if (j > i) {
+                        const int e = lane * E + i;
+                        const bool descending = (e & size) == 0;
+                        const u64 a = v[i];
+                        const u64 b = v[j];
+                        const bool swap = descending ? (a < b) : (a > b);
+                        v[i] = swap ? b : a;
+                        v[j] = swap ? a : b;
+                    }
+                }
+            } else {
+                const int lane_mask = stride / E;
+                const bool lower = (lane & lane_mask) == 0;
+#pragma unroll
+                for (int i = 0; i < E; ++i) {
+                    const int e = lane * E + i;
+                    const bool descending = (e & size) == 0;
+                    const u64 other = __shfl_xor_sync(0xffffffffu, v[i], lane_mask);
+                    const u64 hi = v[i] > other ? v[i] : other;
+                    const u64 lo = v[i] > other ? other : v[i];
+                    v[i] = (lower == descending) ? hi : lo;
+                }
+            }
+        }
+    }
+}
+
 // Sorts the buffers of the queries selected by `mask` (bit q) descending and truncates them
 // to k. Only the filled prefix is sorted (rounded up to a power of two), with shift-only index
 // arithmetic. Must be called by every thread of the CTA, after a __syncthreads() that follows
@@ -97,46 +137,6 @@ __device__ inline void topk_flush_mask(const TopkSmem& t, uint32_t mask, int nth
         t.thr[q] = (n >= t.k) ? t.buf[q * cap + t.k - 1] : 0ull;
     }
     __syncthreads();
-}
-
-// Warp-cooperative descending bitonic sort of 32 * E keys held in registers, element index
-// lane * E + i. Strides below E swap registers inside a lane; larger strides exchange the
-// same register with the partner lane (lane ^ stride / E).
-template <int E>
-__device__ __forceinline__ void warp_sort_desc_regs(u64 (&v)[E], int lane) {
-#pragma unroll
-    for (int size = 2; size <= 32 * E; size <<= 1) {
-#pragma unroll
-        for (int stride = size >> 1; stride > 0; stride >>= 1) {
-            if (stride < E) {
-#pragma unroll
-                for (int i = 0; i < E; ++i) {
-                    const int j = i ^ stride;
-                    if (j > i) {
-                        const int e = lane * E + i;
-                        const bool descending = (e & size) == 0;
-                        const u64 a = v[i];
-                        const u64 b = v[j];
-                        const bool swap = descending ? (a < b) : (a > b);
-                        v[i] = swap ? b : a;
-                        v[j] = swap ? a : b;
-                    }
-                }
-            } else {
-                const int lane_mask = stride / E;
-                const bool lower = (lane & lane_mask) == 0;
-#pragma unroll
-                for (int i = 0; i < E; ++i) {
-                    const int e = lane * E + i;
-                    const bool descending = (e & size) == 0;
-                    const u64 other = __shfl_xor_sync(0xffffffffu, v[i], lane_mask);
-                    const u64 hi = v[i] > other ? v[i] : other;
-                    const u64 lo = v[i] > other ? other : v[i];
-                    v[i] = (lower == descending) ? hi : lo;
-                }
-            }
-        }
-    }
 }
 
 // Flushes every query whose buffer could overflow on the next `max_new` offers. Called by
