@@ -143,6 +143,35 @@ int zcgvs_similarity(const void* corpus, int dtype, float scale, const float* ro
                      int64_t doc_count, int dim, const void* queries, int batch,
                      const uint8_t* mask, int metric, float* scores, void* stream);
 
+/* ---------------------------------------------------------------------------------------
+ * Fused candidate rescoring. Replaces the rescore chain of Searcher::recordPipeline
+ * (src/search/searcher.cpp:266-279): launchGatherRescore (src/cuda/rescore.cu:87-130), the
+ * second launchTopK over its [batch, candidate_count] values and launchRemapIndices
+ * (:132-146), as one kernel that gathers every candidate row, scores it exactly against the
+ * fp32 query and writes the final top-k with corpus ids.
+ *
+ *   store           : the rescore corpus (F32, F16, I8 with `scale`, or I8_ROW with
+ *                     `row_scales`); BINARY returns ZCGVS_ERR_INVALID_ARG, as in the reference.
+ *   candidates      : [batch, candidate_count] corpus ids (e.g. a coarse zcgvs_scan_topk
+ *                     result); ids outside [0, doc_count), such as -1 padding, are skipped.
+ *   candidate_count : 1..8192.
+ *   k               : 1..min(ZCGVS_MAX_K, candidate_count).
+ *   out_indices / out_scores : [batch, k], (score desc, id asc), padded with (-1, -FLT_MAX)
+ *                     when fewer than k candidates are valid.
+ * --------------------------------------------------------------------------------------- */
+int zcgvs_rescore_topk(const void* store, int dtype, float scale, const float* row_scales,
+                       int64_t doc_count, int dim, const float* queries, int batch,
+                       const int* candidates, int candidate_count, int metric, int k,
+                       int* out_indices, float* out_scores, void* stream);
+
+/* Score matrix of a candidate set: the reference launchGatherRescore contract
+ * (include/zcgvs/cuda/rescore.cuh:20-32). values[q, j] = exact score of candidates[q, j], or
+ * -FLT_MAX when that id is outside [0, doc_count). */
+int zcgvs_gather_rescore(const void* store, int dtype, float scale, const float* row_scales,
+                         int64_t doc_count, int dim, const float* queries, int batch,
+                         const int* candidates, int candidate_count, int metric, float* values,
+                         void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -305,3 +305,76 @@ void orc_scan_topk(int dtype, const void* corpus, float scale, const float* row_
     }
     free(s);
 }
+
+/* ---------------------------------------------------------------------------------------
+ * Rescore stage: the gather-rescore of src/cuda/rescore.cu:20-63 (every candidate id scored
+ * against the rescore store with the fp32 query, as scores_one does for a whole corpus), the
+ * second launchTopK over the [batch, m] rescored values and the id remap of :65-79, as
+ * Searcher::recordPipeline chains them (src/search/searcher.cpp:266-279). Candidates outside
+ * [0, n) are dropped; the top-k of the rest is taken under (score desc, id asc) on the global
+ * ids, and short lists are padded with (-1, -FLT_MAX). BINARY stores are rejected by the
+ * reference (src/cuda/rescore.cu:102-105); this returns -1 for them.
+ * --------------------------------------------------------------------------------------- */
+static float score_row(int dtype, const void* store, float scale, const float* row_scales, int dim,
+                       int64_t row, const float* query, const int8_t* qq, float qs, int metric) {
+    const int l2 = (metric == ORC_METRIC_L2);
+    if (dtype == ORC_DTYPE_I8_ROW) {
+        const int8_t* x = (const int8_t*)store + (size_t)row * (size_t)dim;
+        int32_t dot = 0;
+        for (int j = 0; j < dim; ++j) dot += (int32_t)x[j] * (int32_t)qq[j];
+        const float a = (float)dot * qs;
+        return a * row_scales[row];
+    }
+    float acc = 0.0f;
+    for (int j = 0; j < dim; ++j) {
+        float x;
+        const size_t at = (size_t)row * (size_t)dim + (size_t)j;
+        if (dtype == ORC_DTYPE_F16) {
+            x = orc_f16_to_f32(((const uint16_t*)store)[at]);
+        } else if (dtype == ORC_DTYPE_I8) {
+            x = (float)((const int8_t*)store)[at] * scale;
+        } else {
+            x = ((const float*)store)[at];
+        }
+        if (l2) {
+            const float d = query[j] - x;
+            acc += d * d;
+        } else {
+            acc += x * query[j];
+        }
+    }
+    return l2 ? -acc : acc;
+}
+
+int orc_rescore_topk(int dtype, const void* store, float scale, const float* row_scales, int64_t n,
+                     int dim, const float* queries, int batch, const int32_t* candidates, int m,
+                     int metric, int k, int32_t* out_idx, float* out_scores) {
+    if (dtype == ORC_DTYPE_BINARY) return -1;
+    uint64_t* keys = (uint64_t*)malloc((size_t)(m > 0 ? m : 1) * sizeof(uint64_t));
+    int8_t* qq = (int8_t*)malloc((size_t)(dim > 0 ? dim : 1));
+    for (int q = 0; q < batch; ++q) {
+        const float* query = queries + (size_t)q * (size_t)dim;
+        float qs = 0.0f;
+        if (dtype == ORC_DTYPE_I8_ROW) orc_quantize_rows_i8(query, 1, dim, qq, &qs);
+        int count = 0;
+        for (int j = 0; j < m; ++j) {
+            const int32_t id = candidates[(size_t)q * (size_t)m + (size_t)j];
+            if (id < 0 || (int64_t)id >= n) continue;
+            const float s = score_row(dtype, store, scale, row_scales, dim, id, query, qq, qs, metric);
+            keys[count++] = make_key(s, (uint32_t)id);
+        }
+        qsort(keys, (size_t)count, sizeof(uint64_t), cmp_desc);
+        for (int j = 0; j < k; ++j) {
+            if (j < count) {
+                out_idx[(size_t)q * k + j] = (int32_t)(~(uint32_t)keys[j]);
+                out_scores[(size_t)q * k + j] = from_orderable((uint32_t)(keys[j] >> 32));
+            } else {
+                out_idx[(size_t)q * k + j] = -1;
+                out_scores[(size_t)q * k + j] = -FLT_MAX;
+            }
+        }
+    }
+    free(qq);
+    free(keys);
+    return 0;
+}

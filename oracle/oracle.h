@@ -33,6 +33,12 @@ void orc_scan_topk(int dtype, const void* corpus, float scale, const float* row_
                    int dim, const float* queries, int batch, const uint8_t* mask, int metric,
                    int k, int id_base, int32_t* out_idx, float* out_scores);
 
+/* Rescore stage (gather + exact score + second top-k + id remap) over candidate ids
+ * [batch, m]; ids outside [0, n) are dropped. Returns -1 for BINARY stores. */
+int orc_rescore_topk(int dtype, const void* store, float scale, const float* row_scales, int64_t n,
+                     int dim, const float* queries, int batch, const int32_t* candidates, int m,
+                     int metric, int k, int32_t* out_idx, float* out_scores);
+
 /* Seeded inputs identical to the reference harnesses' randomMatrix
  * (tests/cpp/test_pipeline.cu:20-31): std::mt19937(seed), std::normal_distribution<float>(0,1),
  * then each row L2-normalised in fp32 (tests/cpp/cpu_reference.hpp:36-49). */

@@ -54,6 +54,8 @@ def lib():
         _lib.orc_scores.argtypes = [i32, _P, f32, _P, i64, i32, _P, i32, _P, i32, _P]
         _lib.orc_topk.argtypes = [_P, i64, i32, i32, i32, _P, _P]
         _lib.orc_scan_topk.argtypes = [i32, _P, f32, _P, i64, i32, _P, i32, _P, i32, i32, i32, _P, _P]
+        _lib.orc_rescore_topk.restype = i32
+        _lib.orc_rescore_topk.argtypes = [i32, _P, f32, _P, i64, i32, _P, i32, _P, i32, i32, i32, _P, _P]
         _lib.orc_gen_normal_rows.argtypes = [i64, i32, u32, i32, _P]
         _lib.orc_gen_uniform.argtypes = [ctypes.c_size_t, u32, f32, f32, _P]
     return _lib
@@ -190,4 +192,22 @@ def scan_topk(storage, dtype, dim, queries, k, scale=1.0, row_scales=None, mask=
     m = None if mask is None else np.ascontiguousarray(mask, dtype=np.uint8)
     lib().orc_scan_topk(dtype, _ptr(storage), scale, _ptr(rs), storage.shape[0], dim,
                         _ptr(queries), batch, _ptr(m), metric, k, id_base, _ptr(idx), _ptr(val))
+    return idx, val
+
+
+def rescore_topk(storage, dtype, dim, queries, candidates, k, scale=1.0, row_scales=None,
+                 metric=METRIC_DOT):
+    """Gather-rescore + second top-k + id remap over candidate ids [batch, m]."""
+    storage = np.ascontiguousarray(storage)
+    queries = np.ascontiguousarray(queries, dtype=np.float32).reshape(-1, dim)
+    batch = queries.shape[0]
+    cand = np.ascontiguousarray(candidates, dtype=np.int32).reshape(batch, -1)
+    idx = np.empty((batch, k), dtype=np.int32)
+    val = np.empty((batch, k), dtype=np.float32)
+    rs = None if row_scales is None else np.ascontiguousarray(row_scales, dtype=np.float32)
+    rc = lib().orc_rescore_topk(dtype, _ptr(storage), scale, _ptr(rs), storage.shape[0], dim,
+                                _ptr(queries), batch, _ptr(cand), cand.shape[1], metric, k,
+                                _ptr(idx), _ptr(val))
+    if rc != 0:
+        raise ValueError("rescore store must hold float32, float16 or int8 rows")
     return idx, val

@@ -57,3 +57,23 @@ def test_per_row_int8_needs_scales(zc):
     status = zc.lib().zcgvs_scan_topk(fake, zc.DTYPE_I8_ROW, 1.0, None, 100, 8, fake, 1, None, zc.METRIC_DOT, 10, 0,
                                       fake, fake, fake, 1 << 20, None)
     assert status == zc.ERR_INVALID_ARG
+
+
+@pytest.mark.parametrize("dtype,m,k,expect", [
+    (3, 100, 10, "float32, float16 or int8"),       # binary rescore store (src/cuda/rescore.cu:102-105)
+    (0, 100, 0, "k must be in"),
+    (0, 100, 1025, "k must be in"),
+    (0, 10, 11, "k exceeds candidate_count"),
+    (0, 8193, 10, "candidate_count exceeds"),
+])
+def test_rescore_rejects_bad_arguments(zc, dtype, m, k, expect):
+    fake = ctypes.c_void_p(16)
+    status = zc.lib().zcgvs_rescore_topk(fake, dtype, 1.0, None, 1000, 8, fake, 1, fake, m, zc.METRIC_DOT, k,
+                                         fake, fake, None)
+    assert status == zc.ERR_INVALID_ARG
+    assert expect in zc.lib().zcgvs_last_error_message().decode()
+
+
+def test_rescore_zero_sized_is_a_noop(zc):
+    assert zc.lib().zcgvs_rescore_topk(None, 0, 1.0, None, 10, 8, None, 1, None, 0, 0, 5, None, None, None) == zc.OK
+    assert zc.lib().zcgvs_gather_rescore(None, 0, 1.0, None, 10, 8, None, 0, None, 4, 0, None, None) == zc.OK

@@ -36,6 +36,10 @@ SIGNATURES = {
     "zcgvs_scan_topk_noalloc": (_i32, [_P, _i32, _f32, _P, _i64, _i32, _P, _i32, _P, _i32, _i32,
                                        _i32, _P, _P, _P]),
     "zcgvs_similarity": (_i32, [_P, _i32, _f32, _P, _i64, _i32, _P, _i32, _P, _i32, _P, _P]),
+    "zcgvs_rescore_topk": (_i32, [_P, _i32, _f32, _P, _i64, _i32, _P, _i32, _P, _i32, _i32, _i32,
+                                  _P, _P, _P]),
+    "zcgvs_gather_rescore": (_i32, [_P, _i32, _f32, _P, _i64, _i32, _P, _i32, _P, _i32, _i32, _P,
+                                    _P]),
 }
 
 
@@ -172,4 +176,37 @@ def similarity(corpus, dtype: int, dim: int, queries, *, scale: float = 1.0, row
         out = torch.empty((batch, doc_count), dtype=torch.float32, device=queries.device)
     check(lib().zcgvs_similarity(_ptr(corpus), dtype, scale, _ptr(row_scales), doc_count, dim,
                                  _ptr(queries), batch, _ptr(mask), metric, _ptr(out), _stream(stream)))
+    return out
+
+
+def rescore_topk(store, dtype: int, dim: int, queries, candidates, k: int, *, scale: float = 1.0,
+                 row_scales=None, metric: int = METRIC_DOT, out=None, stream=None):
+    """Fused gather + exact rescore + top-k over candidate ids [B, M]. Returns (ids, scores)."""
+    import torch
+
+    queries = queries.reshape(-1, dim)
+    batch = queries.shape[0]
+    candidates = candidates.reshape(batch, -1)
+    if out is None:
+        out = (torch.empty((batch, k), dtype=torch.int32, device=queries.device),
+               torch.empty((batch, k), dtype=torch.float32, device=queries.device))
+    check(lib().zcgvs_rescore_topk(_ptr(store), dtype, scale, _ptr(row_scales), store.shape[0], dim,
+                                   _ptr(queries), batch, _ptr(candidates), candidates.shape[1], metric,
+                                   k, _ptr(out[0]), _ptr(out[1]), _stream(stream)))
+    return out
+
+
+def gather_rescore(store, dtype: int, dim: int, queries, candidates, *, scale: float = 1.0,
+                   row_scales=None, metric: int = METRIC_DOT, out=None, stream=None):
+    """Exact scores [B, M] of candidate ids [B, M] (the reference launchGatherRescore)."""
+    import torch
+
+    queries = queries.reshape(-1, dim)
+    batch = queries.shape[0]
+    candidates = candidates.reshape(batch, -1)
+    if out is None:
+        out = torch.empty(candidates.shape, dtype=torch.float32, device=queries.device)
+    check(lib().zcgvs_gather_rescore(_ptr(store), dtype, scale, _ptr(row_scales), store.shape[0], dim,
+                                     _ptr(queries), batch, _ptr(candidates), candidates.shape[1],
+                                     metric, _ptr(out), _stream(stream)))
     return out
