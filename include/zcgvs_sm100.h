@@ -172,6 +172,52 @@ int zcgvs_gather_rescore(const void* store, int dtype, float scale, const float*
                          const int* candidates, int candidate_count, int metric, float* values,
                          void* stream);
 
+/* ---------------------------------------------------------------------------------------
+ * Hybrid lexical + dense search. Replaces the hybrid stages of Searcher::recordPipeline
+ * (src/search/searcher.cpp:236-263: per query launchBm25, launchMaxPositive and
+ * launchFuseScores over [batch, N] score matrices, then launchTopK) with two kernels: a BM25
+ * kernel that writes each query's lexical scores and partial maxima to the workspace, and the
+ * fused scan, which blends score = w * dense + ((1 - w) * lex) * (1 / max(lex)) (0 when the max
+ * is not positive; src/cuda/lexical.cu:66-72) before its top-k.
+ *
+ *   offsets / posting_docs / posting_weights : the CSR index of the reference LexicalIndex
+ *                     (include/zcgvs/data/lexical_index.hpp:14-46): offsets [vocab_size + 1]
+ *                     int64, per-term posting documents int32 and BM25 weights fp32. Posting
+ *                     lists must be sorted by document id within each term (the reference
+ *                     builder writes them so, python/zcgvs_tools/build_lexical.py:143-162).
+ *   query_terms     : [batch, term_stride] term ids; ids outside [0, vocab_size), such as the
+ *                     -1 padding, are ignored. Duplicate ids count once per occurrence, as in
+ *                     the reference (the engine de-duplicates before searching).
+ *   dense_weight    : w above; the dense score is the corpus scan's (masked documents
+ *                     -FLT_MAX before blending, as in the reference).
+ * Lexical scores are sums in (term slot, posting) order, identical to the sequential CPU sum;
+ * term_stride <= 0 or query_terms == NULL runs the dense search alone. The remaining arguments
+ * and the result are those of zcgvs_scan_topk (id_base is 0).
+ * --------------------------------------------------------------------------------------- */
+size_t zcgvs_hybrid_topk_workspace_bytes(int dtype, int64_t doc_count, int dim, int batch, int k);
+
+int zcgvs_hybrid_topk(const void* corpus, int dtype, float scale, const float* row_scales,
+                      int64_t doc_count, int dim, const float* queries, int batch,
+                      const uint8_t* mask, int metric, const int64_t* offsets,
+                      const int* posting_docs, const float* posting_weights, int vocab_size,
+                      const int* query_terms, int term_stride, float dense_weight, int k,
+                      int* out_indices, float* out_scores, void* workspace,
+                      size_t workspace_bytes, void* stream);
+
+/* The reference lexical launchers (include/zcgvs/cuda/lexical.cuh:20-40), same contracts:
+ *   zcgvs_bm25         : scores[d] += weights of d's postings under the valid terms of one
+ *                        query, summed in (slot, posting) order (deterministic; sorted posting
+ *                        lists required). Term ids are trusted to be < the index's vocabulary,
+ *                        as in the reference.
+ *   zcgvs_max_positive : *out_max = max(*out_max, max(0, max_i values[i])) (zero it first).
+ *   zcgvs_fuse_scores  : dense[i] = w * dense[i] + ((1 - w) * lexical[i]) * inv, inv =
+ *                        1 / *lexical_max when positive, else 0. */
+int zcgvs_bm25(const int64_t* offsets, const int* posting_docs, const float* posting_weights,
+               const int* query_terms, int term_count, int doc_count, float* scores, void* stream);
+int zcgvs_max_positive(const float* values, int count, float* out_max, void* stream);
+int zcgvs_fuse_scores(float* dense, const float* lexical, const float* lexical_max, float weight,
+                      int count, void* stream);
+
 #ifdef __cplusplus
 }  /* extern "C" */
 #endif

@@ -378,3 +378,66 @@ int orc_rescore_topk(int dtype, const void* store, float scale, const float* row
     free(keys);
     return 0;
 }
+
+/* ---------------------------------------------------------------------------------------
+ * Lexical scoring, the CPU reference of tests/cpp/test_lexical.cu:71-89:
+ *   orc_bm25          : scores[doc] += weight for every posting of every valid term slot, in
+ *                       slot order then posting order (sequential fp32 adds); postings whose
+ *                       document is outside [0, n) are skipped (src/cuda/lexical.cu:35-39),
+ *                       term ids outside [0, vocab) are ignored.
+ *   orc_max_positive  : max(0, max_i values[i]).
+ *   orc_fuse          : dense[i] = w * dense[i] + ((1 - w) * lex[i]) * inv, inv = 1 / peak when
+ *                       peak > 0 else 0, each operation rounded on its own.
+ *   orc_hybrid_topk   : per query, scores_one (dense, mask -> -FLT_MAX), orc_bm25 from zero,
+ *                       orc_max_positive, orc_fuse, then orc_topk: the hybrid chain of
+ *                       src/search/searcher.cpp:236-263 followed by its top-k.
+ * --------------------------------------------------------------------------------------- */
+void orc_bm25(const int64_t* offsets, const int32_t* docs, const float* weights, int vocab, const int32_t* terms,
+              int term_count, int64_t n, float* scores) {
+    for (int t = 0; t < term_count; ++t) {
+        const int32_t term = terms[t];
+        if (term < 0 || term >= vocab) continue;
+        for (int64_t p = offsets[term]; p < offsets[term + 1]; ++p) {
+            const int32_t doc = docs[p];
+            if (doc < 0 || (int64_t)doc >= n) continue;
+            scores[doc] += weights[p];
+        }
+    }
+}
+
+float orc_max_positive(const float* values, int64_t count) {
+    float best = 0.0f;
+    for (int64_t i = 0; i < count; ++i) {
+        if (values[i] > best) best = values[i];
+    }
+    return best;
+}
+
+void orc_fuse(float* dense, const float* lex, float peak, float w, int64_t count) {
+    const float inv = peak > 0.0f ? 1.0f / peak : 0.0f;
+    for (int64_t i = 0; i < count; ++i) {
+        const float a = w * dense[i];
+        const float b = (1.0f - w) * lex[i];
+        const float c = b * inv;
+        dense[i] = a + c;
+    }
+}
+
+void orc_hybrid_topk(int dtype, const void* corpus, float scale, const float* row_scales, int64_t n, int dim,
+                     const float* queries, int batch, const uint8_t* mask, int metric, const int64_t* offsets,
+                     const int32_t* docs, const float* weights, int vocab, const int32_t* terms, int stride,
+                     float w, int k, int32_t* out_idx, float* out_scores) {
+    float* dense = (float*)malloc((size_t)n * sizeof(float));
+    float* lex = (float*)malloc((size_t)n * sizeof(float));
+    for (int q = 0; q < batch; ++q) {
+        scores_one(dtype, corpus, scale, row_scales, n, dim, queries + (size_t)q * (size_t)dim, mask, metric, dense);
+        if (stride > 0 && terms != NULL) {
+            memset(lex, 0, (size_t)n * sizeof(float));
+            orc_bm25(offsets, docs, weights, vocab, terms + (size_t)q * (size_t)stride, stride, n, lex);
+            orc_fuse(dense, lex, orc_max_positive(lex, n), w, n);
+        }
+        orc_topk(dense, n, 1, k, 0, out_idx + (size_t)q * k, out_scores + (size_t)q * k);
+    }
+    free(lex);
+    free(dense);
+}

@@ -39,6 +39,21 @@ int orc_rescore_topk(int dtype, const void* store, float scale, const float* row
                      int dim, const float* queries, int batch, const int32_t* candidates, int m,
                      int metric, int k, int32_t* out_idx, float* out_scores);
 
+/* Lexical scoring (tests/cpp/test_lexical.cu:71-89) and the hybrid search chain. */
+void orc_bm25(const int64_t* offsets, const int32_t* docs, const float* weights, int vocab, const int32_t* terms,
+              int term_count, int64_t n, float* scores);
+float orc_max_positive(const float* values, int64_t count);
+void orc_fuse(float* dense, const float* lex, float peak, float w, int64_t count);
+void orc_hybrid_topk(int dtype, const void* corpus, float scale, const float* row_scales, int64_t n, int dim,
+                     const float* queries, int batch, const uint8_t* mask, int metric, const int64_t* offsets,
+                     const int32_t* docs, const float* weights, int vocab, const int32_t* terms, int stride,
+                     float w, int k, int32_t* out_idx, float* out_scores);
+
+/* The synthetic index, query and dense scores of tests/cpp/test_lexical.cu:31-67, bit for bit. */
+void orc_gen_lexical_test(uint32_t index_seed, int doc_count, int vocab, int max_postings, float wlo,
+                          float whi, uint32_t query_seed, int term_count, int64_t* offsets, int32_t* docs,
+                          float* weights, int64_t* nnz, int32_t* terms, float* dense);
+
 /* Seeded inputs identical to the reference harnesses' randomMatrix
  * (tests/cpp/test_pipeline.cu:20-31): std::mt19937(seed), std::normal_distribution<float>(0,1),
  * then each row L2-normalised in fp32 (tests/cpp/cpu_reference.hpp:36-49). */

@@ -56,6 +56,13 @@ def lib():
         _lib.orc_scan_topk.argtypes = [i32, _P, f32, _P, i64, i32, _P, i32, _P, i32, i32, i32, _P, _P]
         _lib.orc_rescore_topk.restype = i32
         _lib.orc_rescore_topk.argtypes = [i32, _P, f32, _P, i64, i32, _P, i32, _P, i32, i32, i32, _P, _P]
+        _lib.orc_bm25.argtypes = [_P, _P, _P, i32, _P, i32, i64, _P]
+        _lib.orc_max_positive.restype = f32
+        _lib.orc_max_positive.argtypes = [_P, i64]
+        _lib.orc_fuse.argtypes = [_P, _P, f32, f32, i64]
+        _lib.orc_hybrid_topk.argtypes = [i32, _P, f32, _P, i64, i32, _P, i32, _P, i32, _P, _P, _P, i32, _P, i32,
+                                         f32, i32, _P, _P]
+        _lib.orc_gen_lexical_test.argtypes = [u32, i32, i32, i32, f32, f32, u32, i32, _P, _P, _P, _P, _P, _P]
         _lib.orc_gen_normal_rows.argtypes = [i64, i32, u32, i32, _P]
         _lib.orc_gen_uniform.argtypes = [ctypes.c_size_t, u32, f32, f32, _P]
     return _lib
@@ -210,4 +217,62 @@ def rescore_topk(storage, dtype, dim, queries, candidates, k, scale=1.0, row_sca
                                 _ptr(idx), _ptr(val))
     if rc != 0:
         raise ValueError("rescore store must hold float32, float16 or int8 rows")
+    return idx, val
+
+
+# ----------------------------------------------------------------------------------------
+# Lexical scoring
+# ----------------------------------------------------------------------------------------
+def lexical_test_case(index_seed=41, doc_count=20000, vocab=3000, max_postings=400, wlo=0.01, whi=8.0,
+                      query_seed=42, term_count=24):
+    """The index, query terms and dense scores of tests/cpp/test_lexical.cu:31-67."""
+    nnz = ctypes.c_int64(0)
+    lib().orc_gen_lexical_test(index_seed, doc_count, vocab, max_postings, wlo, whi, query_seed, term_count,
+                               None, None, None, ctypes.byref(nnz), None, None)
+    offsets = np.empty(vocab + 1, dtype=np.int64)
+    docs = np.empty(nnz.value, dtype=np.int32)
+    weights = np.empty(nnz.value, dtype=np.float32)
+    terms = np.empty(term_count, dtype=np.int32)
+    dense = np.empty(doc_count, dtype=np.float32)
+    lib().orc_gen_lexical_test(index_seed, doc_count, vocab, max_postings, wlo, whi, query_seed, term_count,
+                               _ptr(offsets), _ptr(docs), _ptr(weights), ctypes.byref(nnz), _ptr(terms),
+                               _ptr(dense))
+    return offsets, docs, weights, terms, dense
+
+
+def bm25(offsets, docs, weights, vocab, terms, n, init=None):
+    out = np.zeros(n, dtype=np.float32) if init is None else np.array(init, dtype=np.float32)
+    terms = np.ascontiguousarray(terms, dtype=np.int32)
+    lib().orc_bm25(_ptr(np.ascontiguousarray(offsets, dtype=np.int64)), _ptr(np.ascontiguousarray(docs, dtype=np.int32)),
+                   _ptr(np.ascontiguousarray(weights, dtype=np.float32)), vocab, _ptr(terms), terms.size, n, _ptr(out))
+    return out
+
+
+def max_positive(values) -> float:
+    v = np.ascontiguousarray(values, dtype=np.float32)
+    return float(lib().orc_max_positive(_ptr(v), v.size))
+
+
+def fuse(dense, lex, peak, w):
+    out = np.array(dense, dtype=np.float32)
+    lex = np.ascontiguousarray(lex, dtype=np.float32)
+    lib().orc_fuse(_ptr(out), _ptr(lex), peak, w, out.size)
+    return out
+
+
+def hybrid_topk(storage, dtype, dim, queries, k, offsets, docs, weights, vocab, terms, dense_weight, scale=1.0,
+                row_scales=None, mask=None, metric=METRIC_DOT):
+    storage = np.ascontiguousarray(storage)
+    queries = np.ascontiguousarray(queries, dtype=np.float32).reshape(-1, dim)
+    batch = queries.shape[0]
+    terms = np.ascontiguousarray(terms, dtype=np.int32).reshape(batch, -1)
+    idx = np.empty((batch, k), dtype=np.int32)
+    val = np.empty((batch, k), dtype=np.float32)
+    rs = None if row_scales is None else np.ascontiguousarray(row_scales, dtype=np.float32)
+    m = None if mask is None else np.ascontiguousarray(mask, dtype=np.uint8)
+    lib().orc_hybrid_topk(dtype, _ptr(storage), scale, _ptr(rs), storage.shape[0], dim, _ptr(queries), batch, _ptr(m),
+                          metric, _ptr(np.ascontiguousarray(offsets, dtype=np.int64)),
+                          _ptr(np.ascontiguousarray(docs, dtype=np.int32)),
+                          _ptr(np.ascontiguousarray(weights, dtype=np.float32)), vocab, _ptr(terms), terms.shape[1],
+                          dense_weight, k, _ptr(idx), _ptr(val))
     return idx, val

@@ -1,0 +1,163 @@
+"""GPU tier: BM25 lexical scoring and the hybrid search against the CPU oracle.
+
+The reference accumulates BM25 with float atomics and checks its GPU with a tolerance
+(tests/cpp/test_lexical.cu:118-126). This build sums in (term slot, posting) order, so its
+lexical scores, maxima and fused scores must equal the oracle's sequential loop bit for bit; the
+hybrid top-k is bit-exact wherever the dense part is (per-row int8, or dense_weight 0) and within
+1e-4 otherwise. The first cases run the reference test's own index and query
+(test_lexical.cu:31-67, regenerated from its seeds).
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+
+from conftest import assert_topk_parity
+
+pytestmark = pytest.mark.gpu
+
+FLT_MAX = np.finfo(np.float32).max
+
+
+def dev(a, dtype=None):
+    import torch
+
+    return torch.as_tensor(np.ascontiguousarray(a), dtype=dtype).cuda()
+
+
+@pytest.fixture(scope="module")
+def ref_case(orc):
+    import lexical_index as li
+
+    offsets, docs, weights, terms, dense = orc.lexical_test_case()
+    assert not li.postings_sorted(offsets, docs)  # the reference test's index is unsorted
+    s_off, s_docs, s_w = li.sort_postings(offsets, docs, weights)
+    return offsets, docs, weights, terms, dense, s_off, s_docs, s_w
+
+
+def test_bm25_reference_case_bit_exact(zc, orc, ref_case):
+    import torch
+
+    offsets, docs, weights, terms, dense, s_off, s_docs, s_w = ref_case
+    n = dense.size
+    expected = orc.bm25(offsets, docs, weights, 3000, terms, n)  # unsorted index, reference loop order
+    index = zc.LexicalIndex(s_off, s_docs, s_w)
+    scores = torch.zeros(n, dtype=torch.float32, device="cuda")
+    zc.bm25(index, dev(terms), scores)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(scores.cpu().numpy(), expected)
+
+
+def test_bm25_accumulates_onto_existing_scores(zc, orc, ref_case):
+    import torch
+
+    offsets, docs, weights, terms, dense, s_off, s_docs, s_w = ref_case
+    n = dense.size
+    expected = orc.bm25(offsets, docs, weights, 3000, terms, n, init=dense)
+    scores = dev(dense)
+    zc.bm25(zc.LexicalIndex(s_off, s_docs, s_w), dev(terms), scores)
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(scores.cpu().numpy(), expected)
+
+
+def test_max_and_fuse_reference_case(zc, orc, ref_case):
+    import torch
+
+    offsets, docs, weights, terms, dense, *_ = ref_case
+    n = dense.size
+    lex = orc.bm25(offsets, docs, weights, 3000, terms, n)
+    peak = orc.max_positive(lex)
+    d_max = torch.zeros(1, dtype=torch.float32, device="cuda")
+    zc.max_positive(dev(lex), d_max)
+    d_dense = dev(dense)
+    zc.fuse_scores(d_dense, dev(lex), d_max, 0.6)
+    torch.cuda.synchronize()
+    assert float(d_max.item()) == peak
+    np.testing.assert_array_equal(d_dense.cpu().numpy(), orc.fuse(dense, lex, peak, 0.6))
+
+
+def test_max_positive_of_negative_values_is_zero(zc):
+    import torch
+
+    d_max = torch.zeros(1, dtype=torch.float32, device="cuda")
+    zc.max_positive(torch.full((1000,), -3.0, device="cuda"), d_max)
+    assert float(d_max.item()) == 0.0
+
+
+def zipf_case(orc, n, dim, vocab, batch, seed):
+    import lexical_index as li
+
+    offsets, docs, weights = li.synthetic_corpus(n, vocab, 40.0, 1.1, seed, k1=0.9, b=0.4)
+    terms = li.synthetic_queries(batch, vocab, 1.1, seed + 1)
+    corpus = orc.normal_rows(n, dim, 500 + seed)
+    queries = orc.normal_rows(batch, dim, 600 + seed)
+    return offsets.numpy(), docs.numpy(), weights.numpy(), terms, corpus, queries
+
+
+@pytest.mark.parametrize("name,dtype", [("f16", 1), ("f32", 0), ("i8row", 4)])
+@pytest.mark.parametrize("w", [0.0, 0.5, 1.0])
+@pytest.mark.parametrize("batch", [1, 3])
+def test_hybrid_topk(zc, orc, name, dtype, w, batch):
+    import torch
+
+    n, dim, vocab, k = 30000, 384, 3000, 10
+    offsets, docs, weights, terms, corpus, queries = zipf_case(orc, n, dim, vocab, batch, 7 + batch)
+    storage, scale, row_scales = orc.encode(corpus, dtype)
+    st = dev(storage.view(np.int16) if storage.dtype == np.uint16 else storage)
+    idx, val = zc.hybrid_topk(st, dtype, dim, dev(queries), k, zc.LexicalIndex(offsets, docs, weights),
+                              dev(terms), w, scale=scale,
+                              row_scales=None if row_scales is None else dev(row_scales), metric=0)
+    torch.cuda.synchronize()
+    ref_idx, ref_val = orc.hybrid_topk(storage, dtype, dim, queries, k, offsets, docs, weights, vocab, terms, w,
+                                       scale=scale, row_scales=row_scales, metric=0)
+    if name == "i8row" or w == 0.0:
+        np.testing.assert_array_equal(idx.cpu().numpy(), ref_idx)
+        np.testing.assert_array_equal(val.cpu().numpy(), ref_val)
+    else:
+        # Full fused score rows for the near-tie check.
+        full = np.empty((batch, n), dtype=np.float32)
+        dense = orc.scores(storage, dtype, dim, queries, scale=scale, row_scales=row_scales, metric=0)
+        for q in range(batch):
+            lex = orc.bm25(offsets, docs, weights, vocab, terms[q], n)
+            full[q] = orc.fuse(dense[q], lex, orc.max_positive(lex), w)
+        assert_topk_parity(idx.cpu().numpy(), val.cpu().numpy(), full, k, exact=False)
+
+
+def test_hybrid_masked_and_edge_terms(zc, orc):
+    """Masked documents keep w * -FLT_MAX + lexical (the reference fuses after masking);
+    padding, out-of-vocabulary and repeated term ids; a query with no valid terms."""
+    import torch
+
+    n, dim, vocab, k, batch = 20000, 256, 2000, 50, 4
+    offsets, docs, weights, terms, corpus, queries = zipf_case(orc, n, dim, vocab, batch, 21)
+    terms[1, :] = -1                   # no lexical evidence: lex = 0, inverse 0
+    terms[2, 0] = vocab + 5            # out of vocabulary: ignored
+    terms[3, 1] = terms[3, 0]          # repeated term counts twice
+    mask = np.ones(n, dtype=np.uint8)
+    mask[::3] = 0
+    storage, _, row_scales = orc.encode(corpus, 4)
+    for w in (0.0, 0.3):
+        idx, val = zc.hybrid_topk(dev(storage), 4, dim, dev(queries), k, zc.LexicalIndex(offsets, docs, weights),
+                                  dev(terms), w, row_scales=dev(row_scales), mask=dev(mask))
+        torch.cuda.synchronize()
+        ref_idx, ref_val = orc.hybrid_topk(storage, 4, dim, queries, k, offsets, docs, weights, vocab, terms, w,
+                                           row_scales=row_scales, mask=mask)
+        np.testing.assert_array_equal(idx.cpu().numpy(), ref_idx)
+        np.testing.assert_array_equal(val.cpu().numpy(), ref_val)
+
+
+def test_hybrid_without_terms_is_dense_search(zc, orc):
+    import torch
+
+    n, dim = 5000, 128
+    corpus = orc.normal_rows(n, dim, 3)
+    queries = orc.normal_rows(2, dim, 4)
+    storage, _, row_scales = orc.encode(corpus, 4)
+    empty = zc.LexicalIndex(np.zeros(2, dtype=np.int64), np.zeros(0, dtype=np.int32), np.zeros(0, dtype=np.float32))
+    idx, val = zc.hybrid_topk(dev(storage), 4, dim, dev(queries), 20, empty,
+                              torch.empty((2, 0), dtype=torch.int32, device="cuda"), 0.5, row_scales=dev(row_scales))
+    torch.cuda.synchronize()
+    ref_idx, ref_val = orc.scan_topk(storage, 4, dim, queries, 20, row_scales=row_scales)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ref_idx)
+    np.testing.assert_array_equal(val.cpu().numpy(), ref_val)

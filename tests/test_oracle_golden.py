@@ -121,3 +121,67 @@ def test_topk_tie_order(orc):
     assert idx[0].tolist() == [1, 2, 5, 6, 0]
     idx, val = orc.topk(s, 7)
     assert idx[0].tolist()[-2:] == [3, 4]  # -0.0 ties +0.0, lower id first
+
+
+def test_oracle_bm25_matches_sequential_float32_loop(orc):
+    """orc_bm25 against an independent float32 restatement of tests/cpp/test_lexical.cu:71-80
+    on the reference test's own index (regenerated from its seeds)."""
+    offsets, docs, weights, terms, dense = orc.lexical_test_case()
+    assert offsets[-1] == docs.size and terms[-1] == -1 and dense.size == 20000
+    expected = [np.float32(0.0)] * 20000
+    for term in terms:
+        if term < 0:
+            continue
+        for p in range(offsets[term], offsets[term + 1]):
+            expected[docs[p]] = np.float32(expected[docs[p]] + weights[p])
+    np.testing.assert_array_equal(orc.bm25(offsets, docs, weights, 3000, terms, 20000),
+                                  np.array(expected, dtype=np.float32))
+
+
+def test_oracle_fuse_order(orc):
+    dense = np.array([0.5, -1.0, 0.25], dtype=np.float32)
+    lex = np.array([3.0, 0.0, 1.5], dtype=np.float32)
+    w = np.float32(0.6)
+    inv = np.float32(1.0) / np.float32(3.0)
+    expected = [np.float32(np.float32(w * d) + np.float32(np.float32(np.float32(np.float32(1.0) - w) * l) * inv))
+                for d, l in zip(dense, lex)]
+    np.testing.assert_array_equal(orc.fuse(dense, lex, 3.0, 0.6), np.array(expected, dtype=np.float32))
+    assert orc.max_positive(np.array([-2.0, -1.0], dtype=np.float32)) == 0.0
+
+
+def test_sort_postings_keeps_per_document_order():
+    import lexical_index as li
+
+    offsets = np.array([0, 4, 4, 7], dtype=np.int64)
+    docs = np.array([9, 2, 9, 1, 5, 5, 0], dtype=np.int32)
+    weights = np.arange(7, dtype=np.float32)
+    assert not li.postings_sorted(offsets, docs)
+    o, d, w = li.sort_postings(offsets, docs, weights)
+    np.testing.assert_array_equal(d, [1, 2, 9, 9, 0, 5, 5])
+    np.testing.assert_array_equal(w, [3, 1, 0, 2, 6, 4, 5])
+    assert li.postings_sorted(o, d)
+
+
+def test_bm25_weights_match_builder_formula():
+    import math
+
+    import torch
+
+    import lexical_index as li
+
+    # Two documents, three terms: doc 0 = [0, 0, 1], doc 1 = [1, 2].
+    doc_ids = torch.tensor([0, 0, 1, 1])
+    term_ids = torch.tensor([0, 1, 1, 2])
+    tf = torch.tensor([2, 1, 1, 1])
+    lengths = torch.tensor([3, 2])
+    offsets, docs, weights = li.build_csr(doc_ids, term_ids, tf, lengths, 3, k1=0.9, b=0.4)
+    avgdl = 2.5
+    expected = []
+    for d, t, f in [(0, 0, 2), (0, 1, 1), (1, 1, 1), (1, 2, 1)]:
+        df = {0: 1, 1: 2, 2: 1}[t]
+        idf = math.log(1.0 + (2 - df + 0.5) / (df + 0.5))
+        norm = 0.9 * (1.0 - 0.4 + 0.4 * [3, 2][d] / avgdl)
+        expected.append(np.float32(idf * (f * 1.9) / (f + norm)))
+    np.testing.assert_array_equal(offsets.numpy(), [0, 1, 3, 4])
+    np.testing.assert_array_equal(docs.numpy(), [0, 0, 1, 1])
+    np.testing.assert_array_equal(weights.numpy(), np.array(expected, dtype=np.float32))

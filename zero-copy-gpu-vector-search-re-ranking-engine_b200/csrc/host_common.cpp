@@ -73,8 +73,12 @@ cudaError_t ensure_smem_optin(const void* kernel) {
         std::lock_guard<std::mutex> lock(g_mutex);
         if (g_optin.count({device, kernel}) != 0) return cudaSuccess;
     }
-    const cudaError_t status = cudaFuncSetAttribute(
-        kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, device_max_smem() - 2048);
+    // The opt-in limit covers static and dynamic shared memory together.
+    cudaFuncAttributes attr{};
+    cudaError_t status = cudaFuncGetAttributes(&attr, kernel);
+    if (status != cudaSuccess) return status;
+    status = cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                  device_max_smem() - static_cast<int>(attr.sharedSizeBytes));
     if (status == cudaSuccess) {
         std::lock_guard<std::mutex> lock(g_mutex);
         g_optin.insert({device, kernel});

@@ -27,7 +27,8 @@ int device_sm_count();
 // Largest dynamic shared memory one CTA may opt into on the current device (cached).
 int device_max_smem();
 
-// Opts `kernel` into the device's maximum dynamic shared memory once per device.
+// Opts `kernel` into the largest dynamic shared memory the device allows next to its static
+// shared memory, once per device.
 cudaError_t ensure_smem_optin(const void* kernel);
 
 inline std::size_t round_up(std::size_t value, std::size_t to) {

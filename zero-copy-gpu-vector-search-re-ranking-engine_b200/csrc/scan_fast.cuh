@@ -52,6 +52,7 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float s_red[kWarpsAll];
     __shared__ float s_qscale[1];
+    __shared__ float s_inv;
     __shared__ u64 s_scratch[32];
     __shared__ u64 s_thr;
     __shared__ u64 s_merge_thr;
@@ -102,6 +103,7 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
         s_abort = 0;
         s_done = 0;
         s_sel_complete = 0;
+        s_inv = (p.lex != nullptr) ? hybrid_inverse(p, pass) : 0.0f;
     }
     for (int i = tid; i < kCandCap; i += kFastThreads) cbuf[i] = 0ull;
     stage_queries<MODE, 1, kFastThreads>(p, qsmem, s_qscale, pass, 1, s_red);
@@ -252,6 +254,8 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
             }
         }
         const float qscale = s_qscale[0];
+        const float inv = s_inv;
+        const float* lex_row = p.lex != nullptr ? p.lex + static_cast<size_t>(pass) * p.n : nullptr;
         u64* region = cbuf + warp * kRegionCap;
         unsigned long long* wspill = spill + warp * warp_rows;
         int wcount = 0;         // keys this warp appended (replicated in every lane)
@@ -277,6 +281,11 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
             const bool full_tile = rows == R;
 
             for (int rb = warp * kRowsPerWarp; rb < rows; rb += kRowsPerStep) {
+                // Hybrid: this lane's row's lexical score, loaded before the dot product so
+                // its latency overlaps the arithmetic.
+                const int r_own = rb + (gl >> kGroupShift) * RPW + grp;
+                float lexv = 0.0f;
+                if (lex_row != nullptr && (full_tile || r_own < rows)) lexv = __ldg(lex_row + row0 + r_own);
                 QElem acc[RW];
 #pragma unroll
                 for (int rr = 0; rr < RW; ++rr) {
@@ -308,6 +317,7 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
                         score = acc[0];
                     }
                     if (p.mask != nullptr && side_mask[r] == 0) score = -FLT_MAX;
+                    if (lex_row != nullptr) score = hybrid_blend(score, lexv, p.dense_weight, inv);
                     // Cheap float pre-check; only candidates at or above the threshold's score
                     // pay for the exact 64-bit key comparison.
                     if (!(score < thr_score) || thr == 0ull) {

@@ -6,6 +6,7 @@
 #include <string>
 
 #include "host_common.h"
+#include "lexical.h"
 #include "scan_fast.cuh"
 #include "scan_instances.h"
 #include "zcgvs_sm100.h"
@@ -322,12 +323,23 @@ size_t zcgvs_scan_topk_workspace_bytes(int dtype, int64_t doc_count, int dim, in
     return bytes;
 }
 
-int zcgvs_scan_topk(const void* corpus, int dtype, float scale, const float* row_scales,
-                    int64_t doc_count, int dim, const float* queries, int batch,
-                    const uint8_t* mask, int metric, int k, int id_base, int* out_indices,
-                    float* out_scores, void* workspace, size_t workspace_bytes, void* stream) {
-    using namespace zc;
-    if (doc_count <= 0 || batch <= 0 || dim <= 0) return ok();
+}  // extern "C"
+
+namespace zc {
+namespace {
+
+// Lexical inputs of a hybrid search (nullptr = dense only).
+struct HybridArgs {
+    const float* lex = nullptr;
+    const float* lex_part = nullptr;
+    int lex_parts = 0;
+    float dense_weight = 1.0f;
+};
+
+// Validation shared by the dense and hybrid entry points; fills the plan.
+int validate_scan(const void* corpus, int dtype, const float* row_scales, int64_t doc_count, int dim,
+                  const float* queries, int batch, const uint8_t* mask, int metric, int k, int id_base,
+                  int* out_indices, float* out_scores, ScanPlan& plan) {
     if (k <= 0) return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: k must be positive");
     if (k > ZCGVS_MAX_K) {
         return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: k=" + std::to_string(k) + " exceeds kernel capacity " +
@@ -351,15 +363,13 @@ int zcgvs_scan_topk(const void* corpus, int dtype, float scale, const float* row
     }
     int status = check_alignment(dtype, corpus, row_scales, queries, out_indices, out_scores);
     if (status != ZCGVS_OK) return status;
-    ScanPlan plan;
-    status = make_plan(dtype, doc_count, dim, batch, k, metric, false, aligned16(corpus),
-                       mask != nullptr, plan);
-    if (status != ZCGVS_OK) return status;
-    if (workspace == nullptr || workspace_bytes < plan.ws_total) {
-        return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: workspace smaller than zcgvs_scan_topk_workspace_bytes()");
-    }
-    if (!aligned16(workspace)) return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: workspace must be 16-byte aligned");
+    return make_plan(dtype, doc_count, dim, batch, k, metric, false, aligned16(corpus), mask != nullptr, plan);
+}
 
+int run_scan_topk(const ScanPlan& plan, const void* corpus, float scale, const float* row_scales,
+                  int64_t doc_count, int dim, const float* queries, int batch, const uint8_t* mask, int k,
+                  int id_base, int* out_indices, float* out_scores, uint8_t* ws, const HybridArgs& hy,
+                  cudaStream_t stream) {
     ScanParams params{};
     params.corpus = static_cast<const uint8_t*>(corpus);
     params.row_scales = row_scales;
@@ -372,7 +382,6 @@ int zcgvs_scan_topk(const void* corpus, int dtype, float scale, const float* row
     params.mask = mask;
     params.k = k;
     params.id_base = static_cast<unsigned int>(id_base);
-    uint8_t* ws = static_cast<uint8_t*>(workspace);
     params.status = reinterpret_cast<unsigned int*>(ws);
     params.counters = reinterpret_cast<unsigned int*>(ws + 16);
     params.lists = reinterpret_cast<unsigned long long*>(ws + plan.ws_header);
@@ -380,7 +389,95 @@ int zcgvs_scan_topk(const void* corpus, int dtype, float scale, const float* row
     params.out_idx = out_indices;
     params.out_scores = out_scores;
     params.out_matrix = nullptr;
-    return launch(plan, params, static_cast<cudaStream_t>(stream));
+    params.lex = hy.lex;
+    params.lex_part = hy.lex_part;
+    params.lex_parts = hy.lex_parts;
+    params.dense_weight = hy.dense_weight;
+    return launch(plan, params, stream);
+}
+
+// Hybrid workspace: the scan's, then lexical scores [batch][n], then partial maxima.
+struct HybridLayout {
+    size_t scan = 0, lex = 0, part = 0, total = 0;
+    int parts = 0;
+};
+
+HybridLayout hybrid_layout(size_t scan_ws, long long n, int batch) {
+    HybridLayout h;
+    h.parts = lexical_parts(n);
+    h.scan = round_up(scan_ws, kWorkspaceAlign);
+    h.lex = round_up(static_cast<size_t>(batch) * static_cast<size_t>(n) * 4, kWorkspaceAlign);
+    h.part = round_up(static_cast<size_t>(batch) * h.parts * 4, kWorkspaceAlign);
+    h.total = h.scan + h.lex + h.part;
+    return h;
+}
+
+}  // namespace
+}  // namespace zc
+
+extern "C" {
+
+int zcgvs_scan_topk(const void* corpus, int dtype, float scale, const float* row_scales,
+                    int64_t doc_count, int dim, const float* queries, int batch,
+                    const uint8_t* mask, int metric, int k, int id_base, int* out_indices,
+                    float* out_scores, void* workspace, size_t workspace_bytes, void* stream) {
+    using namespace zc;
+    if (doc_count <= 0 || batch <= 0 || dim <= 0) return ok();
+    ScanPlan plan;
+    int status = validate_scan(corpus, dtype, row_scales, doc_count, dim, queries, batch, mask, metric, k, id_base,
+                               out_indices, out_scores, plan);
+    if (status != ZCGVS_OK) return status;
+    if (workspace == nullptr || workspace_bytes < plan.ws_total) {
+        return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: workspace smaller than zcgvs_scan_topk_workspace_bytes()");
+    }
+    if (!aligned16(workspace)) return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: workspace must be 16-byte aligned");
+    return run_scan_topk(plan, corpus, scale, row_scales, doc_count, dim, queries, batch, mask, k, id_base,
+                         out_indices, out_scores, static_cast<uint8_t*>(workspace), HybridArgs{},
+                         static_cast<cudaStream_t>(stream));
+}
+
+size_t zcgvs_hybrid_topk_workspace_bytes(int dtype, int64_t doc_count, int dim, int batch, int k) {
+    if (doc_count <= 0 || dim <= 0 || batch <= 0 || k <= 0) return 0;
+    const size_t scan = zcgvs_scan_topk_workspace_bytes(dtype, doc_count, dim, batch, k);
+    return zc::hybrid_layout(scan, doc_count, batch).total;
+}
+
+int zcgvs_hybrid_topk(const void* corpus, int dtype, float scale, const float* row_scales, int64_t doc_count,
+                      int dim, const float* queries, int batch, const uint8_t* mask, int metric,
+                      const int64_t* offsets, const int* posting_docs, const float* posting_weights, int vocab_size,
+                      const int* query_terms, int term_stride, float dense_weight, int k, int* out_indices,
+                      float* out_scores, void* workspace, size_t workspace_bytes, void* stream) {
+    using namespace zc;
+    if (doc_count <= 0 || batch <= 0 || dim <= 0) return ok();
+    ScanPlan plan;
+    int status = validate_scan(corpus, dtype, row_scales, doc_count, dim, queries, batch, mask, metric, k, 0,
+                               out_indices, out_scores, plan);
+    if (status != ZCGVS_OK) return status;
+    const bool lexical = term_stride > 0 && query_terms != nullptr;
+    if (lexical && (offsets == nullptr || posting_docs == nullptr || posting_weights == nullptr || vocab_size <= 0)) {
+        return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs_hybrid_topk: null or empty lexical index");
+    }
+    const HybridLayout h = hybrid_layout(zcgvs_scan_topk_workspace_bytes(dtype, doc_count, dim, batch, k),
+                                         doc_count, batch);
+    if (workspace == nullptr || workspace_bytes < h.total) {
+        return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: workspace smaller than zcgvs_hybrid_topk_workspace_bytes()");
+    }
+    if (!aligned16(workspace)) return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: workspace must be 16-byte aligned");
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    HybridArgs hy;
+    if (lexical) {
+        hy.lex = reinterpret_cast<float*>(ws + h.scan);
+        hy.lex_part = reinterpret_cast<float*>(ws + h.scan + h.lex);
+        hy.lex_parts = h.parts;
+        hy.dense_weight = dense_weight;
+        status = launch_lexical(reinterpret_cast<const long long*>(offsets), posting_docs, posting_weights, vocab_size,
+                                query_terms, term_stride, doc_count, batch, nullptr, reinterpret_cast<float*>(ws + h.scan),
+                                reinterpret_cast<float*>(ws + h.scan + h.lex), st);
+        if (status != ZCGVS_OK) return status;
+    }
+    return run_scan_topk(plan, corpus, scale, row_scales, doc_count, dim, queries, batch, mask, k, 0, out_indices,
+                         out_scores, ws, hy, st);
 }
 
 int zcgvs_similarity(const void* corpus, int dtype, float scale, const float* row_scales,

@@ -75,7 +75,28 @@ struct ScanParams {
     int smem_query_off;
     int smem_topk_off;
     int smem_bar_off;
+    // Hybrid lexical + dense scoring (nullptr lex = dense only): lex[batch][n] lexical scores,
+    // lex_part[batch][lex_parts] non-negative partial maxima from the lexical kernel.
+    const float* lex;
+    const float* lex_part;
+    int lex_parts;
+    float dense_weight;
 };
+
+// Convex blend of a dense score with a max-normalised lexical score in the reference's
+// operation order, w * dense + ((1 - w) * lex) * inv (src/cuda/lexical.cu:66-72), every step
+// rounded on its own as in the CPU loop of tests/cpp/test_lexical.cu:82-89.
+__device__ __forceinline__ float hybrid_blend(float dense, float lex, float w, float inv) {
+    return __fadd_rn(__fmul_rn(w, dense), __fmul_rn(__fmul_rn(__fsub_rn(1.0f, w), lex), inv));
+}
+
+// 1 / max(0, max of the lexical partial maxima of query q), or 0 when that max is not positive
+// (src/cuda/lexical.cu:66-67). Called by one thread.
+__device__ __forceinline__ float hybrid_inverse(const ScanParams& p, int q) {
+    float peak = 0.0f;
+    for (int i = 0; i < p.lex_parts; ++i) peak = fmaxf(peak, p.lex_part[static_cast<size_t>(q) * p.lex_parts + i]);
+    return peak > 0.0f ? __fdiv_rn(1.0f, peak) : 0.0f;
+}
 
 template <int MODE>
 struct ModeTraits;
@@ -270,6 +291,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
     extern __shared__ __align__(128) uint8_t smem[];
     __shared__ float s_red[kScanWarps * QB];
     __shared__ float s_qscale[QB];
+    __shared__ float s_inv[QB];
     __shared__ u64 s_scratch[32];
     __shared__ int s_last;
     __shared__ int s_abort;
@@ -340,6 +362,7 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
     if (!EMIT && tid < QB) {
         tk.count[tid] = 0;
         tk.thr[tid] = 0ull;
+        s_inv[tid] = (p.lex != nullptr && tid < nq) ? hybrid_inverse(p, q0 + tid) : 0.0f;
     }
     __syncthreads();
 
@@ -420,6 +443,10 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
                         float score = __fdiv_rn(static_cast<float>(p.dim - 2 * h[q]),
                                                 static_cast<float>(p.dim));
                         if (masked) score = -FLT_MAX;
+                        if (!EMIT && p.lex != nullptr) {
+                            score = hybrid_blend(score, __ldg(p.lex + static_cast<size_t>(q0 + q) * p.n + row0 + r),
+                                                 p.dense_weight, s_inv[q]);
+                        }
                         if constexpr (EMIT) {
                             p.out_matrix[static_cast<size_t>(q0 + q) * p.n + row0 + r] = score;
                         } else {
@@ -490,6 +517,10 @@ __global__ void __launch_bounds__(kScanThreads, 1) scan_kernel(const ScanParams 
                         score = L2 ? -acc[0] : acc[0];
                     }
                     if (p.mask != nullptr && side_mask[r] == 0) score = -FLT_MAX;
+                    if (!EMIT && p.lex != nullptr) {
+                        score = hybrid_blend(score, __ldg(p.lex + static_cast<size_t>(q0 + q) * p.n + row0 + r),
+                                             p.dense_weight, s_inv[q]);
+                    }
                     if constexpr (EMIT) {
                         p.out_matrix[static_cast<size_t>(q0 + q) * p.n + row0 + r] = score;
                     } else {

@@ -1,0 +1,123 @@
+"""Host-side helpers for the BM25 inverted index the hybrid search consumes.
+
+The index is the reference's CSR layout (include/zcgvs/data/lexical_index.hpp:14-46):
+``offsets`` [vocab + 1] int64, ``docs`` int32 and ``weights`` fp32 per posting, postings grouped
+by term. The CUDA kernels need each term's postings sorted by document id, which the reference
+builder already guarantees (python/zcgvs_tools/build_lexical.py:143-162); ``sort_postings``
+establishes it for any other index without changing a single score (the sort is stable, so the
+additions per document keep their order).
+
+``build_csr`` computes the reference builder's BM25 weights from token counts
+(build_lexical.py:143-154): idf = ln(1 + (N - df + 0.5) / (df + 0.5)),
+w = idf * tf * (k1 + 1) / (tf + k1 * (1 - b + b * len / avgdl)), in float64, stored as fp32.
+``synthetic_corpus`` / ``synthetic_queries`` draw the seeded hybrid workload (Poisson document
+lengths, Zipf term frequencies) on any torch device.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+
+
+def sort_postings(offsets, docs, weights):
+    """Stable sort of every term's postings by document id. numpy arrays in, numpy arrays out."""
+    offsets = np.asarray(offsets, dtype=np.int64)
+    docs = np.asarray(docs, dtype=np.int32)
+    weights = np.asarray(weights, dtype=np.float32)
+    term_of = np.repeat(np.arange(offsets.size - 1, dtype=np.int64), np.diff(offsets))
+    order = np.lexsort((docs, term_of))  # last key is primary; lexsort is stable
+    return offsets.copy(), docs[order], weights[order]
+
+
+def postings_sorted(offsets, docs) -> bool:
+    """True when every term's postings are non-decreasing in document id."""
+    offsets = np.asarray(offsets, dtype=np.int64)
+    docs = np.asarray(docs, dtype=np.int64)
+    if docs.size < 2:
+        return True
+    drops = np.flatnonzero(np.diff(docs) < 0) + 1  # positions where a document id decreases
+    starts = np.zeros(docs.size, dtype=bool)
+    starts[offsets[1:-1][offsets[1:-1] < docs.size]] = True
+    return bool(starts[drops].all())
+
+
+def build_csr(doc_ids, term_ids, tf, lengths, vocab: int, k1: float = 1.2, b: float = 0.75):
+    """BM25 CSR index from unique (doc, term) pairs with term frequencies.
+
+    doc_ids, term_ids, tf: torch int64 tensors of the pairs (any order); lengths: torch tensor
+    [n_docs] of document token counts. Returns torch (offsets int64 [vocab + 1], docs int32,
+    weights fp32) on the inputs' device, postings sorted by (term, doc).
+    """
+    import torch
+
+    n_docs = lengths.numel()
+    key = term_ids * n_docs + doc_ids
+    order = torch.argsort(key)
+    doc_ids, term_ids, tf = doc_ids[order], term_ids[order], tf[order].to(torch.float64)
+    df = torch.bincount(term_ids, minlength=vocab).to(torch.float64)
+    avgdl = float(lengths.to(torch.float64).mean()) if n_docs else 0.0
+    if avgdl <= 0.0:
+        avgdl = 1.0
+    idf = torch.log(1.0 + (n_docs - df + 0.5) / (df + 0.5))
+    norm = k1 * (1.0 - b + b * lengths.to(torch.float64)[doc_ids] / avgdl)
+    weights = (idf[term_ids] * (tf * (k1 + 1.0)) / (tf + norm)).to(torch.float32)
+    offsets = torch.zeros(vocab + 1, dtype=torch.int64, device=doc_ids.device)
+    offsets[1:] = torch.cumsum(torch.bincount(term_ids, minlength=vocab), 0)
+    return offsets, doc_ids.to(torch.int32), weights
+
+
+def zipf_probs(vocab: int, s: float, device=None):
+    import torch
+
+    ranks = torch.arange(1, vocab + 1, dtype=torch.float64, device=device)
+    p = ranks.pow(-s)
+    return p / p.sum()
+
+
+def synthetic_corpus(n_docs: int, vocab: int, mean_len: float, zipf_s: float, seed: int, device=None,
+                     k1: float = 1.2, b: float = 0.75, chunk_tokens: int = 1 << 27):
+    """Seeded BM25 index: lengths ~ Poisson(mean_len), tokens ~ Zipf(zipf_s) over the vocabulary
+    (term id = rank - 1). Returns torch (offsets, docs, weights) on `device`."""
+    import torch
+
+    gen = torch.Generator(device=device or "cpu")
+    gen.manual_seed(seed)
+    rate = torch.full((n_docs,), float(mean_len), dtype=torch.float64, device=device)
+    lengths = torch.poisson(rate, generator=gen).to(torch.int64)
+    probs = zipf_probs(vocab, zipf_s, device).to(torch.float32)
+    starts = torch.cumsum(lengths, 0) - lengths
+    pairs = []
+    # Draw tokens in chunks of whole documents so the (doc, term) keys fit memory.
+    doc0 = 0
+    while doc0 < n_docs:
+        doc1 = int(torch.searchsorted(starts, (starts[doc0] + chunk_tokens).reshape(1), right=True)[0])
+        doc1 = max(doc1, doc0 + 1)
+        count = int(lengths[doc0:doc1].sum())
+        if count:
+            tokens = torch.multinomial(probs, count, replacement=True, generator=gen)
+            owner = torch.repeat_interleave(torch.arange(doc0, doc1, device=device), lengths[doc0:doc1])
+            key, tf = torch.unique(owner * vocab + tokens, return_counts=True)
+            pairs.append((key // vocab, key % vocab, tf))
+        doc0 = doc1
+    doc_ids = torch.cat([p[0] for p in pairs]) if pairs else torch.empty(0, dtype=torch.int64, device=device)
+    term_ids = torch.cat([p[1] for p in pairs]) if pairs else torch.empty(0, dtype=torch.int64, device=device)
+    tf = torch.cat([p[2] for p in pairs]) if pairs else torch.empty(0, dtype=torch.int64, device=device)
+    return build_csr(doc_ids, term_ids, tf, lengths, vocab, k1, b)
+
+
+def synthetic_queries(batch: int, vocab: int, zipf_s: float, seed: int, min_terms: int = 3, max_terms: int = 12):
+    """[batch, max_terms] int32 numpy term ids: a U{min..max} count of Zipf-drawn terms per query,
+    de-duplicated in first-occurrence order (Engine::lexicalTerms, src/engine/engine.cpp:150-172)
+    and padded with -1."""
+    rng = np.random.default_rng(seed)
+    ranks = np.arange(1, vocab + 1, dtype=np.float64)
+    p = ranks ** (-zipf_s)
+    p /= p.sum()
+    out = np.full((batch, max_terms), -1, dtype=np.int32)
+    for q in range(batch):
+        count = int(rng.integers(min_terms, max_terms + 1))
+        drawn = rng.choice(vocab, size=count, p=p)
+        _, first = np.unique(drawn, return_index=True)
+        uniq = drawn[np.sort(first)]
+        out[q, : uniq.size] = uniq
+    return out

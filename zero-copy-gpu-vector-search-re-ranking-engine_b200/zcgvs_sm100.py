@@ -40,6 +40,12 @@ SIGNATURES = {
                                   _P, _P, _P]),
     "zcgvs_gather_rescore": (_i32, [_P, _i32, _f32, _P, _i64, _i32, _P, _i32, _P, _i32, _i32, _P,
                                     _P]),
+    "zcgvs_hybrid_topk_workspace_bytes": (_sz, [_i32, _i64, _i32, _i32, _i32]),
+    "zcgvs_hybrid_topk": (_i32, [_P, _i32, _f32, _P, _i64, _i32, _P, _i32, _P, _i32, _P, _P, _P, _i32,
+                                 _P, _i32, _f32, _i32, _P, _P, _P, _sz, _P]),
+    "zcgvs_bm25": (_i32, [_P, _P, _P, _P, _i32, _i32, _P, _P]),
+    "zcgvs_max_positive": (_i32, [_P, _i32, _P, _P]),
+    "zcgvs_fuse_scores": (_i32, [_P, _P, _P, _f32, _i32, _P]),
 }
 
 
@@ -210,3 +216,58 @@ def gather_rescore(store, dtype: int, dim: int, queries, candidates, *, scale: f
                                      _ptr(queries), batch, _ptr(candidates), candidates.shape[1],
                                      metric, _ptr(out), _stream(stream)))
     return out
+
+
+class LexicalIndex:
+    """Device copy of a CSR BM25 index (offsets int64, docs int32, weights fp32; torch tensors).
+    Posting lists must be sorted by document within each term (lexical_index.sort_postings)."""
+
+    def __init__(self, offsets, docs, weights, device=None):
+        import torch
+
+        self.offsets = torch.as_tensor(offsets, dtype=torch.int64, device=device or "cuda")
+        self.docs = torch.as_tensor(docs, dtype=torch.int32, device=device or "cuda")
+        self.weights = torch.as_tensor(weights, dtype=torch.float32, device=device or "cuda")
+        self.vocab = self.offsets.numel() - 1
+
+
+def hybrid_topk(corpus, dtype: int, dim: int, queries, k: int, index: LexicalIndex, terms,
+                dense_weight: float, *, scale: float = 1.0, row_scales=None, mask=None,
+                metric: int = METRIC_DOT, workspace: Workspace | None = None, out=None, stream=None):
+    """Hybrid BM25 + dense top-k. terms: int32 device tensor [B, stride] (-1 padded)."""
+    import torch
+
+    doc_count = corpus.shape[0]
+    queries = queries.reshape(-1, dim)
+    batch = queries.shape[0]
+    if terms.dim() != 2:
+        terms = terms.reshape(batch, -1)
+    if out is None:
+        out = (torch.empty((batch, k), dtype=torch.int32, device=queries.device),
+               torch.empty((batch, k), dtype=torch.float32, device=queries.device))
+    ws = workspace or Workspace(queries.device)
+    nbytes = int(lib().zcgvs_hybrid_topk_workspace_bytes(dtype, doc_count, dim, batch, k))
+    buf = ws.get(nbytes, stream)
+    check(lib().zcgvs_hybrid_topk(_ptr(corpus), dtype, scale, _ptr(row_scales), doc_count, dim, _ptr(queries),
+                                  batch, _ptr(mask), metric, _ptr(index.offsets), _ptr(index.docs),
+                                  _ptr(index.weights), index.vocab, _ptr(terms), terms.shape[1], dense_weight, k,
+                                  _ptr(out[0]), _ptr(out[1]), _ptr(buf), buf.numel(), _stream(stream)))
+    return out
+
+
+def bm25(index: LexicalIndex, terms, scores, stream=None):
+    """scores[d] += BM25 weights of one query's terms (the reference launchBm25)."""
+    check(lib().zcgvs_bm25(_ptr(index.offsets), _ptr(index.docs), _ptr(index.weights), _ptr(terms),
+                           terms.numel(), scores.numel(), _ptr(scores), _stream(stream)))
+    return scores
+
+
+def max_positive(values, out_max, stream=None):
+    check(lib().zcgvs_max_positive(_ptr(values), values.numel(), _ptr(out_max), _stream(stream)))
+    return out_max
+
+
+def fuse_scores(dense, lexical, lexical_max, weight: float, stream=None):
+    check(lib().zcgvs_fuse_scores(_ptr(dense), _ptr(lexical), _ptr(lexical_max), weight, dense.numel(),
+                                  _stream(stream)))
+    return dense
