@@ -85,28 +85,72 @@ def make_queries(torch, device, seed, count):
 
 
 class ClockSampler:
-    """Samples SM clocks and throttle reasons with nvidia-smi during the timed region."""
+    """Samples SM clocks and clock-event (throttle) reasons during the timed region.
 
+    Polls NVML from a thread every `interval_s` (a timed region can be only tens of ms long);
+    falls back to an `nvidia-smi -lms` subprocess when NVML is unavailable. Read-only: no
+    setting of the GPU is changed.
+    """
+
+    REASONS = (("hw_slowdown", "nvmlClocksEventReasonHwSlowdown"),
+               ("hw_thermal_slowdown", "nvmlClocksEventReasonHwThermalSlowdown"),
+               ("sw_thermal_slowdown", "nvmlClocksEventReasonSwThermalSlowdown"),
+               ("sw_power_cap", "nvmlClocksEventReasonSwPowerCap"))
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
 
-    def __init__(self, gpu_index: int):
-        self.gpu_index = gpu_index
+    def __init__(self, cuda_index: int, interval_s: float = 0.002):
+        self.cuda_index = cuda_index
+        self.interval_s = interval_s
+        self.samples = []          # (sm_mhz, reason bitmask)
+        self.max_mhz = None
         self.proc = None
+        self.thread = None
+        self.stop = None
+        self.nvml = None
+
+    def _poll(self, handle):
+        nv = self.nvml
+        while not self.stop.is_set():
+            try:
+                self.samples.append((float(nv.nvmlDeviceGetClockInfo(handle, nv.NVML_CLOCK_SM)),
+                                     int(nv.nvmlDeviceGetCurrentClocksEventReasons(handle))))
+            except Exception:  # noqa: BLE001 - a failed read only loses one sample
+                pass
+            self.stop.wait(self.interval_s)
 
     def __enter__(self):
+        import threading
+
+        try:
+            import pynvml as nv
+            import torch
+
+            nv.nvmlInit()
+            handle = nv.nvmlDeviceGetHandleByIndex(torch.cuda._get_nvml_device_index(self.cuda_index))
+            self.max_mhz = float(nv.nvmlDeviceGetMaxClockInfo(handle, nv.NVML_CLOCK_SM))
+            self.nvml = nv
+            self.stop = threading.Event()
+            self.thread = threading.Thread(target=self._poll, args=(handle,), daemon=True)
+            self.thread.start()
+            return self
+        except Exception:  # noqa: BLE001 - fall back to nvidia-smi
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.gpu_index}", f"--query-gpu={self.FIELDS}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
+                ["nvidia-smi", f"--id={self.cuda_index}", f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "20"],
                 stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
         except OSError:
             self.proc = None
         return self
 
     def __exit__(self, *exc):
-        self.lines = []
+        if self.thread is not None:
+            self.stop.set()
+            self.thread.join()
+            return
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -114,25 +158,33 @@ class ClockSampler:
             except subprocess.TimeoutExpired:
                 self.proc.kill()
                 out, _ = self.proc.communicate()
-            self.lines = [ln for ln in out.splitlines() if ln.strip()]
+            for ln in out.splitlines():
+                parts = [p.strip() for p in ln.split(",")]
+                if len(parts) < 9:
+                    continue
+                try:
+                    mhz = float(parts[1])
+                    self.max_mhz = float(parts[2])
+                except ValueError:
+                    continue
+                mask = sum(1 << i for i, flag in enumerate(parts[5:9]) if flag.lower() == "active")
+                self.samples.append((mhz, mask))
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in getattr(self, "lines", []):
-            parts = [p.strip() for p in ln.split(",")]
-            if len(parts) < 9:
-                continue
-            try:
-                sm.append(float(parts[1]))
-                mx = float(parts[2])
-            except ValueError:
-                continue
-            for name, flag in zip(names, parts[5:9]):
-                if flag.lower() == "active":
-                    reasons.add(name)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        reasons = set()
+        for _, mask in self.samples:
+            if self.nvml is not None:
+                for name, const in self.REASONS:
+                    if mask & getattr(self.nvml, const):
+                        reasons.add(name)
+            else:
+                for i, (name, _) in enumerate(self.REASONS):
+                    if mask & (1 << i):
+                        reasons.add(name)
+        sm = [mhz for mhz, _ in self.samples]
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(reasons), "samples": len(sm),
+                "source": "nvml" if self.nvml is not None else "nvidia-smi"}
 
 
 def measured_peaks():
@@ -151,7 +203,7 @@ def profiled_traffic(workload: str):
         return None
 
 
-def cpu_baseline(codes_host, scales_host, queries_host, budget_s=20.0):
+def cpu_baseline(codes_host, scales_host, queries_host, budget_s=12.0):
     """Times the reference CPU path on a bounded query sample; returns the cpu_baseline dict."""
     sys.path.insert(0, str(ROOT / "oracle"))
     import ctypes
@@ -168,15 +220,20 @@ def cpu_baseline(codes_host, scales_host, queries_host, budget_s=20.0):
         ref = oracle.ref_lib()
     if ref is not None:
         corpus = codes_host.astype(np.float32) * scales_host[:, None]
-        sample = max(1, min(len(queries_host), 2 * threads))
-        out = np.empty((sample, TOP_K), dtype=np.int32)
-        q = np.ascontiguousarray(queries_host[:sample])
-        elapsed = ref.refcpu_search(corpus.ctypes.data_as(ctypes.c_void_p), N_DOCS, DIM,
-                                    q.ctypes.data_as(ctypes.c_void_p), sample, TOP_K, threads,
-                                    out.ctypes.data_as(ctypes.c_void_p))
-        return {"value": sample / elapsed, "unit": UNIT, "cores": min(threads, sample), "kind": "reference",
-                "sample": f"{sample} queries x full {N_DOCS}x{DIM} corpus (dequantised fp32), "
-                          f"cpuCosineSimilarity + cpuTopKIndices, {min(threads, sample)} threads",
+        # Chunks of one query per thread until about `budget_s` of CPU time (or the query set)
+        # is used up.
+        chunk = max(1, min(len(queries_host), threads))
+        out = np.empty((chunk, TOP_K), dtype=np.int32)
+        done, elapsed = 0, 0.0
+        while done < len(queries_host) and (done == 0 or elapsed < budget_s):
+            q = np.ascontiguousarray(queries_host[done:done + chunk])
+            elapsed += ref.refcpu_search(corpus.ctypes.data_as(ctypes.c_void_p), N_DOCS, DIM,
+                                         q.ctypes.data_as(ctypes.c_void_p), q.shape[0], TOP_K, threads,
+                                         out.ctypes.data_as(ctypes.c_void_p))
+            done += q.shape[0]
+        return {"value": done / elapsed, "unit": UNIT, "cores": min(threads, chunk), "kind": "reference",
+                "sample": f"{done} queries x full {N_DOCS}x{DIM} corpus (dequantised fp32), "
+                          f"cpuCosineSimilarity + cpuTopKIndices, {min(threads, chunk)} threads",
                 "seconds": elapsed}
     # Oracle port fallback (single thread, exact per-row int8 arithmetic).
     sample = 2
@@ -345,7 +402,8 @@ def run_ours(args):
                        "l2": "inputs larger than L2 (772 MB corpus vs 126 MB L2)"},
             "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peak, "unit": "GB/s",
                          "frac": achieved_gbs / peak, "traffic": traffic,
-                         "peak_source": peak_kind, "kernel": "zc::scan_kernel<I8R,QB,JC>",
+                         "peak_source": peak_kind,
+                         "kernel": "zc::scan_fast_kernel<kModeI8R,3>" if B == 1 else "zc::scan_kernel<kModeI8R,QB>",
                          "algorithmic_bytes_per_launch": algo_bytes},
             "e2e": {"value": world * B * e2e_steps / e2e_s, "unit": UNIT,
                     "h2d_bytes_per_step": B * DIM * 4, "d2h_bytes_per_step": B * k * 8},

@@ -173,6 +173,20 @@ int zcgvs_gather_rescore(const void* store, int dtype, float scale, const float*
                          void* stream);
 
 /* ---------------------------------------------------------------------------------------
+ * Merge of per-shard top-k lists (row-sharded multi-GPU search). No reference counterpart:
+ * the reference runs on one GPU; its single-GPU merge is mergeTopKKernel
+ * (src/cuda/topk.cu:76-115).
+ *
+ *   list_indices / list_scores : [lists, batch, k_in] (the layout an all-gather of every
+ *                     shard's [batch, k_in] result produces); ids are global (each shard
+ *                     searched with id_base = its first row); ids < 0 are padding.
+ *   lists * k_in    : at most 16384.
+ *   out_indices / out_scores   : [batch, k], (score desc, id asc), padded with (-1, -FLT_MAX).
+ * --------------------------------------------------------------------------------------- */
+int zcgvs_merge_topk(const int* list_indices, const float* list_scores, int lists, int batch,
+                     int k_in, int k, int* out_indices, float* out_scores, void* stream);
+
+/* ---------------------------------------------------------------------------------------
  * Hybrid lexical + dense search. Replaces the hybrid stages of Searcher::recordPipeline
  * (src/search/searcher.cpp:236-263: per query launchBm25, launchMaxPositive and
  * launchFuseScores over [batch, N] score matrices, then launchTopK) with two kernels: a BM25

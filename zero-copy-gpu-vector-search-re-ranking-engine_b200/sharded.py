@@ -1,0 +1,72 @@
+"""Row-sharded search across the GPUs of one node (one process per GPU, torch.distributed).
+
+The reference runs on one GPU. For corpora that do not fit one GPU (50M x 768 fp16 is 77 GB)
+or to scale one query stream over 8 GPUs, rows are split into P contiguous shards, one per
+rank. Every rank searches its shard with ``id_base`` = its first row, so its [B, k] result
+carries global ids; one NCCL all-gather brings every shard's result to every rank; and
+``zcgvs_merge_topk`` selects the global top-k under (score desc, id asc). The union of per-shard
+top-k lists contains the global top-k and the order is total, so the result is identical to a
+single-GPU search over the whole corpus.
+
+The exchange is [P, B, k] ids and score bits (B x k x 8 bytes per rank): latency-bound, so one
+all-gather of a packed int32 tensor is used, capturable in a CUDA graph.
+"""
+
+from __future__ import annotations
+
+
+def shard_bounds(n: int, world: int, rank: int) -> tuple[int, int]:
+    """Rows [begin, end) of shard `rank` when n rows are split as evenly as possible."""
+    base, extra = divmod(n, world)
+    begin = rank * base + min(rank, extra)
+    return begin, begin + base + (1 if rank < extra else 0)
+
+
+class ShardedSearch:
+    """One rank's part of a row-sharded top-k search.
+
+    local_search(queries, k, id_base) -> (ids int32 [B, k], scores fp32 [B, k]) searches this
+    rank's shard; merge(ids [P, B, k], scores [P, B, k], k) -> ([B, k], [B, k]) merges. The
+    defaults are the CUDA library's zcgvs_scan_topk and zcgvs_merge_topk; the all-gather goes
+    through torch.distributed (NCCL on GPUs).
+    """
+
+    def __init__(self, shard_begin: int, local_search, merge=None, group=None):
+        self.shard_begin = shard_begin
+        self.local_search = local_search
+        if merge is None:
+            import zcgvs_sm100 as zc
+
+            merge = zc.merge_topk
+        self.merge = merge
+        self.group = group
+
+    def search(self, queries, k: int):
+        import torch
+        import torch.distributed as dist
+
+        ids, scores = self.local_search(queries, k, self.shard_begin)
+        world = dist.get_world_size(self.group)
+        # One packed exchange: ids and the scores' bit patterns side by side.
+        packed = torch.stack([ids, scores.view(torch.int32)])            # [2, B, k]
+        # Concatenated along dim 0 (the layout every backend accepts), then viewed per rank.
+        gathered = torch.empty((world * 2,) + tuple(packed.shape[1:]), dtype=packed.dtype, device=packed.device)
+        dist.all_gather_into_tensor(gathered, packed, group=self.group)
+        gathered = gathered.view((world, 2) + tuple(packed.shape[1:]))
+        all_ids = gathered[:, 0].contiguous()                              # [P, B, k]
+        all_scores = gathered[:, 1].contiguous().view(torch.float32)
+        return self.merge(all_ids, all_scores, k)
+
+
+def scan_shard_search(corpus_shard, dtype: int, dim: int, *, scale: float = 1.0, row_scales=None, mask=None,
+                      metric: int = 1, workspace=None):
+    """local_search for ShardedSearch over a device-resident shard with zcgvs_scan_topk."""
+    import zcgvs_sm100 as zc
+
+    ws = workspace or zc.Workspace(corpus_shard.device)
+
+    def run(queries, k, id_base):
+        return zc.scan_topk(corpus_shard, dtype, dim, queries, k, scale=scale, row_scales=row_scales, mask=mask,
+                            metric=metric, id_base=id_base, workspace=ws)
+
+    return run

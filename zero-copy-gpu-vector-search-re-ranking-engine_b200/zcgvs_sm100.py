@@ -40,6 +40,7 @@ SIGNATURES = {
                                   _P, _P, _P]),
     "zcgvs_gather_rescore": (_i32, [_P, _i32, _f32, _P, _i64, _i32, _P, _i32, _P, _i32, _i32, _P,
                                     _P]),
+    "zcgvs_merge_topk": (_i32, [_P, _P, _i32, _i32, _i32, _i32, _P, _P, _P]),
     "zcgvs_hybrid_topk_workspace_bytes": (_sz, [_i32, _i64, _i32, _i32, _i32]),
     "zcgvs_hybrid_topk": (_i32, [_P, _i32, _f32, _P, _i64, _i32, _P, _i32, _P, _i32, _P, _P, _P, _i32,
                                  _P, _i32, _f32, _i32, _P, _P, _P, _sz, _P]),
@@ -271,3 +272,16 @@ def fuse_scores(dense, lexical, lexical_max, weight: float, stream=None):
     check(lib().zcgvs_fuse_scores(_ptr(dense), _ptr(lexical), _ptr(lexical_max), weight, dense.numel(),
                                   _stream(stream)))
     return dense
+
+
+def merge_topk(list_indices, list_scores, k: int, out=None, stream=None):
+    """Global top-k of per-shard lists [P, B, k_in] (int32 ids, fp32 scores) -> ([B, k], [B, k])."""
+    import torch
+
+    lists, batch, k_in = list_indices.shape
+    if out is None:
+        out = (torch.empty((batch, k), dtype=torch.int32, device=list_indices.device),
+               torch.empty((batch, k), dtype=torch.float32, device=list_indices.device))
+    check(lib().zcgvs_merge_topk(_ptr(list_indices), _ptr(list_scores), lists, batch, k_in, k, _ptr(out[0]),
+                                 _ptr(out[1]), _stream(stream)))
+    return out
