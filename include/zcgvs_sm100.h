@@ -173,6 +173,38 @@ int zcgvs_gather_rescore(const void* store, int dtype, float scale, const float*
                          void* stream);
 
 /* ---------------------------------------------------------------------------------------
+ * Tensor-core batched search (tcgen05 MMA, TMEM accumulators, TMA). For large query batches
+ * the scan is a dense contraction; the reference has no tensor-core path (it runs its CUDA-core
+ * similarity kernel per 8 queries, src/cuda/similarity.cu:83-164, and writes the [batch, N]
+ * score matrix). Corpora: ZCGVS_DTYPE_F16 (queries rounded to fp16, fp32 accumulation) and
+ * ZCGVS_DTYPE_I8_ROW (queries quantised per row as in zcgvs_scan_topk, exact int32 dot, so the
+ * result equals zcgvs_scan_topk bit for bit). Rows must be multiples of 128 bytes (dim % 64 == 0
+ * for F16, dim % 128 == 0 for I8_ROW); metric dot or cosine.
+ *
+ * zcgvs_gemm_topk: a threshold pre-pass over a sample of document tiles (per query, the k-th
+ * largest tile maximum, a lower bound of the k-th best score), a filtered pass over the whole
+ * corpus that keeps only documents at or above it, and an exact selection of those candidates.
+ * Arguments and result as zcgvs_scan_topk. A query with more than 16384 candidates at its
+ * threshold sets bit 8 of the workspace status word (zcgvs_workspace_status); its result is
+ * then incomplete. The workspace must be 256-byte aligned; it needs no zero-fill.
+ *
+ * zcgvs_gemm_similarity: the [batch, doc_count] score matrix (masked documents -FLT_MAX).
+ * --------------------------------------------------------------------------------------- */
+size_t zcgvs_gemm_topk_workspace_bytes(int dtype, int64_t doc_count, int dim, int batch, int k);
+
+int zcgvs_gemm_topk(const void* corpus, int dtype, const float* row_scales, int64_t doc_count,
+                    int dim, const float* queries, int batch, const uint8_t* mask, int metric,
+                    int k, int id_base, int* out_indices, float* out_scores, void* workspace,
+                    size_t workspace_bytes, void* stream);
+
+size_t zcgvs_gemm_similarity_workspace_bytes(int dtype, int64_t doc_count, int dim, int batch);
+
+int zcgvs_gemm_similarity(const void* corpus, int dtype, const float* row_scales,
+                          int64_t doc_count, int dim, const float* queries, int batch,
+                          const uint8_t* mask, int metric, float* scores, void* workspace,
+                          size_t workspace_bytes, void* stream);
+
+/* ---------------------------------------------------------------------------------------
  * Merge of per-shard top-k lists (row-sharded multi-GPU search). No reference counterpart:
  * the reference runs on one GPU; its single-GPU merge is mergeTopKKernel
  * (src/cuda/topk.cu:76-115).

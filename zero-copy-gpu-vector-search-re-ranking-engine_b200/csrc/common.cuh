@@ -10,6 +10,9 @@
 
 namespace zc {
 
+// Storage modes of the scan kernels; the codes equal the ABI dtype codes.
+enum ScanMode : int { kModeF32 = 0, kModeF16 = 1, kModeI8M = 2, kModeBin = 3, kModeI8R = 4 };
+
 using u64 = unsigned long long;
 
 // ---------------------------------------------------------------------------------------

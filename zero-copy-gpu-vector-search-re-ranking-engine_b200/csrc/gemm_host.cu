@@ -1,0 +1,442 @@
+// Host side and helper kernels of the tensor-core batched search (gemm_scan.cuh).
+//
+// zcgvs_gemm_topk runs four kernels on one stream, all on the caller's workspace:
+//   1. prep      : queries -> fp16 (ZCGVS_DTYPE_F16) or per-row int8 + scale (ZCGVS_DTYPE_I8_ROW,
+//                  the quantiser of the streaming scan) in the layout the TMA loads read.
+//   2. tile max  : the tensor-core scan over the first T document tiles, writing each query's
+//                  maximum score per tile.
+//   3. threshold : per query, thr = the k-th largest of the sample's 32-document chunk maxima.
+//                  k chunks each hold a document scoring >= thr, so at least k documents do:
+//                  every member of the exact top-k scores >= thr. Also clears the counters.
+//   4. filter    : the tensor-core scan over all tiles, appending every document whose key
+//                  (score, id) is >= the query's threshold key to its candidate buffer.
+//   5. select    : per query, the exact (score desc, id asc) top-k of its candidates.
+//   6. retry     : a query whose candidates overflowed the buffer (capacity C) raises its
+//                  threshold key to the k-th largest key it did capture (any k captured
+//                  documents bound the k-th best from below) and runs the filter and select
+//                  again; both retry kernels return at once when no query overflowed, so the
+//                  launch sequence is fixed (capturable in a CUDA graph).
+// T = max(k / 4, 8 k N_tiles / C) tiles keeps the expected candidate count well under C.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+#include <cuda_runtime.h>
+
+#include <algorithm>
+#include <cfloat>
+#include <climits>
+#include <string>
+
+#include "gemm_scan.cuh"
+#include "host_common.h"
+#include "topk_cta.cuh"
+#include "zcgvs_sm100.h"
+
+namespace zc {
+namespace gemm {
+
+namespace {
+
+constexpr int kCandCap = 16384;
+constexpr int kSelectThreads = 512;
+constexpr size_t kAlign = 256;
+
+// Queries -> the MMA operand layout: fp16 rows, or int8 rows with a per-row scale computed
+// exactly as the streaming scan's quantiser (scan_kernel.cuh, stage_queries).
+template <int MODE>
+__global__ void prep_queries_kernel(const float* __restrict__ queries, int dim, void* out, float* qscale) {
+    __shared__ float s_red[8];
+    __shared__ float s_scale;
+    const int q = blockIdx.x;
+    const float* src = queries + static_cast<size_t>(q) * dim;
+    if constexpr (MODE == kModeF16) {
+        __half* dst = static_cast<__half*>(out) + static_cast<size_t>(q) * dim;
+        for (int j = threadIdx.x; j < dim; j += blockDim.x) dst[j] = __float2half_rn(src[j]);
+    } else {
+        float m = 0.0f;
+        for (int j = threadIdx.x; j < dim; j += blockDim.x) m = fmaxf(m, fabsf(src[j]));
+        m = warp_max_f32(m);
+        if ((threadIdx.x & 31) == 0) s_red[threadIdx.x >> 5] = m;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            float mm = 0.0f;
+            for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) mm = fmaxf(mm, s_red[w]);
+            s_scale = mm > 0.0f ? __fdiv_rn(mm, 127.0f) : 1.0f;
+            qscale[q] = s_scale;
+        }
+        __syncthreads();
+        const float inv = __fdiv_rn(1.0f, s_scale);
+        int8_t* dst = static_cast<int8_t*>(out) + static_cast<size_t>(q) * dim;
+        for (int j = threadIdx.x; j < dim; j += blockDim.x) {
+            const float r = rintf(__fmul_rn(src[j], inv));
+            dst[j] = static_cast<int8_t>(fminf(fmaxf(r, -127.0f), 127.0f));
+        }
+    }
+}
+
+// thr_key[q] = the smallest key of the k-th largest chunk maximum's score (0, i.e. keep every
+// document, with fewer than k chunks); clears the candidate counter and the done flag of q;
+// block 0 clears the retry flag.
+__global__ void __launch_bounds__(kSelectThreads) threshold_kernel(const float* __restrict__ chunk_max, int chunks,
+                                                                   int k, int cap, unsigned long long* thr_key,
+                                                                   unsigned int* cand_count, int* done,
+                                                                   unsigned int* retry) {
+    extern __shared__ __align__(16) u64 keys[];
+    __shared__ int s_count;
+    __shared__ u64 s_thr;
+    const int q = blockIdx.x;
+    for (int i = threadIdx.x; i < cap; i += kSelectThreads) {
+        keys[i] = i < chunks ? make_key(chunk_max[static_cast<size_t>(q) * chunks + i], static_cast<uint32_t>(i)) : 0ull;
+    }
+    TopkSmem t;
+    t.buf = keys;
+    t.count = &s_count;
+    t.thr = &s_thr;
+    t.cap = cap;
+    t.k = k;
+    if (threadIdx.x == 0) s_count = chunks;
+    __syncthreads();
+    topk_flush_mask(t, 1u, kSelectThreads);
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        // keys[k - 1] exists only when there are at least k chunks (the buffer holds cap >= chunks).
+        const float score = chunks >= k ? key_score(keys[k - 1]) : -INFINITY;
+        thr_key[q] = score > -INFINITY ? (static_cast<u64>(orderable_bits(score)) << 32) : 0ull;
+        cand_count[q] = 0u;
+        done[q] = 0;
+        if (q == 0) *retry = 0u;
+    }
+}
+
+// The exact top-k of each query's candidates. A query whose buffer overflowed keeps no result:
+// on the first pass (final == 0) its threshold key rises to the k-th largest key it captured,
+// its counter is cleared and the retry flag is set; on the retry pass (final == 1) it writes what
+// it has and records the overflow in the status word. Queries already answered are skipped.
+__global__ void __launch_bounds__(kSelectThreads) select_kernel(const unsigned long long* __restrict__ cand,
+                                                                unsigned int* cand_count, int cap, int k,
+                                                                unsigned long long* thr_key, int* done,
+                                                                unsigned int* retry, unsigned int* status, int final,
+                                                                int* out_idx, float* out_scores) {
+    extern __shared__ __align__(16) u64 keys[];
+    __shared__ int s_count;
+    __shared__ u64 s_thr;
+    const int q = blockIdx.x;
+    if (final && (*reinterpret_cast<const volatile unsigned int*>(retry) == 0u || done[q])) return;
+    const unsigned int total = cand_count[q];
+    const bool overflow = total > static_cast<unsigned int>(cap);
+    const int n = static_cast<int>(overflow ? static_cast<unsigned int>(cap) : total);
+    const int size = n < 2 ? 2 : 1 << (32 - __clz(n - 1));
+    for (int i = threadIdx.x; i < size; i += kSelectThreads) {
+        keys[i] = i < n ? cand[static_cast<size_t>(q) * cap + i] : 0ull;
+    }
+    TopkSmem t;
+    t.buf = keys;
+    t.count = &s_count;
+    t.thr = &s_thr;
+    t.cap = cap;
+    t.k = k;
+    if (threadIdx.x == 0) s_count = n;
+    __syncthreads();
+    topk_flush_mask(t, 1u, kSelectThreads);
+    __syncthreads();
+    if (overflow && !final) {
+        if (threadIdx.x == 0) {
+            thr_key[q] = keys[k - 1];
+            cand_count[q] = 0u;
+            atomicOr(retry, 1u);
+        }
+        return;
+    }
+    if (overflow && threadIdx.x == 0) atomicOr(status, kStatusOverflow);
+    topk_write(t, 0, out_idx + static_cast<size_t>(q) * k, out_scores + static_cast<size_t>(q) * k, kSelectThreads);
+    if (threadIdx.x == 0) done[q] = 1;
+}
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+    static PFN_cuTensorMapEncodeTiled_v12000 fn = [] {
+        void* ptr = nullptr;
+        cudaDriverEntryPointQueryResult qres{};
+        if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &ptr, cudaEnableDefault, &qres) != cudaSuccess ||
+            qres != cudaDriverEntryPointSuccess) {
+            ptr = nullptr;
+        }
+        return reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(ptr);
+    }();
+    return fn;
+}
+
+// 2-D tiled tensor map over a row-major [rows, row_bytes] operand: box = 128 bytes of K by
+// box_rows rows, 128-byte swizzle; rows past the end read as zero.
+int make_map(CUtensorMap* map, const void* base, int mode, long long rows, int row_bytes, int box_rows) {
+    const auto fn = encode_fn();
+    if (fn == nullptr) return fail(ZCGVS_ERR_CUDA, "zcgvs gemm: cuTensorMapEncodeTiled is unavailable");
+    const bool f16 = (mode == kModeF16);
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(f16 ? row_bytes / 2 : row_bytes), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+    const cuuint32_t box[2] = {static_cast<cuuint32_t>(f16 ? kBKBytes / 2 : kBKBytes), static_cast<cuuint32_t>(box_rows)};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(map, f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_UINT8, 2,
+                          const_cast<void*>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                          CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        return fail(ZCGVS_ERR_CUDA, "zcgvs gemm: cuTensorMapEncodeTiled failed (" + std::to_string(static_cast<int>(r)) + ")");
+    }
+    return ZCGVS_OK;
+}
+
+struct GemmLayout {
+    int mode = 0;
+    int kblocks = 0, mtiles = 0, ntiles = 0, sample_tiles = 0;
+    size_t q_bytes = 0;
+    size_t off_q = 0, off_qscale = 0, off_cmax = 0, off_thr = 0, off_count = 0, off_done = 0, off_cand = 0, total = 0;
+};
+
+int plan_gemm(int dtype, long long n, int dim, int batch, int k, GemmLayout& g) {
+    if (dtype == ZCGVS_DTYPE_F16) {
+        g.mode = kModeF16;
+    } else if (dtype == ZCGVS_DTYPE_I8_ROW) {
+        g.mode = kModeI8R;
+    } else {
+        return fail(ZCGVS_ERR_UNSUPPORTED, "zcgvs gemm: the tensor-core scan takes float16 or per-row int8 corpora");
+    }
+    const int row_bytes = static_cast<int>(row_bytes_of(dtype, dim));
+    if (row_bytes % kBKBytes != 0) {
+        return fail(ZCGVS_ERR_UNSUPPORTED, "zcgvs gemm: rows must be a multiple of 128 bytes (dim % " +
+                                               std::to_string(g.mode == kModeF16 ? 64 : 128) + " == 0)");
+    }
+    g.kblocks = row_bytes / kBKBytes;
+    g.mtiles = (batch + kBM - 1) / kBM;
+    g.ntiles = static_cast<int>((n + kBN - 1) / kBN);
+    const long long want = std::max<long long>((k + 3) / 4, (8LL * k * g.ntiles + kCandCap - 1) / kCandCap);
+    g.sample_tiles = static_cast<int>(std::min<long long>(g.ntiles, want));
+    g.q_bytes = static_cast<size_t>(batch) * row_bytes;
+    size_t off = 16;  // status word, retry flag
+    auto take = [&](size_t bytes) {
+        off = round_up(off, kAlign);
+        const size_t at = off;
+        off += bytes;
+        return at;
+    };
+    g.off_q = take(g.q_bytes);
+    g.off_qscale = take(4ull * batch);
+    g.off_cmax = take(4ull * batch * g.sample_tiles * kChunks);
+    g.off_thr = take(8ull * batch);
+    g.off_count = take(4ull * batch);
+    g.off_done = take(4ull * batch);
+    g.off_cand = take(8ull * batch * kCandCap);
+    g.total = round_up(off, kAlign);
+    return ZCGVS_OK;
+}
+
+int stage_count() {
+    const int budget = device_max_smem() - 2048;
+    const int side = 4 * 2 * kBN * 5;  // per epilogue warp and accumulator: row scales + validity
+    const int fixed = 1024 + 8 * (2 * 8 + 5) + side;
+    return std::max(2, std::min(8, (budget - fixed) / kStageBytes));
+}
+
+size_t gemm_smem(int stages) {
+    return 1024 + static_cast<size_t>(stages) * kStageBytes + 8 * (2 * stages + 5) + 4 * 2 * kBN * 5;
+}
+
+using GemmFn = void (*)(const CUtensorMap, const CUtensorMap, const GemmParams);
+
+template <int EPI>
+GemmFn gemm_fn(int mode) {
+    return mode == kModeI8R ? gemm_scan_kernel<kModeI8R, EPI> : gemm_scan_kernel<kModeF16, EPI>;
+}
+
+int launch_gemm(GemmFn fn, const CUtensorMap& mq, const CUtensorMap& mx, GemmParams p, cudaStream_t stream) {
+    cudaError_t e = ensure_smem_optin(reinterpret_cast<const void*>(fn));
+    if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(gemm_scan_kernel)");
+    const long long items = static_cast<long long>(p.mtiles) * p.ntiles;
+    const int grid = static_cast<int>(std::min<long long>(items, device_sm_count()));
+    fn<<<grid, kThreads, gemm_smem(p.stages), stream>>>(mq, mx, p);
+    e = cudaGetLastError();
+    return e == cudaSuccess ? ok() : fail_cuda(e, "gemm_scan_kernel launch");
+}
+
+int prep(const GemmLayout& g, const float* queries, int batch, int dim, uint8_t* ws, cudaStream_t stream) {
+    if (g.mode == kModeI8R) {
+        prep_queries_kernel<kModeI8R><<<batch, 256, 0, stream>>>(queries, dim, ws + g.off_q,
+                                                                reinterpret_cast<float*>(ws + g.off_qscale));
+    } else {
+        prep_queries_kernel<kModeF16><<<batch, 256, 0, stream>>>(queries, dim, ws + g.off_q,
+                                                                reinterpret_cast<float*>(ws + g.off_qscale));
+    }
+    const cudaError_t e = cudaGetLastError();
+    return e == cudaSuccess ? ok() : fail_cuda(e, "prep_queries_kernel launch");
+}
+
+int validate(const void* corpus, int dtype, const float* row_scales, long long n, int dim, const float* queries,
+             int batch, int metric, const void* workspace) {
+    if (corpus == nullptr || queries == nullptr || workspace == nullptr) {
+        return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs gemm: null corpus, query or workspace pointer");
+    }
+    if (n > INT_MAX) return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs gemm: corpus exceeds the supported document count");
+    if (metric == ZCGVS_METRIC_L2) return fail(ZCGVS_ERR_UNSUPPORTED, "zcgvs gemm: the tensor-core scan scores dot/cosine");
+    if (metric != ZCGVS_METRIC_DOT && metric != ZCGVS_METRIC_COSINE) {
+        return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs gemm: unknown metric");
+    }
+    if (dtype == ZCGVS_DTYPE_I8_ROW && row_scales == nullptr) {
+        return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs gemm: the per-row int8 store needs row_scales");
+    }
+    if ((reinterpret_cast<uintptr_t>(corpus) & 15u) != 0 || (reinterpret_cast<uintptr_t>(workspace) & 255u) != 0) {
+        return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs gemm: corpus must be 16-byte and workspace 256-byte aligned");
+    }
+    if (batch > INT_MAX / 2) return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs gemm: batch too large");
+    return ZCGVS_OK;
+}
+
+}  // namespace
+}  // namespace gemm
+}  // namespace zc
+
+extern "C" {
+
+size_t zcgvs_gemm_topk_workspace_bytes(int dtype, int64_t doc_count, int dim, int batch, int k) {
+    if (doc_count <= 0 || dim <= 0 || batch <= 0 || k <= 0) return 0;
+    zc::gemm::GemmLayout g;
+    const size_t bytes = zc::gemm::plan_gemm(dtype, doc_count, dim, batch, std::min(k, ZCGVS_MAX_K), g) == ZCGVS_OK
+                             ? g.total
+                             : 0;
+    zc::ok();
+    return bytes;
+}
+
+int zcgvs_gemm_topk(const void* corpus, int dtype, const float* row_scales, int64_t doc_count, int dim,
+                    const float* queries, int batch, const uint8_t* mask, int metric, int k, int id_base,
+                    int* out_indices, float* out_scores, void* workspace, size_t workspace_bytes, void* stream) {
+    using namespace zc;
+    using namespace zc::gemm;
+    if (doc_count <= 0 || batch <= 0 || dim <= 0) return ok();
+    int status = validate(corpus, dtype, row_scales, doc_count, dim, queries, batch, metric, workspace);
+    if (status != ZCGVS_OK) return status;
+    if (k <= 0 || k > ZCGVS_MAX_K) {
+        return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs gemm: k must be in [1, " + std::to_string(ZCGVS_MAX_K) + "]");
+    }
+    if (k > doc_count) return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs gemm: k exceeds corpus size");
+    if (out_indices == nullptr || out_scores == nullptr) return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs gemm: null output");
+    if (id_base < 0 || static_cast<long long>(id_base) + doc_count - 1 > INT_MAX) {
+        return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs gemm: id_base + doc_count exceeds the int32 id range");
+    }
+    GemmLayout g;
+    status = plan_gemm(dtype, doc_count, dim, batch, k, g);
+    if (status != ZCGVS_OK) return status;
+    if (workspace_bytes < g.total) {
+        return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs gemm: workspace smaller than zcgvs_gemm_topk_workspace_bytes()");
+    }
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int row_bytes = static_cast<int>(row_bytes_of(dtype, dim));
+    CUtensorMap mq, mx;
+    status = make_map(&mq, ws + g.off_q, g.mode, batch, row_bytes, kBM);
+    if (status != ZCGVS_OK) return status;
+    status = make_map(&mx, corpus, g.mode, doc_count, row_bytes, kBN);
+    if (status != ZCGVS_OK) return status;
+    status = prep(g, queries, batch, dim, ws, st);
+    if (status != ZCGVS_OK) return status;
+
+    GemmParams p{};
+    p.n = doc_count;
+    p.batch = batch;
+    p.kblocks = g.kblocks;
+    p.mtiles = g.mtiles;
+    p.id_base = static_cast<unsigned>(id_base);
+    p.qscale = reinterpret_cast<const float*>(ws + g.off_qscale);
+    p.row_scales = row_scales;
+    p.mask = mask;
+    p.chunk_max = reinterpret_cast<float*>(ws + g.off_cmax);
+    p.thr_key = reinterpret_cast<const unsigned long long*>(ws + g.off_thr);
+    p.cand_count = reinterpret_cast<unsigned int*>(ws + g.off_count);
+    p.cand = reinterpret_cast<unsigned long long*>(ws + g.off_cand);
+    p.cand_cap = kCandCap;
+    p.status = reinterpret_cast<unsigned int*>(ws);
+    p.stages = stage_count();
+
+    // Threshold pre-pass over the first sample tiles.
+    GemmParams ps = p;
+    ps.ntiles = g.sample_tiles;
+    ps.n = std::min<long long>(doc_count, static_cast<long long>(g.sample_tiles) * kBN);
+    status = launch_gemm(gemm_fn<kTileMax>(g.mode), mq, mx, ps, st);
+    if (status != ZCGVS_OK) return status;
+    const int chunks = g.sample_tiles * kChunks;
+    const int tcap = next_pow2(std::max(chunks, 2));
+    unsigned long long* thr_key = reinterpret_cast<unsigned long long*>(ws + g.off_thr);
+    int* done = reinterpret_cast<int*>(ws + g.off_done);
+    unsigned int* retry = reinterpret_cast<unsigned int*>(ws + 4);
+    cudaError_t e = ensure_smem_optin(reinterpret_cast<const void*>(threshold_kernel));
+    if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(threshold_kernel)");
+    threshold_kernel<<<batch, kSelectThreads, static_cast<size_t>(tcap) * 8, st>>>(p.chunk_max, chunks, k, tcap,
+                                                                                 thr_key, p.cand_count, done, retry);
+    e = cudaGetLastError();
+    if (e != cudaSuccess) return fail_cuda(e, "threshold_kernel launch");
+    e = ensure_smem_optin(reinterpret_cast<const void*>(select_kernel));
+    if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(select_kernel)");
+
+    // Filter pass over the whole corpus and its selection, then the (usually empty) retry.
+    p.ntiles = g.ntiles;
+    p.done = done;
+    for (int pass = 0; pass < 2; ++pass) {
+        p.retry = pass == 0 ? nullptr : retry;
+        status = launch_gemm(gemm_fn<kFilter>(g.mode), mq, mx, p, st);
+        if (status != ZCGVS_OK) return status;
+        select_kernel<<<batch, kSelectThreads, static_cast<size_t>(kCandCap) * 8, st>>>(
+            p.cand, p.cand_count, kCandCap, k, thr_key, done, retry, p.status, pass, out_indices, out_scores);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return fail_cuda(e, "select_kernel launch");
+    }
+    return ok();
+}
+
+size_t zcgvs_gemm_similarity_workspace_bytes(int dtype, int64_t doc_count, int dim, int batch) {
+    if (doc_count <= 0 || dim <= 0 || batch <= 0) return 0;
+    zc::gemm::GemmLayout g;
+    const size_t bytes = zc::gemm::plan_gemm(dtype, doc_count, dim, batch, 1, g) == ZCGVS_OK
+                             ? zc::round_up(g.off_qscale + 4ull * batch, 256)
+                             : 0;
+    zc::ok();
+    return bytes;
+}
+
+int zcgvs_gemm_similarity(const void* corpus, int dtype, const float* row_scales, int64_t doc_count, int dim,
+                          const float* queries, int batch, const uint8_t* mask, int metric, float* scores,
+                          void* workspace, size_t workspace_bytes, void* stream) {
+    using namespace zc;
+    using namespace zc::gemm;
+    if (doc_count <= 0 || batch <= 0 || dim <= 0) return ok();
+    int status = validate(corpus, dtype, row_scales, doc_count, dim, queries, batch, metric, workspace);
+    if (status != ZCGVS_OK) return status;
+    if (scores == nullptr) return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs gemm: null score pointer");
+    GemmLayout g;
+    status = plan_gemm(dtype, doc_count, dim, batch, 1, g);
+    if (status != ZCGVS_OK) return status;
+    if (workspace_bytes < g.off_qscale + 4ull * batch) {
+        return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs gemm: workspace smaller than zcgvs_gemm_similarity_workspace_bytes()");
+    }
+    uint8_t* ws = static_cast<uint8_t*>(workspace);
+    const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    const int row_bytes = static_cast<int>(row_bytes_of(dtype, dim));
+    CUtensorMap mq, mx;
+    status = make_map(&mq, ws + g.off_q, g.mode, batch, row_bytes, kBM);
+    if (status != ZCGVS_OK) return status;
+    status = make_map(&mx, corpus, g.mode, doc_count, row_bytes, kBN);
+    if (status != ZCGVS_OK) return status;
+    status = prep(g, queries, batch, dim, ws, st);
+    if (status != ZCGVS_OK) return status;
+    GemmParams p{};
+    p.n = doc_count;
+    p.batch = batch;
+    p.kblocks = g.kblocks;
+    p.mtiles = g.mtiles;
+    p.ntiles = g.ntiles;
+    p.qscale = reinterpret_cast<const float*>(ws + g.off_qscale);
+    p.row_scales = row_scales;
+    p.mask = mask;
+    p.out_matrix = scores;
+    p.status = reinterpret_cast<unsigned int*>(ws);
+    p.stages = stage_count();
+    return launch_gemm(gemm_fn<kEmit>(g.mode), mq, mx, p, st);
+}
+
+}  // extern "C"

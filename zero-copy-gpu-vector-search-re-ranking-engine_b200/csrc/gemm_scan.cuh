@@ -1,0 +1,383 @@
+// Tensor-core corpus scan for large query batches (tcgen05 + TMEM + TMA), sm_100a.
+//
+// For a batch of B queries the scan is a dense contraction S = Q . X^T ([B, d] x [d, N]); the
+// reference computes it with one CUDA-core kernel per 8 queries (src/cuda/similarity.cu:83-164)
+// and writes the [B, N] score matrix to HBM before its top-k. Here:
+//
+//   * Work items are (query block m of 128 rows, document tile n of 256 rows); a persistent CTA
+//     walks items m-fastest so the CTAs running at the same time share document tiles in L2.
+//   * Warp 4 (producer) moves 128-byte K slices of the query block (128 x 128 B) and of the
+//     document tile (256 x 128 B) into a ring of shared-memory stages with 2-D TMA loads
+//     (128-byte swizzle, the canonical K-major layout of the tensor-core descriptors).
+//   * Warp 5 (one elected thread) issues tcgen05.mma (kind::f16: fp16 x fp16 -> fp32, or
+//     kind::i8: int8 x int8 -> int32, both operands K-major) into one of two 128 x 256 fp32/int32
+//     accumulators in tensor memory, and commits each stage back to the producer and each
+//     finished accumulator to the epilogue through mbarriers.
+//   * Warps 0-3 (epilogue) read the accumulator with tcgen05.ld (warp w owns TMEM lanes
+//     32w..32w+31, i.e. query rows) while the next item's MMAs run in the other accumulator,
+//     and either write the scores (EMIT), reduce each query's maximum over the tile (TILE_MAX,
+//     the threshold pre-pass) or keep only scores at or above a per-query threshold (FILTER),
+//     appending them as 64-bit selection keys to a per-query candidate buffer.
+//
+// Every mbarrier wait is bounded; on a timeout the kernel records a status bit, stops issuing,
+// waits (bounded) for its own copies and MMAs in flight, frees its tensor memory and returns.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_fp16.h>
+
+#include "common.cuh"
+
+namespace zc {
+
+namespace gemm {
+
+constexpr int kBM = 128;                  // query rows per item (TMEM lanes)
+constexpr int kBN = 256;                  // document rows per item (TMEM columns)
+constexpr int kBKBytes = 128;             // one 128-byte swizzle row of K per stage
+constexpr int kStageA = kBM * kBKBytes;   // 16 KB
+constexpr int kStageB = kBN * kBKBytes;   // 32 KB
+constexpr int kStageBytes = kStageA + kStageB;
+constexpr int kThreads = 192;             // warps 0-3 epilogue, 4 producer, 5 MMA
+constexpr int kEpiThreads = 128;
+constexpr int kProducerWarp = 4;
+constexpr int kMmaWarp = 5;
+constexpr int kTmemCols = 512;            // two 256-column accumulators
+constexpr int kChunks = kBN / 32;         // threshold granularity: 32-document chunks per tile
+
+enum Epilogue : int { kEmit = 0, kTileMax = 1, kFilter = 2 };
+
+constexpr uint32_t kStatusTmemWait = 4u;    // an accumulator hand-off wait ran out
+constexpr uint32_t kStatusOverflow = 8u;    // a candidate buffer overflowed
+
+struct GemmParams {
+    long long n;                 // documents
+    int batch;                   // queries
+    int kblocks;                 // d * elem_bytes / 128
+    int mtiles, ntiles;          // items = mtiles * ntiles
+    unsigned id_base;
+    const float* qscale;         // I8R: [batch]
+    const float* row_scales;     // I8R: [n]
+    const uint8_t* mask;         // optional [n]
+    float* out_matrix;           // kEmit: [batch][n]
+    float* chunk_max;            // kTileMax: [batch][ntiles * kChunks] maxima of 32-column chunks
+    const unsigned long long* thr_key;  // kFilter: [batch] key thresholds (0 = keep everything)
+    const int* done;             // kFilter: [batch] queries already answered (skipped), or nullptr
+    const unsigned int* retry;   // kFilter: run only when *retry != 0 (nullptr = always)
+    unsigned int* cand_count;    // kFilter: [batch]
+    unsigned long long* cand;    // kFilter: [batch][cand_cap]
+    int cand_cap;
+    unsigned int* status;
+    int stages;
+};
+
+__device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t smem_addr) {
+    // K-major, 128-byte swizzle: 8-row core groups 1024 bytes apart (SBO = 64 x 16 B), leading
+    // offset unused (1), descriptor version 1 (sm_100), base offset 0 (stages are 1024-aligned).
+    return static_cast<uint64_t>((smem_addr >> 4) & 0x3FFFu) | (static_cast<uint64_t>(1) << 16) |
+           (static_cast<uint64_t>(64) << 32) | (static_cast<uint64_t>(1) << 46) | (static_cast<uint64_t>(2) << 61);
+}
+
+// Instruction descriptor: D format (1 = f32, 2 = s32), A/B formats, K-major operands,
+// N >> 3 at bit 17, M >> 4 at bit 24.
+template <int MODE>
+__device__ __forceinline__ constexpr uint32_t instr_desc() {
+    return MODE == kModeI8R ? ((2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kBN >> 3) << 17) |
+                               (static_cast<uint32_t>(kBM >> 4) << 24))
+                            : ((1u << 4) | (static_cast<uint32_t>(kBN >> 3) << 17) |
+                               (static_cast<uint32_t>(kBM >> 4) << 24));
+}
+
+template <int MODE>
+__device__ __forceinline__ void mma_issue(uint32_t tmem_d, uint64_t a_desc, uint64_t b_desc, uint32_t accumulate) {
+    constexpr uint32_t idesc = instr_desc<MODE>();
+    if constexpr (MODE == kModeI8R) {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+            "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+    } else {
+        asm volatile(
+            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
+            "tcgen05.mma.cta_group::1.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
+            "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
+    }
+}
+
+__device__ __forceinline__ void mma_commit(u64* bar) {
+    asm volatile("tcgen05.commit.cta_group::1.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(smem_u32(bar))
+                 : "memory");
+}
+
+__device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
+__device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
+
+__device__ __forceinline__ void tmem_ld32(uint32_t taddr, uint32_t (&v)[32]) {
+    asm volatile(
+        "tcgen05.ld.sync.aligned.32x32b.x32.b32 {%0, %1, %2, %3, %4, %5, %6, %7, %8, %9, %10, %11, %12, %13, %14, "
+        "%15, %16, %17, %18, %19, %20, %21, %22, %23, %24, %25, %26, %27, %28, %29, %30, %31}, [%32];"
+        : "=r"(v[0]), "=r"(v[1]), "=r"(v[2]), "=r"(v[3]), "=r"(v[4]), "=r"(v[5]), "=r"(v[6]), "=r"(v[7]), "=r"(v[8]),
+          "=r"(v[9]), "=r"(v[10]), "=r"(v[11]), "=r"(v[12]), "=r"(v[13]), "=r"(v[14]), "=r"(v[15]), "=r"(v[16]),
+          "=r"(v[17]), "=r"(v[18]), "=r"(v[19]), "=r"(v[20]), "=r"(v[21]), "=r"(v[22]), "=r"(v[23]), "=r"(v[24]),
+          "=r"(v[25]), "=r"(v[26]), "=r"(v[27]), "=r"(v[28]), "=r"(v[29]), "=r"(v[30]), "=r"(v[31])
+        : "r"(taddr));
+    asm volatile("tcgen05.wait::ld.sync.aligned;" ::: "memory");
+}
+
+__device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* map, int x, int y, u64* bar) {
+    asm volatile(
+        "cp.async.bulk.tensor.2d.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], [%4];" ::"r"(
+            smem_u32(smem_dst)),
+        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(smem_u32(bar))
+        : "memory");
+}
+
+template <int MODE, int EPI>
+__global__ void __launch_bounds__(kThreads, 1)
+    gemm_scan_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_x,
+                     const GemmParams p) {
+    extern __shared__ __align__(1024) uint8_t smem_raw[];
+    // Stage ring first, 1024-aligned (the swizzle pattern and base offset 0 assume it).
+    uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
+    const int S = p.stages;
+    u64* full = reinterpret_cast<u64*>(smem + static_cast<size_t>(S) * kStageBytes);
+    u64* empty = full + S;
+    u64* acc_full = empty + S;        // [2]
+    u64* acc_empty = acc_full + 2;    // [2]
+    u64* drain = acc_empty + 2;       // [1]
+    // Per epilogue warp and accumulator: the tile's row scales and validity bytes.
+    float* side = reinterpret_cast<float*>(drain + 1);                    // [4][2][kBN]
+    uint8_t* side_mask = reinterpret_cast<uint8_t*>(side + 4 * 2 * kBN);  // [4][2][kBN]
+    __shared__ uint32_t s_tmem;
+    __shared__ int s_abort;
+
+    const int tid = threadIdx.x;
+    const int warp = tid >> 5;
+    const int lane = tid & 31;
+    // A retry pass with nothing to retry returns before allocating anything.
+    if (EPI == kFilter && p.retry != nullptr && *reinterpret_cast<const volatile unsigned int*>(p.retry) == 0u) return;
+    const long long items = static_cast<long long>(p.mtiles) * p.ntiles;
+
+    if (tid == 0) {
+        for (int s = 0; s < S; ++s) {
+            mbar_init(&full[s], 1);
+            mbar_init(&empty[s], 1);
+        }
+        for (int a = 0; a < 2; ++a) {
+            mbar_init(&acc_full[a], 1);
+            mbar_init(&acc_empty[a], 4);
+        }
+        mbar_init(drain, 1);
+        fence_mbarrier_init();
+        s_abort = 0;
+    }
+    if (warp == kMmaWarp) {
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
+    }
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    const uint32_t tmem_base = s_tmem;
+    volatile int* abort_flag = &s_abort;
+
+    if (warp == kProducerWarp) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t phase = 0;
+            long long issued = 0;
+            bool ok = true;
+            for (long long w = blockIdx.x; w < items && ok; w += gridDim.x) {
+                const int m = static_cast<int>(w % p.mtiles);
+                const int n = static_cast<int>(w / p.mtiles);
+                for (int kb = 0; kb < p.kblocks; ++kb) {
+                    if (issued >= S) {
+                        ok = !*abort_flag && mbar_wait_bounded(&empty[s], phase ^ 1u, p.status, kStatusTileWaitTimeout);
+                        if (!ok) {
+                            *abort_flag = 1;
+                            break;
+                        }
+                    }
+                    uint8_t* st = smem + static_cast<size_t>(s) * kStageBytes;
+                    mbar_arrive_expect_tx(&full[s], kStageBytes);
+                    tma_load_2d(st, &map_q, kb * (kBKBytes / (MODE == kModeI8R ? 1 : 2)), m * kBM, &full[s]);
+                    tma_load_2d(st + kStageA, &map_x, kb * (kBKBytes / (MODE == kModeI8R ? 1 : 2)), n * kBN, &full[s]);
+                    ++issued;
+                    if (++s == S) {
+                        s = 0;
+                        phase ^= 1u;
+                    }
+                }
+            }
+            // Wait (bounded) for the copies still in flight before the CTA can retire.
+            if (*abort_flag) {
+                for (long long i = issued > S ? issued - S : 0; i < issued; ++i) {
+                    mbar_wait_bounded(&full[i % S], static_cast<uint32_t>((i / S) & 1), p.status, kStatusDrainTimeout);
+                }
+            }
+        }
+    } else if (warp == kMmaWarp) {
+        if (lane == 0) {
+            int s = 0;
+            uint32_t phase = 0;
+            long long local = 0;
+            bool ok = true;
+            for (long long w = blockIdx.x; w < items && ok; w += gridDim.x, ++local) {
+                const int a = static_cast<int>(local & 1);
+                if (local >= 2) {
+                    ok = !*abort_flag &&
+                         mbar_wait_bounded(&acc_empty[a], static_cast<uint32_t>(((local >> 1) - 1) & 1), p.status,
+                                           kStatusTmemWait);
+                    if (!ok) {
+                        *abort_flag = 1;
+                        break;
+                    }
+                }
+                tc_fence_after();
+                const uint32_t tmem_d = tmem_base + static_cast<uint32_t>(a * kBN);
+                for (int kb = 0; kb < p.kblocks; ++kb) {
+                    ok = !*abort_flag && mbar_wait_bounded(&full[s], phase, p.status, kStatusTileWaitTimeout);
+                    if (!ok) {
+                        *abort_flag = 1;
+                        break;
+                    }
+                    tc_fence_after();
+                    const uint32_t a_addr = smem_u32(smem + static_cast<size_t>(s) * kStageBytes);
+                    const uint32_t b_addr = a_addr + kStageA;
+                    const uint64_t a_desc = smem_desc_sw128(a_addr);
+                    const uint64_t b_desc = smem_desc_sw128(b_addr);
+#pragma unroll
+                    for (int kk = 0; kk < kBKBytes / 32; ++kk) {
+                        // Each MMA consumes 32 bytes of K (16 fp16 or 32 int8): advance both start
+                        // addresses by 32 bytes (2 units of 16 B) inside the swizzled row.
+                        mma_issue<MODE>(tmem_d, a_desc + static_cast<uint64_t>(2 * kk),
+                                        b_desc + static_cast<uint64_t>(2 * kk), (kb > 0 || kk > 0) ? 1u : 0u);
+                    }
+                    mma_commit(&empty[s]);  // frees the stage when these MMAs have read it
+                    if (++s == S) {
+                        s = 0;
+                        phase ^= 1u;
+                    }
+                }
+                if (!ok) break;
+                mma_commit(&acc_full[a]);  // accumulator a is complete
+            }
+            // Make sure no MMA is in flight before the tensor memory is released.
+            mma_commit(drain);
+            mbar_wait_bounded(drain, 0u, p.status, kStatusDrainTimeout);
+        }
+    } else {
+        // ---------------- epilogue warps 0-3 ----------------
+        const int row = warp * 32 + lane;  // TMEM lane = query row within the block
+        long long local = 0;
+        for (long long w = blockIdx.x; w < items; w += gridDim.x, ++local) {
+            const int m = static_cast<int>(w % p.mtiles);
+            const int n = static_cast<int>(w / p.mtiles);
+            const int a = static_cast<int>(local & 1);
+            const int q = m * kBM + row;
+            const bool q_ok = q < p.batch;
+            const long long doc0 = static_cast<long long>(n) * kBN;
+            // This warp's copy of the tile's per-document side data (row scales, validity), so
+            // the epilogue warps never wait on one another.
+            float* scales = side + (warp * 2 + a) * kBN;
+            uint8_t* mk = side_mask + (warp * 2 + a) * kBN;
+            for (int j = lane; j < kBN; j += 32) {
+                const long long d = doc0 + j;
+                if constexpr (MODE == kModeI8R) scales[j] = d < p.n ? __ldg(p.row_scales + d) : 0.0f;
+                mk[j] = (d < p.n && (p.mask == nullptr || __ldg(p.mask + d) != 0)) ? 1 : 0;
+            }
+            __syncwarp();
+            bool ok = true;
+            if (lane == 0) {
+                ok = !*abort_flag && mbar_wait_bounded(&acc_full[a], static_cast<uint32_t>((local >> 1) & 1), p.status,
+                                                       kStatusTmemWait);
+                if (!ok) *abort_flag = 1;
+            }
+            ok = __shfl_sync(0xffffffffu, ok ? 1 : 0, 0) != 0;
+            if (!ok) break;
+            tc_fence_after();
+            float qs = 1.0f, thr = INFINITY;
+            unsigned long long thr_key = ~0ull;
+            bool live = q_ok;
+            if (q_ok) {
+                if constexpr (MODE == kModeI8R) qs = __ldg(p.qscale + q);
+                if constexpr (EPI == kFilter) {
+                    live = p.done == nullptr || p.done[q] == 0;
+                    thr_key = p.thr_key[q];
+                    thr = thr_key == 0ull ? -INFINITY : score_from_bits(static_cast<uint32_t>(thr_key >> 32));
+                }
+            }
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(a * kBN);
+#pragma unroll 1
+            for (int c = 0; c < kBN / 32; ++c) {
+                uint32_t v[32];
+                __syncwarp();  // tcgen05.ld is warp-collective; the append branch below diverges
+                tmem_ld32(taddr + static_cast<uint32_t>(c * 32), v);
+                float sc[32];
+#pragma unroll
+                for (int j = 0; j < 32; ++j) {
+                    const int col = c * 32 + j;
+                    float score;
+                    if constexpr (MODE == kModeI8R) {
+                        score = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(v[j])), qs), scales[col]);
+                    } else {
+                        score = __uint_as_float(v[j]);
+                    }
+                    sc[j] = mk[col] ? score : -INFINITY;  // invalid (padding / masked) documents
+                }
+                if constexpr (EPI == kEmit) {
+                    if (q_ok) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            const long long d = doc0 + c * 32 + j;
+                            if (d < p.n) {
+                                const bool allowed = p.mask == nullptr || __ldg(p.mask + d) != 0;
+                                p.out_matrix[static_cast<size_t>(q) * p.n + d] = allowed ? sc[j] : -FLT_MAX;
+                            }
+                        }
+                    }
+                } else if constexpr (EPI == kTileMax) {
+                    float best = -INFINITY;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) best = fmaxf(best, sc[j]);
+                    if (q_ok) p.chunk_max[(static_cast<size_t>(q) * p.ntiles + n) * kChunks + c] = best;
+                } else {
+                    float best = -INFINITY;
+#pragma unroll
+                    for (int j = 0; j < 32; ++j) best = fmaxf(best, sc[j]);
+                    if (live && best >= thr && best > -INFINITY) {
+#pragma unroll 1
+                        for (int j = 0; j < 32; ++j) {
+                            if (sc[j] >= thr && sc[j] > -INFINITY) {
+                                const unsigned long long key =
+                                    make_key(sc[j], p.id_base + static_cast<unsigned>(doc0 + c * 32 + j));
+                                if (key < thr_key) continue;
+                                const unsigned int slot = atomicAdd(p.cand_count + q, 1u);
+                                if (slot < static_cast<unsigned int>(p.cand_cap)) {
+                                    p.cand[static_cast<size_t>(q) * p.cand_cap + slot] = key;
+                                }
+                            }
+                        }
+                    }
+                }
+            }
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive_cta(&acc_empty[a]);
+        }
+    }
+
+    tc_fence_before();
+    __syncthreads();
+    tc_fence_after();
+    if (warp == kMmaWarp) {
+        __syncwarp();
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
+                     : "memory");
+    }
+}
+
+}  // namespace gemm
+}  // namespace zc

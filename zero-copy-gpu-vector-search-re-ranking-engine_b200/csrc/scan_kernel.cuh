@@ -30,8 +30,6 @@
 
 namespace zc {
 
-enum ScanMode : int { kModeF32 = 0, kModeF16 = 1, kModeI8M = 2, kModeBin = 3, kModeI8R = 4 };
-
 constexpr int kScanThreads = 512;
 constexpr int kScanWarps = kScanThreads / 32;
 

@@ -40,6 +40,10 @@ SIGNATURES = {
                                   _P, _P, _P]),
     "zcgvs_gather_rescore": (_i32, [_P, _i32, _f32, _P, _i64, _i32, _P, _i32, _P, _i32, _i32, _P,
                                     _P]),
+    "zcgvs_gemm_topk_workspace_bytes": (_sz, [_i32, _i64, _i32, _i32, _i32]),
+    "zcgvs_gemm_topk": (_i32, [_P, _i32, _P, _i64, _i32, _P, _i32, _P, _i32, _i32, _i32, _P, _P, _P, _sz, _P]),
+    "zcgvs_gemm_similarity_workspace_bytes": (_sz, [_i32, _i64, _i32, _i32]),
+    "zcgvs_gemm_similarity": (_i32, [_P, _i32, _P, _i64, _i32, _P, _i32, _P, _i32, _P, _P, _sz, _P]),
     "zcgvs_merge_topk": (_i32, [_P, _P, _i32, _i32, _i32, _i32, _P, _P, _P]),
     "zcgvs_hybrid_topk_workspace_bytes": (_sz, [_i32, _i64, _i32, _i32, _i32]),
     "zcgvs_hybrid_topk": (_i32, [_P, _i32, _f32, _P, _i64, _i32, _P, _i32, _P, _i32, _P, _P, _P, _i32,
@@ -284,4 +288,43 @@ def merge_topk(list_indices, list_scores, k: int, out=None, stream=None):
                torch.empty((batch, k), dtype=torch.float32, device=list_indices.device))
     check(lib().zcgvs_merge_topk(_ptr(list_indices), _ptr(list_scores), lists, batch, k_in, k, _ptr(out[0]),
                                  _ptr(out[1]), _stream(stream)))
+    return out
+
+
+def gemm_topk(corpus, dtype: int, dim: int, queries, k: int, *, row_scales=None, mask=None,
+              metric: int = METRIC_DOT, id_base: int = 0, workspace: Workspace | None = None, out=None,
+              stream=None):
+    """Tensor-core batched top-k (F16 or I8_ROW corpora). Returns (ids [B, k], scores [B, k])."""
+    import torch
+
+    doc_count = corpus.shape[0]
+    queries = queries.reshape(-1, dim)
+    batch = queries.shape[0]
+    if out is None:
+        out = (torch.empty((batch, k), dtype=torch.int32, device=queries.device),
+               torch.empty((batch, k), dtype=torch.float32, device=queries.device))
+    ws = workspace or Workspace(queries.device)
+    nbytes = int(lib().zcgvs_gemm_topk_workspace_bytes(dtype, doc_count, dim, batch, k))
+    buf = ws.get(nbytes, stream)
+    check(lib().zcgvs_gemm_topk(_ptr(corpus), dtype, _ptr(row_scales), doc_count, dim, _ptr(queries), batch,
+                                _ptr(mask), metric, k, id_base, _ptr(out[0]), _ptr(out[1]), _ptr(buf), buf.numel(),
+                                _stream(stream)))
+    return out
+
+
+def gemm_similarity(corpus, dtype: int, dim: int, queries, *, row_scales=None, mask=None, metric: int = METRIC_DOT,
+                    workspace: Workspace | None = None, out=None, stream=None):
+    """Tensor-core score matrix [B, N]."""
+    import torch
+
+    doc_count = corpus.shape[0]
+    queries = queries.reshape(-1, dim)
+    batch = queries.shape[0]
+    if out is None:
+        out = torch.empty((batch, doc_count), dtype=torch.float32, device=queries.device)
+    ws = workspace or Workspace(queries.device)
+    nbytes = int(lib().zcgvs_gemm_similarity_workspace_bytes(dtype, doc_count, dim, batch))
+    buf = ws.get(nbytes, stream)
+    check(lib().zcgvs_gemm_similarity(_ptr(corpus), dtype, _ptr(row_scales), doc_count, dim, _ptr(queries), batch,
+                                      _ptr(mask), metric, _ptr(out), _ptr(buf), buf.numel(), _stream(stream)))
     return out
