@@ -151,3 +151,27 @@ def test_gemm_topk_overflow_retry_is_exact(zc, orc):
     np.testing.assert_array_equal(idx.cpu().numpy(), ref_i)
     np.testing.assert_array_equal(val.cpu().numpy(), ref_v)
     assert ws.status() == 0
+
+
+def test_gemm_topk_statistical_bound_fallback_is_exact(zc, orc):
+    """The threshold sample (the first tiles) holds 20 documents far above the rest, one per
+    chunk: the statistical bound (16th chunk maximum) lets only those 20 through (< k), the safe
+    bound keeps every document (fewer sample chunks than k) and overflows the candidate buffer,
+    and the raised bound of the second retry must still return the exact top-k."""
+    import torch
+
+    n, dim, batch, k = 40000, 128, 3, 100
+    rng = np.random.default_rng(9)
+    storage = rng.integers(-20, 21, size=(n, dim), dtype=np.int8)
+    v = rng.integers(60, 127, size=dim).astype(np.int8)
+    for i in range(20):
+        storage[32 * i] = v
+    row_scales = np.full(n, 0.01, dtype=np.float32)
+    queries = np.tile(v.astype(np.float32) / 127.0, (batch, 1))
+    ws = zc.Workspace()
+    idx, val = zc.gemm_topk(dev(storage), 4, dim, dev(queries), k, row_scales=dev(row_scales), workspace=ws)
+    torch.cuda.synchronize()
+    ref_i, ref_v = orc.scan_topk(storage, 4, dim, queries, k, row_scales=row_scales)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ref_i)
+    np.testing.assert_array_equal(val.cpu().numpy(), ref_v)
+    assert ws.status() == 0

@@ -1,22 +1,27 @@
 // Host side and helper kernels of the tensor-core batched search (gemm_scan.cuh).
 //
-// zcgvs_gemm_topk runs four kernels on one stream, all on the caller's workspace:
+// zcgvs_gemm_topk runs these kernels on one stream, all on the caller's workspace:
 //   1. prep      : queries -> fp16 (ZCGVS_DTYPE_F16) or per-row int8 + scale (ZCGVS_DTYPE_I8_ROW,
 //                  the quantiser of the streaming scan) in the layout the TMA loads read.
-//   2. tile max  : the tensor-core scan over the first T document tiles, writing each query's
-//                  maximum score per tile.
-//   3. threshold : per query, thr = the k-th largest of the sample's 32-document chunk maxima.
-//                  k chunks each hold a document scoring >= thr, so at least k documents do:
-//                  every member of the exact top-k scores >= thr. Also clears the counters.
-//   4. filter    : the tensor-core scan over all tiles, appending every document whose key
-//                  (score, id) is >= the query's threshold key to its candidate buffer.
+//   2. sample    : the tensor-core scan over the first T document tiles, writing each query's
+//                  maximum score per 32-document chunk.
+//   3. threshold : per query, from those chunk maxima: the safe bound, the k-th largest (k
+//                  chunks each hold a document scoring >= it, so every member of the exact top-k
+//                  scores >= it), and a tighter statistical bound, the 16th largest, which a
+//                  sample of T = 16 / E of the tiles places so that about E documents of the whole
+//                  corpus pass it. The filter starts with the tighter of the two.
+//   4. filter    : the tensor-core scan over all tiles; every document whose key (score, id) is
+//                  >= its query's threshold key goes to the CTA's mailbox (a shared-memory
+//                  reservation and plain stores: the epilogue never waits on a global atomic).
+//      bucket    : mailbox entries -> per-query candidate buffers (parallel global atomics).
 //   5. select    : per query, the exact (score desc, id asc) top-k of its candidates.
-//   6. retry     : a query whose candidates overflowed the buffer (capacity C) raises its
-//                  threshold key to the k-th largest key it did capture (any k captured
-//                  documents bound the k-th best from below) and runs the filter and select
-//                  again; both retry kernels return at once when no query overflowed, so the
-//                  launch sequence is fixed (capturable in a CUDA graph).
-// T = max(k / 4, 8 k N_tiles / C) tiles keeps the expected candidate count well under C.
+//   6. retry     : the result of a query is exact when at least k candidates passed a bound and
+//                  none were lost. Otherwise the query is scanned again: with the safe bound when
+//                  a statistical bound let fewer than k through, or with its threshold raised to
+//                  the k-th largest key it did capture (k captured documents bound the k-th best
+//                  from below) when its candidates overflowed a buffer. The retry scans only the
+//                  query blocks holding such a query and returns at once when there is none, so
+//                  the launch sequence is fixed (capturable in a CUDA graph).
 #include <cuda.h>
 #include <cudaTypedefs.h>
 #include <cuda_runtime.h>
@@ -37,6 +42,8 @@ namespace gemm {
 namespace {
 
 constexpr int kCandCap = 16384;
+constexpr int kStatRank = 16;  // rank of the statistical threshold among the sample's chunk maxima
+constexpr int kPasses = 3;     // the filter pass and up to two retries
 constexpr int kSelectThreads = 512;
 constexpr size_t kAlign = 256;
 
@@ -78,8 +85,10 @@ __global__ void prep_queries_kernel(const float* __restrict__ queries, int dim, 
 // block 0 clears the retry flag.
 __global__ void __launch_bounds__(kSelectThreads) threshold_kernel(const float* __restrict__ chunk_max, int chunks,
                                                                    int k, int cap, unsigned long long* thr_key,
+                                                                   unsigned long long* thr_safe,
                                                                    unsigned int* cand_count, int* done,
-                                                                   unsigned int* retry) {
+                                                                   unsigned int* retry, unsigned int* mneed,
+                                                                   int mtiles) {
     extern __shared__ __align__(16) u64 keys[];
     __shared__ int s_count;
     __shared__ u64 s_thr;
@@ -92,37 +101,68 @@ __global__ void __launch_bounds__(kSelectThreads) threshold_kernel(const float* 
     t.count = &s_count;
     t.thr = &s_thr;
     t.cap = cap;
-    t.k = k;
+    t.k = max(k, kStatRank);
     if (threadIdx.x == 0) s_count = chunks;
     __syncthreads();
     topk_flush_mask(t, 1u, kSelectThreads);
     __syncthreads();
     if (threadIdx.x == 0) {
-        // keys[k - 1] exists only when there are at least k chunks (the buffer holds cap >= chunks).
-        const float score = chunks >= k ? key_score(keys[k - 1]) : -INFINITY;
-        thr_key[q] = score > -INFINITY ? (static_cast<u64>(orderable_bits(score)) << 32) : 0ull;
+        // keys[r - 1] exists only when there are at least r chunks (the buffer holds cap >= chunks).
+        auto bound = [&](int r) {
+            const float score = chunks >= r ? key_score(keys[r - 1]) : -INFINITY;
+            return score > -INFINITY ? (static_cast<u64>(orderable_bits(score)) << 32) : 0ull;
+        };
+        const u64 safe = bound(k);
+        thr_safe[q] = safe;
+        thr_key[q] = kStatRank < k ? max(bound(kStatRank), safe) : safe;
+        if (q < mtiles) {
+            for (int i = 0; i < kPasses; ++i) mneed[i * mtiles + q] = 0u;
+        }
         cand_count[q] = 0u;
         done[q] = 0;
-        if (q == 0) *retry = 0u;
+        if (q == 0) {
+            for (int i = 0; i < 2 * kPasses; ++i) retry[i] = 0u;  // retry requests, mailbox overflows
+        }
     }
 }
 
-// The exact top-k of each query's candidates. A query whose buffer overflowed keeps no result:
-// on the first pass (final == 0) its threshold key rises to the k-th largest key it captured,
-// its counter is cleared and the retry flag is set; on the retry pass (final == 1) it writes what
-// it has and records the overflow in the status word. Queries already answered are skipped.
+// Moves the mailbox entries of every filter CTA (blockIdx.y) into per-query candidate buffers.
+// On a retry pass (retry != nullptr) it runs only when some query is being retried.
+__global__ void bucket_kernel(const unsigned long long* __restrict__ mb_key, const unsigned int* __restrict__ mb_query,
+                              const unsigned int* __restrict__ mb_count, int mb_cap, unsigned int* cand_count,
+                              unsigned long long* cand, int cap, const unsigned int* retry) {
+    if (retry != nullptr && *reinterpret_cast<const volatile unsigned int*>(retry) == 0u) return;
+    const int c = blockIdx.y;
+    const unsigned int n = mb_count[c];
+    const size_t base = static_cast<size_t>(c) * mb_cap;
+    for (unsigned int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        const unsigned int q = mb_query[base + i];
+        const unsigned int slot = atomicAdd(cand_count + q, 1u);
+        if (slot < static_cast<unsigned int>(cap)) cand[static_cast<size_t>(q) * cap + slot] = mb_key[base + i];
+    }
+}
+
+// The exact top-k of each query's candidates after filter pass `pass`. flags[i] (i < kPasses)
+// requests retry pass i, flags[kPasses + i] records a mailbox overflow in pass i; mneed[i] lists
+// the query blocks retry pass i scans. A query is answered when at least k candidates passed
+// its bound and none were lost, or on the last pass (then an overflow is recorded in the status
+// word). Otherwise it asks for the next pass with the safe bound (a statistical bound let fewer
+// than k through) or a raised bound (the k-th largest key it captured, after an overflow).
 __global__ void __launch_bounds__(kSelectThreads) select_kernel(const unsigned long long* __restrict__ cand,
                                                                 unsigned int* cand_count, int cap, int k,
-                                                                unsigned long long* thr_key, int* done,
-                                                                unsigned int* retry, unsigned int* status, int final,
-                                                                int* out_idx, float* out_scores) {
+                                                                unsigned long long* thr_key,
+                                                                const unsigned long long* thr_safe, int* done,
+                                                                unsigned int* flags, unsigned int* mneed, int mtiles,
+                                                                unsigned int* status, int pass, int* out_idx,
+                                                                float* out_scores) {
     extern __shared__ __align__(16) u64 keys[];
     __shared__ int s_count;
     __shared__ u64 s_thr;
     const int q = blockIdx.x;
-    if (final && (*reinterpret_cast<const volatile unsigned int*>(retry) == 0u || done[q])) return;
+    if (pass > 0 && (*reinterpret_cast<const volatile unsigned int*>(flags + pass) == 0u || done[q])) return;
+    const bool final = pass == kPasses - 1;
     const unsigned int total = cand_count[q];
-    const bool overflow = total > static_cast<unsigned int>(cap);
+    const bool overflow = total > static_cast<unsigned int>(cap) || flags[kPasses + pass] != 0u;
     const int n = static_cast<int>(overflow ? static_cast<unsigned int>(cap) : total);
     const int size = n < 2 ? 2 : 1 << (32 - __clz(n - 1));
     for (int i = threadIdx.x; i < size; i += kSelectThreads) {
@@ -138,15 +178,21 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(const unsigned l
     __syncthreads();
     topk_flush_mask(t, 1u, kSelectThreads);
     __syncthreads();
-    if (overflow && !final) {
+    const bool short_list = !overflow && n < k && thr_key[q] != thr_safe[q];
+    if ((overflow || short_list) && !final) {
         if (threadIdx.x == 0) {
-            thr_key[q] = keys[k - 1];
+            if (short_list) {
+                thr_key[q] = thr_safe[q];
+            } else if (n >= k) {
+                thr_key[q] = keys[k - 1];  // k captured documents bound the k-th best
+            }
             cand_count[q] = 0u;
-            atomicOr(retry, 1u);
+            mneed[(pass + 1) * mtiles + q / kBM] = 1u;
+            atomicOr(flags + pass + 1, 1u);
         }
         return;
     }
-    if (overflow && threadIdx.x == 0) atomicOr(status, kStatusOverflow);
+    if ((overflow || short_list) && threadIdx.x == 0) atomicOr(status, kStatusOverflow);
     topk_write(t, 0, out_idx + static_cast<size_t>(q) * k, out_scores + static_cast<size_t>(q) * k, kSelectThreads);
     if (threadIdx.x == 0) done[q] = 1;
 }
@@ -188,7 +234,10 @@ struct GemmLayout {
     int mode = 0;
     int kblocks = 0, mtiles = 0, ntiles = 0, sample_tiles = 0;
     size_t q_bytes = 0;
-    size_t off_q = 0, off_qscale = 0, off_cmax = 0, off_thr = 0, off_count = 0, off_done = 0, off_cand = 0, total = 0;
+    size_t off_q = 0, off_qscale = 0, off_cmax = 0, off_thr = 0, off_count = 0, off_done = 0, off_cand = 0;
+    size_t off_mb_key = 0, off_mb_query = 0, off_mb_count = 0, total = 0;
+    int mb_cap = 0, mb_ctas = 0, expected = 0;
+    size_t off_thr_safe = 0, off_mneed = 0;
 };
 
 int plan_gemm(int dtype, long long n, int dim, int batch, int k, GemmLayout& g) {
@@ -207,10 +256,13 @@ int plan_gemm(int dtype, long long n, int dim, int batch, int k, GemmLayout& g) 
     g.kblocks = row_bytes / kBKBytes;
     g.mtiles = (batch + kBM - 1) / kBM;
     g.ntiles = static_cast<int>((n + kBN - 1) / kBN);
-    const long long want = std::max<long long>((k + 3) / 4, (8LL * k * g.ntiles + kCandCap - 1) / kCandCap);
-    g.sample_tiles = static_cast<int>(std::min<long long>(g.ntiles, want));
+    // Expected candidates per query E; the statistical bound (rank 16) needs a sample of 16 / E
+    // of the tiles for about E documents of the corpus to pass it.
+    g.expected = std::min(4096, std::max(1024, 8 * k));
+    const long long want = (static_cast<long long>(g.ntiles) * kStatRank + g.expected - 1) / g.expected;
+    g.sample_tiles = static_cast<int>(std::max<long long>(1, std::min<long long>(g.ntiles, want)));
     g.q_bytes = static_cast<size_t>(batch) * row_bytes;
-    size_t off = 16;  // status word, retry flag
+    size_t off = 16 + 8 * kPasses;  // status word, per-pass retry and overflow flags
     auto take = [&](size_t bytes) {
         off = round_up(off, kAlign);
         const size_t at = off;
@@ -221,9 +273,29 @@ int plan_gemm(int dtype, long long n, int dim, int batch, int k, GemmLayout& g) 
     g.off_qscale = take(4ull * batch);
     g.off_cmax = take(4ull * batch * g.sample_tiles * kChunks);
     g.off_thr = take(8ull * batch);
+    g.off_thr_safe = take(8ull * batch);
+    g.off_mneed = take(4ull * kPasses * g.mtiles);
     g.off_count = take(4ull * batch);
     g.off_done = take(4ull * batch);
     g.off_cand = take(8ull * batch * kCandCap);
+    // Mailboxes: 4x the candidates one filter CTA is expected to produce, never more than its
+    // items can produce at all. A query keeps about k * tiles / sample tiles documents (every
+    // document when the sample has fewer than k chunks).
+    g.mb_ctas = device_sm_count();
+    const long long items = static_cast<long long>(g.mtiles) * g.ntiles;
+    const long long per_cta = (items + g.mb_ctas - 1) / g.mb_ctas;
+    const double frac = g.sample_tiles * kChunks < k
+                            ? 1.0
+                            : std::min(1.0, std::max(static_cast<double>(g.expected),
+                                                     static_cast<double>(k) * g.ntiles / g.sample_tiles) /
+                                                static_cast<double>(n));
+    const long long rows = std::min(batch, kBM);
+    const long long bound = per_cta * rows * kBN;
+    const long long want_mb = std::max<long long>(4096, static_cast<long long>(4.0 * frac * static_cast<double>(bound)));
+    g.mb_cap = static_cast<int>(round_up(static_cast<size_t>(std::min(bound, want_mb)), 1024));
+    g.off_mb_key = take(8ull * g.mb_ctas * g.mb_cap);
+    g.off_mb_query = take(4ull * g.mb_ctas * g.mb_cap);
+    g.off_mb_count = take(4ull * g.mb_ctas);
     g.total = round_up(off, kAlign);
     return ZCGVS_OK;
 }
@@ -348,9 +420,12 @@ int zcgvs_gemm_topk(const void* corpus, int dtype, const float* row_scales, int6
     p.mask = mask;
     p.chunk_max = reinterpret_cast<float*>(ws + g.off_cmax);
     p.thr_key = reinterpret_cast<const unsigned long long*>(ws + g.off_thr);
-    p.cand_count = reinterpret_cast<unsigned int*>(ws + g.off_count);
-    p.cand = reinterpret_cast<unsigned long long*>(ws + g.off_cand);
-    p.cand_cap = kCandCap;
+    unsigned int* cand_count = reinterpret_cast<unsigned int*>(ws + g.off_count);
+    unsigned long long* cand = reinterpret_cast<unsigned long long*>(ws + g.off_cand);
+    p.mb_key = reinterpret_cast<unsigned long long*>(ws + g.off_mb_key);
+    p.mb_query = reinterpret_cast<unsigned int*>(ws + g.off_mb_query);
+    p.mb_count = reinterpret_cast<unsigned int*>(ws + g.off_mb_count);
+    p.mb_cap = g.mb_cap;
     p.status = reinterpret_cast<unsigned int*>(ws);
     p.stages = stage_count();
 
@@ -364,11 +439,13 @@ int zcgvs_gemm_topk(const void* corpus, int dtype, const float* row_scales, int6
     const int tcap = next_pow2(std::max(chunks, 2));
     unsigned long long* thr_key = reinterpret_cast<unsigned long long*>(ws + g.off_thr);
     int* done = reinterpret_cast<int*>(ws + g.off_done);
-    unsigned int* retry = reinterpret_cast<unsigned int*>(ws + 4);
+    unsigned int* retry = reinterpret_cast<unsigned int*>(ws + 16);  // [2 * kPasses] flags
     cudaError_t e = ensure_smem_optin(reinterpret_cast<const void*>(threshold_kernel));
     if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(threshold_kernel)");
-    threshold_kernel<<<batch, kSelectThreads, static_cast<size_t>(tcap) * 8, st>>>(p.chunk_max, chunks, k, tcap,
-                                                                                 thr_key, p.cand_count, done, retry);
+    unsigned long long* thr_safe = reinterpret_cast<unsigned long long*>(ws + g.off_thr_safe);
+    unsigned int* mneed = reinterpret_cast<unsigned int*>(ws + g.off_mneed);
+    threshold_kernel<<<batch, kSelectThreads, static_cast<size_t>(tcap) * 8, st>>>(
+        p.chunk_max, chunks, k, tcap, thr_key, thr_safe, cand_count, done, retry, mneed, g.mtiles);
     e = cudaGetLastError();
     if (e != cudaSuccess) return fail_cuda(e, "threshold_kernel launch");
     e = ensure_smem_optin(reinterpret_cast<const void*>(select_kernel));
@@ -377,12 +454,21 @@ int zcgvs_gemm_topk(const void* corpus, int dtype, const float* row_scales, int6
     // Filter pass over the whole corpus and its selection, then the (usually empty) retry.
     p.ntiles = g.ntiles;
     p.done = done;
-    for (int pass = 0; pass < 2; ++pass) {
-        p.retry = pass == 0 ? nullptr : retry;
+    const long long items = static_cast<long long>(p.mtiles) * p.ntiles;
+    const int filter_ctas = static_cast<int>(std::min<long long>(items, g.mb_ctas));
+    for (int pass = 0; pass < kPasses; ++pass) {
+        p.retry = pass == 0 ? nullptr : retry + pass;
+        p.mneed = pass == 0 ? nullptr : mneed + static_cast<size_t>(pass) * g.mtiles;
+        p.mb_overflow = retry + kPasses + pass;
         status = launch_gemm(gemm_fn<kFilter>(g.mode), mq, mx, p, st);
         if (status != ZCGVS_OK) return status;
+        bucket_kernel<<<dim3(32, filter_ctas), 256, 0, st>>>(p.mb_key, p.mb_query, p.mb_count, g.mb_cap, cand_count,
+                                                           cand, kCandCap, p.retry);
+        e = cudaGetLastError();
+        if (e != cudaSuccess) return fail_cuda(e, "bucket_kernel launch");
         select_kernel<<<batch, kSelectThreads, static_cast<size_t>(kCandCap) * 8, st>>>(
-            p.cand, p.cand_count, kCandCap, k, thr_key, done, retry, p.status, pass, out_indices, out_scores);
+            cand, cand_count, kCandCap, k, thr_key, thr_safe, done, retry, mneed, g.mtiles, p.status, pass,
+            out_indices, out_scores);
         e = cudaGetLastError();
         if (e != cudaSuccess) return fail_cuda(e, "select_kernel launch");
     }

@@ -64,9 +64,12 @@ struct GemmParams {
     const unsigned long long* thr_key;  // kFilter: [batch] key thresholds (0 = keep everything)
     const int* done;             // kFilter: [batch] queries already answered (skipped), or nullptr
     const unsigned int* retry;   // kFilter: run only when *retry != 0 (nullptr = always)
-    unsigned int* cand_count;    // kFilter: [batch]
-    unsigned long long* cand;    // kFilter: [batch][cand_cap]
-    int cand_cap;
+    const unsigned int* mneed;   // kFilter: [mtiles] query blocks to scan (nullptr = all)
+    unsigned long long* mb_key;  // kFilter: per-CTA mailbox [gridDim.x][mb_cap] candidate keys
+    unsigned int* mb_query;      // kFilter: the query of each mailbox entry
+    unsigned int* mb_count;      // kFilter: [gridDim.x] entries written (capped at mb_cap)
+    unsigned int* mb_overflow;   // kFilter: set when any mailbox overflowed
+    int mb_cap;
     unsigned int* status;
     int stages;
 };
@@ -132,6 +135,28 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
         : "memory");
 }
 
+// v[j] for a warp-uniform runtime j without indexing the register array (which would move
+// it to local memory): a uniform branch over the 32 cases.
+__device__ __forceinline__ float pick32(const float (&v)[32], int j) {
+    switch (j) {
+#define ZC_PICK(i) \
+    case i:        \
+        return v[i];
+        ZC_PICK(0) ZC_PICK(1) ZC_PICK(2) ZC_PICK(3) ZC_PICK(4) ZC_PICK(5) ZC_PICK(6) ZC_PICK(7)
+        ZC_PICK(8) ZC_PICK(9) ZC_PICK(10) ZC_PICK(11) ZC_PICK(12) ZC_PICK(13) ZC_PICK(14) ZC_PICK(15)
+        ZC_PICK(16) ZC_PICK(17) ZC_PICK(18) ZC_PICK(19) ZC_PICK(20) ZC_PICK(21) ZC_PICK(22) ZC_PICK(23)
+        ZC_PICK(24) ZC_PICK(25) ZC_PICK(26) ZC_PICK(27) ZC_PICK(28) ZC_PICK(29) ZC_PICK(30) ZC_PICK(31)
+#undef ZC_PICK
+        default:
+            return v[31];
+    }
+}
+
+// Item w of this CTA's walk is skipped when its query block needs no scan (retry passes).
+__device__ __forceinline__ bool item_skipped(const GemmParams& p, long long w) {
+    return p.mneed != nullptr && p.mneed[w % p.mtiles] == 0u;
+}
+
 template <int MODE, int EPI>
 __global__ void __launch_bounds__(kThreads, 1)
     gemm_scan_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_x,
@@ -150,6 +175,7 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* side_mask = reinterpret_cast<uint8_t*>(side + 4 * 2 * kBN);  // [4][2][kBN]
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort;
+    __shared__ unsigned int s_mb;  // mailbox entries reserved by this CTA
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
@@ -170,6 +196,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(drain, 1);
         fence_mbarrier_init();
         s_abort = 0;
+        s_mb = 0u;
     }
     if (warp == kMmaWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
@@ -190,6 +217,7 @@ __global__ void __launch_bounds__(kThreads, 1)
             long long issued = 0;
             bool ok = true;
             for (long long w = blockIdx.x; w < items && ok; w += gridDim.x) {
+                if (item_skipped(p, w)) continue;
                 const int m = static_cast<int>(w % p.mtiles);
                 const int n = static_cast<int>(w / p.mtiles);
                 for (int kb = 0; kb < p.kblocks; ++kb) {
@@ -224,7 +252,8 @@ __global__ void __launch_bounds__(kThreads, 1)
             uint32_t phase = 0;
             long long local = 0;
             bool ok = true;
-            for (long long w = blockIdx.x; w < items && ok; w += gridDim.x, ++local) {
+            for (long long w = blockIdx.x; w < items && ok; w += gridDim.x) {
+                if (item_skipped(p, w)) continue;
                 const int a = static_cast<int>(local & 1);
                 if (local >= 2) {
                     ok = !*abort_flag &&
@@ -263,6 +292,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                 }
                 if (!ok) break;
                 mma_commit(&acc_full[a]);  // accumulator a is complete
+                ++local;
             }
             // Make sure no MMA is in flight before the tensor memory is released.
             mma_commit(drain);
@@ -272,7 +302,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------- epilogue warps 0-3 ----------------
         const int row = warp * 32 + lane;  // TMEM lane = query row within the block
         long long local = 0;
-        for (long long w = blockIdx.x; w < items; w += gridDim.x, ++local) {
+        for (long long w = blockIdx.x; w < items; w += gridDim.x) {
+            if (item_skipped(p, w)) continue;
             const int m = static_cast<int>(w % p.mtiles);
             const int n = static_cast<int>(w / p.mtiles);
             const int a = static_cast<int>(local & 1);
@@ -344,20 +375,33 @@ __global__ void __launch_bounds__(kThreads, 1)
                     for (int j = 0; j < 32; ++j) best = fmaxf(best, sc[j]);
                     if (q_ok) p.chunk_max[(static_cast<size_t>(q) * p.ntiles + n) * kChunks + c] = best;
                 } else {
-                    float best = -INFINITY;
+                    // Candidates go to this CTA's mailbox. Each lane marks its passing columns;
+                    // the warp visits only column positions where some lane passes, reserving
+                    // slots with one shared-memory atomic per position and storing without
+                    // waiting, so the epilogue never waits on a global atomic.
+                    uint32_t pass = 0u;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) best = fmaxf(best, sc[j]);
-                    if (live && best >= thr && best > -INFINITY) {
-#pragma unroll 1
-                        for (int j = 0; j < 32; ++j) {
-                            if (sc[j] >= thr && sc[j] > -INFINITY) {
-                                const unsigned long long key =
-                                    make_key(sc[j], p.id_base + static_cast<unsigned>(doc0 + c * 32 + j));
-                                if (key < thr_key) continue;
-                                const unsigned int slot = atomicAdd(p.cand_count + q, 1u);
-                                if (slot < static_cast<unsigned int>(p.cand_cap)) {
-                                    p.cand[static_cast<size_t>(q) * p.cand_cap + slot] = key;
-                                }
+                    for (int j = 0; j < 32; ++j) pass |= (live && sc[j] >= thr && sc[j] > -INFINITY ? 1u : 0u) << j;
+                    uint32_t cols = __reduce_or_sync(0xffffffffu, pass);
+                    const size_t mb_base = static_cast<size_t>(blockIdx.x) * static_cast<size_t>(p.mb_cap);
+                    while (cols != 0u) {
+                        const int j = __ffs(cols) - 1;
+                        cols &= cols - 1u;
+                        const float v = pick32(sc, j);
+                        const unsigned long long key =
+                            make_key(v, p.id_base + static_cast<unsigned>(doc0 + c * 32 + j));
+                        const bool take = ((pass >> j) & 1u) != 0u && key >= thr_key;
+                        const uint32_t ballot = __ballot_sync(0xffffffffu, take);
+                        if (ballot == 0u) continue;
+                        const int leader = __ffs(ballot) - 1;
+                        unsigned int base = 0u;
+                        if (lane == leader) base = atomicAdd(&s_mb, static_cast<unsigned int>(__popc(ballot)));
+                        base = __shfl_sync(0xffffffffu, base, leader);
+                        if (take) {
+                            const unsigned int slot = base + __popc(ballot & ((1u << lane) - 1u));
+                            if (slot < static_cast<unsigned int>(p.mb_cap)) {
+                                p.mb_key[mb_base + slot] = key;
+                                p.mb_query[mb_base + slot] = static_cast<unsigned int>(q);
                             }
                         }
                     }
@@ -366,12 +410,20 @@ __global__ void __launch_bounds__(kThreads, 1)
             tc_fence_before();
             __syncwarp();
             if (lane == 0) mbar_arrive_cta(&acc_empty[a]);
+            ++local;
         }
     }
 
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
+    if constexpr (EPI == kFilter) {
+        if (tid == 0) {
+            const unsigned int used = s_mb;
+            p.mb_count[blockIdx.x] = min(used, static_cast<unsigned int>(p.mb_cap));
+            if (used > static_cast<unsigned int>(p.mb_cap)) atomicOr(p.mb_overflow, 1u);
+        }
+    }
     if (warp == kMmaWarp) {
         __syncwarp();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
