@@ -137,10 +137,10 @@ __device__ __forceinline__ void bulk_copy_g2s(void* dst_smem, const void* src_gm
         : "memory");
 }
 
-// L2 policy for data read exactly once (the corpus stream): its lines are evicted first, so
-// the kernel's own code, candidate lists and counters stay in L2 while hundreds of MB stream
-// through it. Without it the one-shot tail of the kernel (CTA selection, last-CTA merge)
-// fetches its instructions from DRAM.
+// L2 policy for data read exactly once (the corpus stream): its lines are the first to be
+// evicted, so the small data the kernel reuses (candidate lists, counters) is not pushed out
+// of L2 by the hundreds of MB streaming through it. (On the 1M x 768 batch-1 scan the
+// measured time is the same with and without it.)
 __device__ __forceinline__ u64 l2_policy_evict_first() {
     u64 policy;
     asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(policy));

@@ -126,7 +126,8 @@ __global__ void __launch_bounds__(kSelectThreads) threshold_kernel(const float* 
     }
 }
 
-// Moves the mailbox entries of every filter CTA (blockIdx.y) into per-query candidate buffers.
+// Moves the mailbox entries of every filter epilogue warp (blockIdx.y) into per-query
+// candidate buffers.
 // On a retry pass (retry != nullptr) it runs only when some query is being retried.
 __global__ void bucket_kernel(const unsigned long long* __restrict__ mb_key, const unsigned int* __restrict__ mb_query,
                               const unsigned int* __restrict__ mb_count, int mb_cap, unsigned int* cand_count,
@@ -136,6 +137,7 @@ __global__ void bucket_kernel(const unsigned long long* __restrict__ mb_key, con
     const unsigned int n = mb_count[c];
     const size_t base = static_cast<size_t>(c) * mb_cap;
     for (unsigned int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
+        if (mb_key[base + i] == 0ull) continue;  // a tie rejected by its key
         const unsigned int q = mb_query[base + i];
         const unsigned int slot = atomicAdd(cand_count + q, 1u);
         if (slot < static_cast<unsigned int>(cap)) cand[static_cast<size_t>(q) * cap + slot] = mb_key[base + i];
@@ -163,7 +165,8 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(const unsigned l
     const bool final = pass == kPasses - 1;
     const unsigned int total = cand_count[q];
     const bool overflow = total > static_cast<unsigned int>(cap) || flags[kPasses + pass] != 0u;
-    const int n = static_cast<int>(overflow ? static_cast<unsigned int>(cap) : total);
+    // Only the entries this pass wrote (the buffer may hold older ones past them).
+    const int n = static_cast<int>(min(total, static_cast<unsigned int>(cap)));
     const int size = n < 2 ? 2 : 1 << (32 - __clz(n - 1));
     for (int i = threadIdx.x; i < size; i += kSelectThreads) {
         keys[i] = i < n ? cand[static_cast<size_t>(q) * cap + i] : 0ull;
@@ -292,10 +295,11 @@ int plan_gemm(int dtype, long long n, int dim, int batch, int k, GemmLayout& g) 
     const long long rows = std::min(batch, kBM);
     const long long bound = per_cta * rows * kBN;
     const long long want_mb = std::max<long long>(4096, static_cast<long long>(4.0 * frac * static_cast<double>(bound)));
-    g.mb_cap = static_cast<int>(round_up(static_cast<size_t>(std::min(bound, want_mb)), 1024));
-    g.off_mb_key = take(8ull * g.mb_ctas * g.mb_cap);
-    g.off_mb_query = take(4ull * g.mb_ctas * g.mb_cap);
-    g.off_mb_count = take(4ull * g.mb_ctas);
+    // Per epilogue warp (4 per CTA): a quarter of the CTA's share, rounded up.
+    g.mb_cap = static_cast<int>(round_up(static_cast<size_t>((std::min(bound, want_mb) + 3) / 4), 1024));
+    g.off_mb_key = take(8ull * g.mb_ctas * 4 * g.mb_cap);
+    g.off_mb_query = take(4ull * g.mb_ctas * 4 * g.mb_cap);
+    g.off_mb_count = take(4ull * g.mb_ctas * 4);
     g.total = round_up(off, kAlign);
     return ZCGVS_OK;
 }
@@ -462,7 +466,7 @@ int zcgvs_gemm_topk(const void* corpus, int dtype, const float* row_scales, int6
         p.mb_overflow = retry + kPasses + pass;
         status = launch_gemm(gemm_fn<kFilter>(g.mode), mq, mx, p, st);
         if (status != ZCGVS_OK) return status;
-        bucket_kernel<<<dim3(32, filter_ctas), 256, 0, st>>>(p.mb_key, p.mb_query, p.mb_count, g.mb_cap, cand_count,
+        bucket_kernel<<<dim3(8, filter_ctas * 4), 256, 0, st>>>(p.mb_key, p.mb_query, p.mb_count, g.mb_cap, cand_count,
                                                            cand, kCandCap, p.retry);
         e = cudaGetLastError();
         if (e != cudaSuccess) return fail_cuda(e, "bucket_kernel launch");

@@ -65,11 +65,11 @@ struct GemmParams {
     const int* done;             // kFilter: [batch] queries already answered (skipped), or nullptr
     const unsigned int* retry;   // kFilter: run only when *retry != 0 (nullptr = always)
     const unsigned int* mneed;   // kFilter: [mtiles] query blocks to scan (nullptr = all)
-    unsigned long long* mb_key;  // kFilter: per-CTA mailbox [gridDim.x][mb_cap] candidate keys
+    unsigned long long* mb_key;  // kFilter: mailbox [gridDim.x * 4 epilogue warps][mb_cap] keys (0 = empty)
     unsigned int* mb_query;      // kFilter: the query of each mailbox entry
-    unsigned int* mb_count;      // kFilter: [gridDim.x] entries written (capped at mb_cap)
+    unsigned int* mb_count;      // kFilter: [gridDim.x * 4] entries written (capped at mb_cap)
     unsigned int* mb_overflow;   // kFilter: set when any mailbox overflowed
-    int mb_cap;
+    int mb_cap;                  // entries per epilogue warp
     unsigned int* status;
     int stages;
 };
@@ -175,7 +175,6 @@ __global__ void __launch_bounds__(kThreads, 1)
     uint8_t* side_mask = reinterpret_cast<uint8_t*>(side + 4 * 2 * kBN);  // [4][2][kBN]
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort;
-    __shared__ unsigned int s_mb;  // mailbox entries reserved by this CTA
 
     const int tid = threadIdx.x;
     const int warp = tid >> 5;
@@ -196,7 +195,6 @@ __global__ void __launch_bounds__(kThreads, 1)
         mbar_init(drain, 1);
         fence_mbarrier_init();
         s_abort = 0;
-        s_mb = 0u;
     }
     if (warp == kMmaWarp) {
         asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
@@ -302,6 +300,8 @@ __global__ void __launch_bounds__(kThreads, 1)
         // ---------------- epilogue warps 0-3 ----------------
         const int row = warp * 32 + lane;  // TMEM lane = query row within the block
         long long local = 0;
+        uint32_t wcount = 0u;  // this warp's mailbox entries (kFilter), the same in every lane
+        const size_t seg = (static_cast<size_t>(blockIdx.x) * 4 + warp) * static_cast<size_t>(p.mb_cap);
         for (long long w = blockIdx.x; w < items; w += gridDim.x) {
             if (item_skipped(p, w)) continue;
             const int m = static_cast<int>(w % p.mtiles);
@@ -310,14 +310,19 @@ __global__ void __launch_bounds__(kThreads, 1)
             const int q = m * kBM + row;
             const bool q_ok = q < p.batch;
             const long long doc0 = static_cast<long long>(n) * kBN;
-            // This warp's copy of the tile's per-document side data (row scales, validity), so
-            // the epilogue warps never wait on one another.
+            // This warp's copy of the tile's per-document side data, so the epilogue warps never
+            // wait on one another: one validity word per 32-document chunk (padding rows past the
+            // corpus and masked documents are invalid) and, for per-row int8, the row scales
+            // with NaN for invalid documents (a NaN score fails every comparison).
             float* scales = side + (warp * 2 + a) * kBN;
-            uint8_t* mk = side_mask + (warp * 2 + a) * kBN;
-            for (int j = lane; j < kBN; j += 32) {
-                const long long d = doc0 + j;
-                if constexpr (MODE == kModeI8R) scales[j] = d < p.n ? __ldg(p.row_scales + d) : 0.0f;
-                mk[j] = (d < p.n && (p.mask == nullptr || __ldg(p.mask + d) != 0)) ? 1 : 0;
+            uint32_t* vbits = reinterpret_cast<uint32_t*>(side_mask + (warp * 2 + a) * kBN);
+#pragma unroll 1
+            for (int c = 0; c < kChunks; ++c) {
+                const long long d = doc0 + c * 32 + lane;
+                const bool valid = d < p.n && (p.mask == nullptr || __ldg(p.mask + d) != 0);
+                if constexpr (MODE == kModeI8R) scales[c * 32 + lane] = valid ? __ldg(p.row_scales + d) : __int_as_float(0x7fc00000);
+                const uint32_t word = __ballot_sync(0xffffffffu, valid);
+                if (lane == 0) vbits[c] = word;
             }
             __syncwarp();
             bool ok = true;
@@ -346,17 +351,15 @@ __global__ void __launch_bounds__(kThreads, 1)
                 uint32_t v[32];
                 __syncwarp();  // tcgen05.ld is warp-collective; the append branch below diverges
                 tmem_ld32(taddr + static_cast<uint32_t>(c * 32), v);
+                const uint32_t valid = vbits[c];
                 float sc[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
-                    const int col = c * 32 + j;
-                    float score;
                     if constexpr (MODE == kModeI8R) {
-                        score = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(v[j])), qs), scales[col]);
+                        sc[j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(v[j])), qs), scales[c * 32 + j]);
                     } else {
-                        score = __uint_as_float(v[j]);
+                        sc[j] = __uint_as_float(v[j]);
                     }
-                    sc[j] = mk[col] ? score : -INFINITY;  // invalid (padding / masked) documents
                 }
                 if constexpr (EPI == kEmit) {
                     if (q_ok) {
@@ -364,45 +367,58 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int j = 0; j < 32; ++j) {
                             const long long d = doc0 + c * 32 + j;
                             if (d < p.n) {
-                                const bool allowed = p.mask == nullptr || __ldg(p.mask + d) != 0;
-                                p.out_matrix[static_cast<size_t>(q) * p.n + d] = allowed ? sc[j] : -FLT_MAX;
+                                p.out_matrix[static_cast<size_t>(q) * p.n + d] = ((valid >> j) & 1u) ? sc[j] : -FLT_MAX;
                             }
                         }
                     }
                 } else if constexpr (EPI == kTileMax) {
                     float best = -INFINITY;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) best = fmaxf(best, sc[j]);
+                    for (int j = 0; j < 32; ++j) best = fmaxf(best, ((valid >> j) & 1u) ? sc[j] : -INFINITY);
                     if (q_ok) p.chunk_max[(static_cast<size_t>(q) * p.ntiles + n) * kChunks + c] = best;
                 } else {
-                    // Candidates go to this CTA's mailbox. Each lane marks its passing columns;
-                    // the warp visits only column positions where some lane passes, reserving
-                    // slots with one shared-memory atomic per position and storing without
-                    // waiting, so the epilogue never waits on a global atomic.
-                    uint32_t pass = 0u;
+                    // Candidates go to this warp's own mailbox segment: the lanes' pass counts
+                    // are prefix-summed across the warp and appended at a register counter, so
+                    // the epilogue issues no atomics and never waits on a store.
+                    uint32_t pass = 0u, ties = 0u;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) pass |= (live && sc[j] >= thr && sc[j] > -INFINITY ? 1u : 0u) << j;
-                    uint32_t cols = __reduce_or_sync(0xffffffffu, pass);
-                    const size_t mb_base = static_cast<size_t>(blockIdx.x) * static_cast<size_t>(p.mb_cap);
-                    while (cols != 0u) {
-                        const int j = __ffs(cols) - 1;
-                        cols &= cols - 1u;
-                        const float v = pick32(sc, j);
-                        const unsigned long long key =
-                            make_key(v, p.id_base + static_cast<unsigned>(doc0 + c * 32 + j));
-                        const bool take = ((pass >> j) & 1u) != 0u && key >= thr_key;
-                        const uint32_t ballot = __ballot_sync(0xffffffffu, take);
-                        if (ballot == 0u) continue;
-                        const int leader = __ffs(ballot) - 1;
-                        unsigned int base = 0u;
-                        if (lane == leader) base = atomicAdd(&s_mb, static_cast<unsigned int>(__popc(ballot)));
-                        base = __shfl_sync(0xffffffffu, base, leader);
-                        if (take) {
-                            const unsigned int slot = base + __popc(ballot & ((1u << lane) - 1u));
-                            if (slot < static_cast<unsigned int>(p.mb_cap)) {
-                                p.mb_key[mb_base + slot] = key;
-                                p.mb_query[mb_base + slot] = static_cast<unsigned int>(q);
+                    for (int j = 0; j < 32; ++j) {
+                        pass |= (sc[j] > thr ? 1u : 0u) << j;
+                        ties |= (sc[j] == thr ? 1u : 0u) << j;
+                    }
+                    pass = live ? (pass & valid) : 0u;
+                    ties = live ? (ties & valid) : 0u;
+                    // A score equal to the threshold's passes only if its key (ties by id) does.
+                    while (ties != 0u) {
+                        const int j = __ffs(ties) - 1;
+                        ties &= ties - 1u;
+                        if (make_key(thr, p.id_base + static_cast<unsigned>(doc0 + c * 32 + j)) >= thr_key) pass |= 1u << j;
+                    }
+                    const uint32_t cnt = static_cast<uint32_t>(__popc(pass));
+                    uint32_t incl = cnt;
+#pragma unroll
+                    for (int o = 1; o < 32; o <<= 1) {
+                        const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+                        if (lane >= o) incl += t;
+                    }
+                    const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
+                    if (total != 0u) {
+                        uint32_t slot = wcount + incl - cnt;
+                        wcount += total;
+                        uint32_t bits = pass;
+                        while (bits != 0u) {
+                            const int j = __ffs(bits) - 1;
+                            bits &= bits - 1u;
+                            float v = sc[0];
+#pragma unroll
+                            for (int jj = 1; jj < 32; ++jj) v = (j == jj) ? sc[jj] : v;
+                            const unsigned long long key =
+                                make_key(v, p.id_base + static_cast<unsigned>(doc0 + c * 32 + j));
+                            if (slot < static_cast<uint32_t>(p.mb_cap)) {
+                                p.mb_key[seg + slot] = key;
+                                p.mb_query[seg + slot] = static_cast<unsigned int>(q);
                             }
+                            ++slot;
                         }
                     }
                 }
@@ -412,18 +428,18 @@ __global__ void __launch_bounds__(kThreads, 1)
             if (lane == 0) mbar_arrive_cta(&acc_empty[a]);
             ++local;
         }
+        if constexpr (EPI == kFilter) {
+            if (lane == 0) {
+                p.mb_count[blockIdx.x * 4 + warp] = min(wcount, static_cast<uint32_t>(p.mb_cap));
+                if (wcount > static_cast<uint32_t>(p.mb_cap)) atomicOr(p.mb_overflow, 1u);
+            }
+        }
     }
 
     tc_fence_before();
     __syncthreads();
     tc_fence_after();
-    if constexpr (EPI == kFilter) {
-        if (tid == 0) {
-            const unsigned int used = s_mb;
-            p.mb_count[blockIdx.x] = min(used, static_cast<unsigned int>(p.mb_cap));
-            if (used > static_cast<unsigned int>(p.mb_cap)) atomicOr(p.mb_overflow, 1u);
-        }
-    }
+
     if (warp == kMmaWarp) {
         __syncwarp();
         asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
