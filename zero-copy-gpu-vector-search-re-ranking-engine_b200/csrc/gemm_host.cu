@@ -45,6 +45,7 @@ constexpr int kCandCap = 16384;
 constexpr int kStatRank = 16;  // rank of the statistical threshold among the sample's chunk maxima
 constexpr int kPasses = 3;     // the filter pass and up to two retries
 constexpr int kSelectThreads = 512;
+constexpr int kSelectCap = 4096;  // selection buffer (32 KB): k (<= 1024) + 4 keys per thread per round
 constexpr size_t kAlign = 256;
 
 // Queries -> the MMA operand layout: fp16 rows, or int8 rows with a per-row scale computed
@@ -93,21 +94,24 @@ __global__ void __launch_bounds__(kSelectThreads) threshold_kernel(const float* 
     __shared__ int s_count;
     __shared__ u64 s_thr;
     const int q = blockIdx.x;
-    for (int i = threadIdx.x; i < cap; i += kSelectThreads) {
-        keys[i] = i < chunks ? make_key(chunk_max[static_cast<size_t>(q) * chunks + i], static_cast<uint32_t>(i)) : 0ull;
-    }
     TopkSmem t;
     t.buf = keys;
     t.count = &s_count;
     t.thr = &s_thr;
     t.cap = cap;
     t.k = max(k, kStatRank);
-    if (threadIdx.x == 0) s_count = chunks;
+    if (threadIdx.x == 0) {
+        s_count = 0;
+        s_thr = 0ull;
+    }
     __syncthreads();
+    const float* row = chunk_max + static_cast<size_t>(q) * chunks;
+    topk_offer_all<4>(t, 0, chunks, 0ull, [&](int i) { return make_key(row[i], static_cast<uint32_t>(i)); },
+                      kSelectThreads);
     topk_flush_mask(t, 1u, kSelectThreads);
     __syncthreads();
     if (threadIdx.x == 0) {
-        // keys[r - 1] exists only when there are at least r chunks (the buffer holds cap >= chunks).
+        // keys[r - 1] holds the r-th largest when there are at least r chunks (r <= t.k).
         auto bound = [&](int r) {
             const float score = chunks >= r ? key_score(keys[r - 1]) : -INFINITY;
             return score > -INFINITY ? (static_cast<u64>(orderable_bits(score)) << 32) : 0ull;
@@ -167,18 +171,19 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(const unsigned l
     const bool overflow = total > static_cast<unsigned int>(cap) || flags[kPasses + pass] != 0u;
     // Only the entries this pass wrote (the buffer may hold older ones past them).
     const int n = static_cast<int>(min(total, static_cast<unsigned int>(cap)));
-    const int size = n < 2 ? 2 : 1 << (32 - __clz(n - 1));
-    for (int i = threadIdx.x; i < size; i += kSelectThreads) {
-        keys[i] = i < n ? cand[static_cast<size_t>(q) * cap + i] : 0ull;
-    }
     TopkSmem t;
     t.buf = keys;
     t.count = &s_count;
     t.thr = &s_thr;
-    t.cap = cap;
+    t.cap = kSelectCap;
     t.k = k;
-    if (threadIdx.x == 0) s_count = n;
+    if (threadIdx.x == 0) {
+        s_count = 0;
+        s_thr = 0ull;
+    }
     __syncthreads();
+    const unsigned long long* mine = cand + static_cast<size_t>(q) * cap;
+    topk_offer_all<4>(t, 0, n, 0ull, [&](int i) { return mine[i]; }, kSelectThreads);
     topk_flush_mask(t, 1u, kSelectThreads);
     __syncthreads();
     const bool short_list = !overflow && n < k && thr_key[q] != thr_safe[q];
@@ -295,24 +300,31 @@ int plan_gemm(int dtype, long long n, int dim, int batch, int k, GemmLayout& g) 
     const long long rows = std::min(batch, kBM);
     const long long bound = per_cta * rows * kBN;
     const long long want_mb = std::max<long long>(4096, static_cast<long long>(4.0 * frac * static_cast<double>(bound)));
-    // Per epilogue warp (4 per CTA): a quarter of the CTA's share, rounded up.
+    // Per epilogue warp: a quarter of the CTA's share (a warp sees a quarter of the rows and
+    // half of the columns, so this leaves a margin of 2), rounded up.
     g.mb_cap = static_cast<int>(round_up(static_cast<size_t>((std::min(bound, want_mb) + 3) / 4), 1024));
-    g.off_mb_key = take(8ull * g.mb_ctas * 4 * g.mb_cap);
-    g.off_mb_query = take(4ull * g.mb_ctas * 4 * g.mb_cap);
-    g.off_mb_count = take(4ull * g.mb_ctas * 4);
+    g.off_mb_key = take(8ull * g.mb_ctas * kEpiWarps * g.mb_cap);
+    g.off_mb_query = take(4ull * g.mb_ctas * kEpiWarps * g.mb_cap);
+    g.off_mb_count = take(4ull * g.mb_ctas * kEpiWarps);
     g.total = round_up(off, kAlign);
     return ZCGVS_OK;
 }
 
 int stage_count() {
     const int budget = device_max_smem() - 2048;
-    const int side = 4 * 2 * kBN * 5;  // per epilogue warp and accumulator: row scales + validity
+    const int side = 16 + kEpiWarps * 2 * (kHalf * 4 + 16);  // per epilogue warp and accumulator: scales, validity
     const int fixed = 1024 + 8 * (2 * 8 + 5) + side;
     return std::max(2, std::min(8, (budget - fixed) / kStageBytes));
 }
 
 size_t gemm_smem(int stages) {
-    return 1024 + static_cast<size_t>(stages) * kStageBytes + 8 * (2 * stages + 5) + 4 * 2 * kBN * 5;
+    return 1024 + static_cast<size_t>(stages) * kStageBytes + 8 * (2 * stages + 5) + 16 +
+           kEpiWarps * 2 * (kHalf * 4 + 16);
+}
+
+// Vector side-data loads need 16-byte aligned row scales and 4-byte aligned mask bytes.
+int side_vec_ok(const float* row_scales, const uint8_t* mask) {
+    return (reinterpret_cast<uintptr_t>(row_scales) % 16 == 0 && reinterpret_cast<uintptr_t>(mask) % 4 == 0) ? 1 : 0;
 }
 
 using GemmFn = void (*)(const CUtensorMap, const CUtensorMap, const GemmParams);
@@ -432,6 +444,7 @@ int zcgvs_gemm_topk(const void* corpus, int dtype, const float* row_scales, int6
     p.mb_cap = g.mb_cap;
     p.status = reinterpret_cast<unsigned int*>(ws);
     p.stages = stage_count();
+    p.side_vec = side_vec_ok(row_scales, mask);
 
     // Threshold pre-pass over the first sample tiles.
     GemmParams ps = p;
@@ -440,7 +453,7 @@ int zcgvs_gemm_topk(const void* corpus, int dtype, const float* row_scales, int6
     status = launch_gemm(gemm_fn<kTileMax>(g.mode), mq, mx, ps, st);
     if (status != ZCGVS_OK) return status;
     const int chunks = g.sample_tiles * kChunks;
-    const int tcap = next_pow2(std::max(chunks, 2));
+    const int tcap = kSelectCap;
     unsigned long long* thr_key = reinterpret_cast<unsigned long long*>(ws + g.off_thr);
     int* done = reinterpret_cast<int*>(ws + g.off_done);
     unsigned int* retry = reinterpret_cast<unsigned int*>(ws + 16);  // [2 * kPasses] flags
@@ -466,11 +479,11 @@ int zcgvs_gemm_topk(const void* corpus, int dtype, const float* row_scales, int6
         p.mb_overflow = retry + kPasses + pass;
         status = launch_gemm(gemm_fn<kFilter>(g.mode), mq, mx, p, st);
         if (status != ZCGVS_OK) return status;
-        bucket_kernel<<<dim3(8, filter_ctas * 4), 256, 0, st>>>(p.mb_key, p.mb_query, p.mb_count, g.mb_cap, cand_count,
+        bucket_kernel<<<dim3(8, filter_ctas * kEpiWarps), 256, 0, st>>>(p.mb_key, p.mb_query, p.mb_count, g.mb_cap, cand_count,
                                                            cand, kCandCap, p.retry);
         e = cudaGetLastError();
         if (e != cudaSuccess) return fail_cuda(e, "bucket_kernel launch");
-        select_kernel<<<batch, kSelectThreads, static_cast<size_t>(kCandCap) * 8, st>>>(
+        select_kernel<<<batch, kSelectThreads, static_cast<size_t>(kSelectCap) * 8, st>>>(
             cand, cand_count, kCandCap, k, thr_key, thr_safe, done, retry, mneed, g.mtiles, p.status, pass,
             out_indices, out_scores);
         e = cudaGetLastError();
@@ -526,6 +539,7 @@ int zcgvs_gemm_similarity(const void* corpus, int dtype, const float* row_scales
     p.out_matrix = scores;
     p.status = reinterpret_cast<unsigned int*>(ws);
     p.stages = stage_count();
+    p.side_vec = side_vec_ok(row_scales, mask);
     return launch_gemm(gemm_fn<kEmit>(g.mode), mq, mx, p, st);
 }
 

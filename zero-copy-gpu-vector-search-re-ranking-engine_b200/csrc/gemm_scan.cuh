@@ -38,10 +38,11 @@ constexpr int kBKBytes = 128;             // one 128-byte swizzle row of K per s
 constexpr int kStageA = kBM * kBKBytes;   // 16 KB
 constexpr int kStageB = kBN * kBKBytes;   // 32 KB
 constexpr int kStageBytes = kStageA + kStageB;
-constexpr int kThreads = 192;             // warps 0-3 epilogue, 4 producer, 5 MMA
-constexpr int kEpiThreads = 128;
-constexpr int kProducerWarp = 4;
-constexpr int kMmaWarp = 5;
+constexpr int kEpiWarps = 8;              // two per TMEM lane quarter, one per column half
+constexpr int kThreads = 32 * (kEpiWarps + 2);  // warps 0-7 epilogue, 8 producer, 9 MMA
+constexpr int kProducerWarp = kEpiWarps;
+constexpr int kMmaWarp = kEpiWarps + 1;
+constexpr int kHalf = kBN / 2;            // columns per epilogue warp
 constexpr int kTmemCols = 512;            // two 256-column accumulators
 constexpr int kChunks = kBN / 32;         // threshold granularity: 32-document chunks per tile
 
@@ -72,6 +73,7 @@ struct GemmParams {
     int mb_cap;                  // entries per epilogue warp
     unsigned int* status;
     int stages;
+    int side_vec;                // row_scales 16-byte and mask 4-byte aligned: vector side loads
 };
 
 __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t smem_addr) {
@@ -171,8 +173,9 @@ __global__ void __launch_bounds__(kThreads, 1)
     u64* acc_empty = acc_full + 2;    // [2]
     u64* drain = acc_empty + 2;       // [1]
     // Per epilogue warp and accumulator: the tile's row scales and validity bytes.
-    float* side = reinterpret_cast<float*>(drain + 1);                    // [4][2][kBN]
-    uint8_t* side_mask = reinterpret_cast<uint8_t*>(side + 4 * 2 * kBN);  // [4][2][kBN]
+    // 16-byte aligned: the epilogue stores float4s here.
+    float* side = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(drain + 1) + 15) & ~uintptr_t(15));  // [8][2][kHalf]
+    uint32_t* side_bits = reinterpret_cast<uint32_t*>(side + kEpiWarps * 2 * kHalf);  // [8][2][4] validity
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort;
 
@@ -190,7 +193,7 @@ __global__ void __launch_bounds__(kThreads, 1)
         }
         for (int a = 0; a < 2; ++a) {
             mbar_init(&acc_full[a], 1);
-            mbar_init(&acc_empty[a], 4);
+            mbar_init(&acc_empty[a], kEpiWarps);
         }
         mbar_init(drain, 1);
         fence_mbarrier_init();
@@ -297,34 +300,80 @@ __global__ void __launch_bounds__(kThreads, 1)
             mbar_wait_bounded(drain, 0u, p.status, kStatusDrainTimeout);
         }
     } else {
-        // ---------------- epilogue warps 0-3 ----------------
-        const int row = warp * 32 + lane;  // TMEM lane = query row within the block
+        // ---------------- epilogue warps 0-7 ----------------
+        // Warp w reads TMEM lanes 32 (w % 4) .. + 31 (query rows) and columns
+        // (w / 4) * 128 .. + 127 of each accumulator (documents): four 32-column chunks.
+        const int row = (warp & 3) * 32 + lane;
+        const int half = warp >> 2;
         long long local = 0;
         uint32_t wcount = 0u;  // this warp's mailbox entries (kFilter), the same in every lane
-        const size_t seg = (static_cast<size_t>(blockIdx.x) * 4 + warp) * static_cast<size_t>(p.mb_cap);
-        for (long long w = blockIdx.x; w < items; w += gridDim.x) {
-            if (item_skipped(p, w)) continue;
+        const size_t seg = (static_cast<size_t>(blockIdx.x) * kEpiWarps + warp) * static_cast<size_t>(p.mb_cap);
+        // Side data of an item for this warp's half tile, one load per lane (documents 4 lane ..
+        // 4 lane + 3): the row scales (per-row int8) and the allow-mask bytes. Loaded one item
+        // ahead so the latency overlaps the previous item's epilogue.
+        auto next_item = [&](long long w) {
+            do {
+                w += gridDim.x;
+            } while (w < items && item_skipped(p, w));
+            return w;
+        };
+        auto load_side = [&](long long w, float4& sv, uint32_t& mv) {
+            sv = make_float4(0.f, 0.f, 0.f, 0.f);
+            mv = 0u;
+            if (w >= items) return;
+            const long long d = (w / p.mtiles) * kBN + half * kHalf + 4 * lane;
+            if (p.side_vec && d + 3 < p.n) {
+                if constexpr (MODE == kModeI8R) sv = __ldg(reinterpret_cast<const float4*>(p.row_scales + d));
+                mv = p.mask != nullptr ? __ldg(reinterpret_cast<const uint32_t*>(p.mask + d)) : 0x01010101u;
+            } else {
+                float t[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    if (d + i < p.n) {
+                        if constexpr (MODE == kModeI8R) t[i] = __ldg(p.row_scales + d + i);
+                        const uint32_t allowed = p.mask != nullptr ? (__ldg(p.mask + d + i) != 0 ? 1u : 0u) : 1u;
+                        mv |= allowed << (8 * i);
+                    }
+                }
+                sv = make_float4(t[0], t[1], t[2], t[3]);
+            }
+        };
+        long long w = blockIdx.x;
+        if (w < items && item_skipped(p, w)) w = next_item(w);
+        float4 sv;
+        uint32_t mv;
+        load_side(w, sv, mv);
+        while (w < items) {
             const int m = static_cast<int>(w % p.mtiles);
             const int n = static_cast<int>(w / p.mtiles);
             const int a = static_cast<int>(local & 1);
             const int q = m * kBM + row;
             const bool q_ok = q < p.batch;
-            const long long doc0 = static_cast<long long>(n) * kBN;
-            // This warp's copy of the tile's per-document side data, so the epilogue warps never
-            // wait on one another: one validity word per 32-document chunk (padding rows past the
-            // corpus and masked documents are invalid) and, for per-row int8, the row scales
-            // with NaN for invalid documents (a NaN score fails every comparison).
-            float* scales = side + (warp * 2 + a) * kBN;
-            uint32_t* vbits = reinterpret_cast<uint32_t*>(side_mask + (warp * 2 + a) * kBN);
-#pragma unroll 1
-            for (int c = 0; c < kChunks; ++c) {
-                const long long d = doc0 + c * 32 + lane;
-                const bool valid = d < p.n && (p.mask == nullptr || __ldg(p.mask + d) != 0);
-                if constexpr (MODE == kModeI8R) scales[c * 32 + lane] = valid ? __ldg(p.row_scales + d) : __int_as_float(0x7fc00000);
-                const uint32_t word = __ballot_sync(0xffffffffu, valid);
-                if (lane == 0) vbits[c] = word;
+            const long long doc0 = static_cast<long long>(n) * kBN + half * kHalf;  // this warp's first column
+            // This warp's copy of the side data (the epilogue warps never wait on one another):
+            // a validity word per 32-document chunk (padding rows and masked documents are
+            // invalid) and, for per-row int8, row scales with NaN for invalid documents (a NaN
+            // score fails every comparison).
+            float* scales = side + (warp * 2 + a) * kHalf;
+            uint32_t* vbits = side_bits + (warp * 2 + a) * 4;
+            {
+                const uint32_t nib = (mv & 1u) | ((mv >> 7) & 2u) | ((mv >> 14) & 4u) | ((mv >> 21) & 8u);
+                if constexpr (MODE == kModeI8R) {
+                    const float nan = __int_as_float(0x7fc00000);
+                    *reinterpret_cast<float4*>(scales + 4 * lane) =
+                        make_float4((nib & 1u) ? sv.x : nan, (nib & 2u) ? sv.y : nan, (nib & 4u) ? sv.z : nan,
+                                    (nib & 8u) ? sv.w : nan);
+                }
+#pragma unroll
+                for (int cl = 0; cl < 4; ++cl) {
+                    const uint32_t word = __reduce_or_sync(0xffffffffu, (lane >> 3) == cl ? nib << (4 * (lane & 7)) : 0u);
+                    if (lane == 0) vbits[cl] = word;
+                }
+                __syncwarp();
             }
-            __syncwarp();
+            const long long w_next = next_item(w);
+            load_side(w_next, sv, mv);
+
             bool ok = true;
             if (lane == 0) {
                 ok = !*abort_flag && mbar_wait_bounded(&acc_full[a], static_cast<uint32_t>((local >> 1) & 1), p.status,
@@ -345,18 +394,20 @@ __global__ void __launch_bounds__(kThreads, 1)
                     thr = thr_key == 0ull ? -INFINITY : score_from_bits(static_cast<uint32_t>(thr_key >> 32));
                 }
             }
-            const uint32_t taddr = tmem_base + (static_cast<uint32_t>(warp * 32) << 16) + static_cast<uint32_t>(a * kBN);
+            const uint32_t taddr = tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16) +
+                                   static_cast<uint32_t>(a * kBN + half * kHalf);
 #pragma unroll 1
-            for (int c = 0; c < kBN / 32; ++c) {
+            for (int cl = 0; cl < 4; ++cl) {
                 uint32_t v[32];
                 __syncwarp();  // tcgen05.ld is warp-collective; the append branch below diverges
-                tmem_ld32(taddr + static_cast<uint32_t>(c * 32), v);
-                const uint32_t valid = vbits[c];
+                tmem_ld32(taddr + static_cast<uint32_t>(cl * 32), v);
+                const uint32_t valid = vbits[cl];
+                const long long dchunk = doc0 + cl * 32;
                 float sc[32];
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     if constexpr (MODE == kModeI8R) {
-                        sc[j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(v[j])), qs), scales[c * 32 + j]);
+                        sc[j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(v[j])), qs), scales[cl * 32 + j]);
                     } else {
                         sc[j] = __uint_as_float(v[j]);
                     }
@@ -365,7 +416,7 @@ __global__ void __launch_bounds__(kThreads, 1)
                     if (q_ok) {
 #pragma unroll
                         for (int j = 0; j < 32; ++j) {
-                            const long long d = doc0 + c * 32 + j;
+                            const long long d = dchunk + j;
                             if (d < p.n) {
                                 p.out_matrix[static_cast<size_t>(q) * p.n + d] = ((valid >> j) & 1u) ? sc[j] : -FLT_MAX;
                             }
@@ -375,10 +426,9 @@ __global__ void __launch_bounds__(kThreads, 1)
                     float best = -INFINITY;
 #pragma unroll
                     for (int j = 0; j < 32; ++j) best = fmaxf(best, ((valid >> j) & 1u) ? sc[j] : -INFINITY);
-                    if (q_ok) p.chunk_max[(static_cast<size_t>(q) * p.ntiles + n) * kChunks + c] = best;
+                    if (q_ok) p.chunk_max[(static_cast<size_t>(q) * p.ntiles + n) * kChunks + half * 4 + cl] = best;
                 } else {
-                    // Candidates go to this warp's own mailbox segment: the lanes' pass counts
-                    // are prefix-summed across the warp and appended at a register counter, so
+                    // Candidates go to this warp's own mailbox segment at a register counter:
                     // the epilogue issues no atomics and never waits on a store.
                     uint32_t pass = 0u, ties = 0u;
 #pragma unroll
@@ -392,34 +442,42 @@ __global__ void __launch_bounds__(kThreads, 1)
                     while (ties != 0u) {
                         const int j = __ffs(ties) - 1;
                         ties &= ties - 1u;
-                        if (make_key(thr, p.id_base + static_cast<unsigned>(doc0 + c * 32 + j)) >= thr_key) pass |= 1u << j;
+                        if (make_key(thr, p.id_base + static_cast<unsigned>(dchunk + j)) >= thr_key) pass |= 1u << j;
                     }
                     const uint32_t cnt = static_cast<uint32_t>(__popc(pass));
-                    uint32_t incl = cnt;
+                    const uint32_t some = __ballot_sync(0xffffffffu, cnt != 0u);
+                    if (some == 0u) continue;
+                    // Slots: one ballot when no lane has more than one candidate (the common
+                    // case), else an inclusive warp scan of the counts.
+                    uint32_t excl, total;
+                    if (__ballot_sync(0xffffffffu, cnt > 1u) == 0u) {
+                        excl = static_cast<uint32_t>(__popc(some & ((1u << lane) - 1u)));
+                        total = static_cast<uint32_t>(__popc(some));
+                    } else {
+                        uint32_t incl = cnt;
 #pragma unroll
-                    for (int o = 1; o < 32; o <<= 1) {
-                        const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
-                        if (lane >= o) incl += t;
-                    }
-                    const uint32_t total = __shfl_sync(0xffffffffu, incl, 31);
-                    if (total != 0u) {
-                        uint32_t slot = wcount + incl - cnt;
-                        wcount += total;
-                        uint32_t bits = pass;
-                        while (bits != 0u) {
-                            const int j = __ffs(bits) - 1;
-                            bits &= bits - 1u;
-                            float v = sc[0];
-#pragma unroll
-                            for (int jj = 1; jj < 32; ++jj) v = (j == jj) ? sc[jj] : v;
-                            const unsigned long long key =
-                                make_key(v, p.id_base + static_cast<unsigned>(doc0 + c * 32 + j));
-                            if (slot < static_cast<uint32_t>(p.mb_cap)) {
-                                p.mb_key[seg + slot] = key;
-                                p.mb_query[seg + slot] = static_cast<unsigned int>(q);
-                            }
-                            ++slot;
+                        for (int o = 1; o < 32; o <<= 1) {
+                            const uint32_t t = __shfl_up_sync(0xffffffffu, incl, o);
+                            if (lane >= o) incl += t;
                         }
+                        excl = incl - cnt;
+                        total = __shfl_sync(0xffffffffu, incl, 31);
+                    }
+                    uint32_t slot = wcount + excl;
+                    wcount += total;
+                    uint32_t bits = pass;
+                    while (bits != 0u) {
+                        const int j = __ffs(bits) - 1;
+                        bits &= bits - 1u;
+                        float val = sc[0];
+#pragma unroll
+                        for (int jj = 1; jj < 32; ++jj) val = (j == jj) ? sc[jj] : val;
+                        const unsigned long long key = make_key(val, p.id_base + static_cast<unsigned>(dchunk + j));
+                        if (slot < static_cast<uint32_t>(p.mb_cap)) {
+                            p.mb_key[seg + slot] = key;
+                            p.mb_query[seg + slot] = static_cast<unsigned int>(q);
+                        }
+                        ++slot;
                     }
                 }
             }
@@ -427,10 +485,11 @@ __global__ void __launch_bounds__(kThreads, 1)
             __syncwarp();
             if (lane == 0) mbar_arrive_cta(&acc_empty[a]);
             ++local;
+            w = w_next;
         }
         if constexpr (EPI == kFilter) {
             if (lane == 0) {
-                p.mb_count[blockIdx.x * 4 + warp] = min(wcount, static_cast<uint32_t>(p.mb_cap));
+                p.mb_count[blockIdx.x * kEpiWarps + warp] = min(wcount, static_cast<uint32_t>(p.mb_cap));
                 if (wcount > static_cast<uint32_t>(p.mb_cap)) atomicOr(p.mb_overflow, 1u);
             }
         }
