@@ -175,3 +175,17 @@ def test_gemm_topk_statistical_bound_fallback_is_exact(zc, orc):
     np.testing.assert_array_equal(idx.cpu().numpy(), ref_i)
     np.testing.assert_array_equal(val.cpu().numpy(), ref_v)
     assert ws.status() == 0
+
+
+def test_scan_topk_dispatches_large_int8_batches_exactly(zc, orc):
+    """zcgvs_scan_topk on a per-row int8 corpus with >= 64 queries and >= 65536 rows runs on the
+    tensor cores; the result must still equal the oracle bit for bit."""
+    import torch
+
+    n, dim, batch, k = 100000, 256, 96, 100
+    storage, row_scales, queries = case(orc, 4, n, dim, batch, 11)
+    idx, val = zc.scan_topk(dev(storage), 4, dim, dev(queries), k, row_scales=dev(row_scales))
+    torch.cuda.synchronize()
+    ref_i, ref_v = orc.scan_topk(storage, 4, dim, queries, k, row_scales=row_scales)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ref_i)
+    np.testing.assert_array_equal(val.cpu().numpy(), ref_v)

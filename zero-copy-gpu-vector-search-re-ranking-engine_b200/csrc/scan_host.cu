@@ -300,10 +300,47 @@ int launch(const ScanPlan& plan, ScanParams& params, cudaStream_t stream) {
 
 }  // namespace zc
 
+namespace zc {
+namespace {
+
+// Large batches over per-row int8 corpora run on the tensor cores (zcgvs_gemm_topk): the same
+// exact int32 dot products, so the same results bit for bit. Smaller problems stay on the
+// streaming scan, whose single pass has no fixed cost.
+constexpr int kGemmMinBatch = 64;
+constexpr long long kGemmMinDocs = 65536;
+
+bool gemm_eligible(int dtype, long long n, int dim, int batch, int metric) {
+    return dtype == ZCGVS_DTYPE_I8_ROW && batch >= kGemmMinBatch && n >= kGemmMinDocs && dim % 128 == 0 &&
+           (metric == ZCGVS_METRIC_DOT || metric == ZCGVS_METRIC_COSINE);
+}
+
+}  // namespace
+}  // namespace zc
+
 extern "C" {
 
 size_t zcgvs_scan_topk_workspace_bytes(int dtype, int64_t doc_count, int dim, int batch, int k) {
     if (doc_count <= 0 || dim <= 0 || batch <= 0 || k <= 0) return 0;
+    if (zc::gemm_eligible(dtype, doc_count, dim, batch, ZCGVS_METRIC_DOT)) {
+        const size_t gemm = zcgvs_gemm_topk_workspace_bytes(dtype, doc_count, dim, batch, k);
+        zc::ok();
+        // Either path may run (the tensor-core one needs a 256-byte aligned workspace).
+        size_t generic = 0;
+        const int metrics[2] = {ZCGVS_METRIC_DOT, ZCGVS_METRIC_L2};
+        for (const int metric : metrics) {
+            for (const bool aligned : {true, false}) {
+                for (const bool has_mask : {true, false}) {
+                    zc::ScanPlan plan;
+                    if (zc::make_plan(dtype, doc_count, dim, batch, std::min(k, ZCGVS_MAX_K), metric, false, aligned,
+                                      has_mask, plan) == ZCGVS_OK) {
+                        generic = std::max(generic, plan.ws_total);
+                    }
+                }
+            }
+        }
+        zc::ok();
+        return std::max(generic, gemm);
+    }
     // The plan may differ with the corpus alignment (bulk-copy vs plain staging) and the
     // metric, so report the largest workspace any of them needs.
     size_t bytes = 0;
@@ -431,6 +468,12 @@ int zcgvs_scan_topk(const void* corpus, int dtype, float scale, const float* row
         return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: workspace smaller than zcgvs_scan_topk_workspace_bytes()");
     }
     if (!aligned16(workspace)) return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: workspace must be 16-byte aligned");
+    if (gemm_eligible(dtype, doc_count, dim, batch, metric) && (reinterpret_cast<uintptr_t>(workspace) & 255u) == 0 &&
+        (reinterpret_cast<uintptr_t>(corpus) & 15u) == 0 &&
+        workspace_bytes >= zcgvs_gemm_topk_workspace_bytes(dtype, doc_count, dim, batch, k)) {
+        return zcgvs_gemm_topk(corpus, dtype, row_scales, doc_count, dim, queries, batch, mask, metric, k, id_base,
+                               out_indices, out_scores, workspace, workspace_bytes, stream);
+    }
     return run_scan_topk(plan, corpus, scale, row_scales, doc_count, dim, queries, batch, mask, k, id_base,
                          out_indices, out_scores, static_cast<uint8_t*>(workspace), HybridArgs{},
                          static_cast<cudaStream_t>(stream));
