@@ -1,19 +1,31 @@
 """Benchmark of the search hot path on B200 (one process per GPU).
 
-Workload: int8 search, top-100, corpus N = 1,000,000 x d = 768 rows drawn
-N(0,1), L2-normalised, symmetric per-row int8 quantised (fp32 scale per row); fp32 queries
-quantised the same way inside the kernel; scores int32 dot x s_q x s_row. A step is one fused
-scan + top-k call over one batch of queries (default batch 1, the HBM-bound streaming case).
+Default workload (the one its headline metric is quoted on): int8 search,
+top-100, corpus N = 1,000,000 x d = 768 rows drawn N(0,1), L2-normalised, symmetric per-row
+int8 quantised (fp32 scale per row); fp32 queries quantised the same way inside the kernel;
+scores int32 dot x s_q x s_row. A step is one fused scan + top-k call over one batch of
+queries (default batch 1, the HBM-bound streaming case).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--batch B] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+                    [--workload cfg2|cfg2_b1024|cfg1|cfg3|cfg4|cfg5] [--batch B]
 
-N > 1 runs under torchrun as query-parallel replicas (the 772 MB corpus fits every GPU; there
-is no exchange step, so no collective on the data path): each rank scans its own queries
-against its own copy, timing is the max over ranks and `value` is all ranks' queries / time.
+The other BASELINE configs run the same timing contract through --workload:
+  cfg1       exact fp32 inner product, 5,183 x 384, top-10, batch 1 (latency-bound, L2-resident)
+  cfg2_b1024 config 2 at batch 1,024 (the tensor-core path)
+  cfg3       1-bit codes 10M x 1024 -> Hamming top-1,000 -> fp16 rescore to top-10, batch 64
+  cfg4       fp16 50M x 768, batch 4,096, top-100 (tensor cores); N > 1 shards rows
+  cfg5       hybrid BM25 + fp16 dense (2M docs, d = 384), top-10, batch 1
+All inputs are seeded synthetic data with the BASELINE shapes and distributions (no datasets
+are available offline).
+
+N > 1 runs under torchrun, one rank per GPU. Configs whose corpus fits one GPU run
+query-parallel replicas (no collective on the data path, "scaling": "weak"); cfg4 shards its
+rows across the ranks and merges the per-shard top-k with one NCCL all-gather per step
+("scaling": "strong"). Timing is the max over ranks.
 
 --impl reference times the reference's own CPU search path (cpuCosineSimilarity +
-cpuTopKIndices from tests/cpp/cpu_reference.hpp, built into oracle/_ref) on all host cores, on
-the same corpus dequantised to fp32, each step a bounded sample of queries.
+cpuTopKIndices from tests/cpp/cpu_reference.hpp, built into oracle/_ref) on all host cores,
+on the same corpus dequantised to fp32, each step a bounded sample of queries.
 """
 
 from __future__ import annotations
@@ -33,12 +45,6 @@ ROOT = Path(__file__).resolve().parent
 PKG = ROOT / "zero-copy-gpu-vector-search-re-ranking-engine_b200"
 sys.path.insert(0, str(PKG))
 
-N_DOCS = 1_000_000
-DIM = 768
-TOP_K = 100
-NUM_QUERIES = 1024
-CORPUS_SEED = 2001
-QUERY_SEED = 2002
 METRIC = "queries/sec and p50 query latency at 1/2/4/8 B200; scan HBM GB/s vs peak"
 UNIT = "queries/s"
 
@@ -46,9 +52,11 @@ UNIT = "queries/s"
 def parse_args():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=200)
-    ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--batch", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=None)
+    ap.add_argument("--warmup", type=int, default=None)
+    ap.add_argument("--batch", type=int, default=None)
+    ap.add_argument("--workload", default="cfg2",
+                    choices=["cfg1", "cfg2", "cfg2_b1024", "cfg3", "cfg4", "cfg5"])
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     return ap.parse_args()
@@ -59,29 +67,70 @@ def dist_env():
             int(os.environ.get("WORLD_SIZE", "1")))
 
 
-def make_corpus(torch, device, seed):
-    """N(0,1) rows, L2-normalised in fp32, per-row int8: s = max|x|/127, q = clamp(rint(x/s))."""
-    g = torch.Generator(device=device)
-    g.manual_seed(seed)
-    codes = torch.empty((N_DOCS, DIM), dtype=torch.int8, device=device)
-    scales = torch.empty(N_DOCS, dtype=torch.float32, device=device)
-    chunk = 100_000
-    for start in range(0, N_DOCS, chunk):
-        x = torch.randn((min(chunk, N_DOCS - start), DIM), generator=g, device=device, dtype=torch.float32)
-        x = x / x.norm(dim=1, keepdim=True)
-        s = x.abs().amax(dim=1) / 127.0
-        s = torch.where(s > 0, s, torch.ones_like(s))
-        q = torch.round(x * (1.0 / s)[:, None]).clamp_(-127, 127).to(torch.int8)
-        codes[start:start + q.shape[0]] = q
-        scales[start:start + q.shape[0]] = s
-    return codes, scales
+def measured_peaks():
+    try:
+        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text()), "measured"
+    except (OSError, ValueError):
+        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
 
 
-def make_queries(torch, device, seed, count):
-    g = torch.Generator(device=device)
-    g.manual_seed(seed)
-    x = torch.randn((count, DIM), generator=g, device=device, dtype=torch.float32)
-    return (x / x.norm(dim=1, keepdim=True)).contiguous()
+def profiled_traffic(workload: str):
+    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary, if any."""
+    try:
+        return json.loads((ROOT / "profiles" / "traffic.json").read_text()).get(workload)
+    except (OSError, ValueError):
+        return None
+
+
+def oracle_mod():
+    sys.path.insert(0, str(ROOT / "oracle"))
+    import oracle
+
+    return oracle
+
+
+def ref_cpu():
+    """The reference's own CPU search library (oracle/_ref), building it if the tree is here."""
+    oracle = oracle_mod()
+    ref = oracle.ref_lib()
+    if ref is None:
+        try:
+            oracle.build()
+        except Exception:  # noqa: BLE001 - building the reference needs its tree
+            pass
+        ref = oracle.ref_lib()
+    return ref
+
+
+def ref_search_rate(corpus_f32, queries, k, budget_s, rows_total=None):
+    """Queries/s of the reference CPU path (cpuCosineSimilarity + cpuTopKIndices, all host
+    threads) over `corpus_f32`, in chunks of one query per thread until about `budget_s` of CPU
+    time. When the corpus is a row prefix of `rows_total` rows the rate is scaled by
+    prefix / total (the path is linear in the rows)."""
+    import ctypes
+
+    ref = ref_cpu()
+    if ref is None:
+        return None
+    threads = os.cpu_count() or 1
+    corpus_f32 = np.ascontiguousarray(corpus_f32, dtype=np.float32)
+    n, d = corpus_f32.shape
+    chunk = max(1, min(len(queries), threads))
+    out = np.empty((chunk, k), dtype=np.int32)
+    done, elapsed = 0, 0.0
+    while done < len(queries) and (done == 0 or elapsed < budget_s):
+        q = np.ascontiguousarray(queries[done:done + chunk], dtype=np.float32)
+        elapsed += ref.refcpu_search(corpus_f32.ctypes.data_as(ctypes.c_void_p), n, d,
+                                     q.ctypes.data_as(ctypes.c_void_p), q.shape[0], k, threads,
+                                     out.ctypes.data_as(ctypes.c_void_p))
+        done += q.shape[0]
+    rate = done / elapsed
+    scale = 1.0 if rows_total is None else n / rows_total
+    return {"value": rate * scale, "unit": UNIT, "cores": min(threads, chunk), "kind": "reference",
+            "sample": (f"{done} queries x {n}x{d} fp32 corpus, cpuCosineSimilarity + cpuTopKIndices, "
+                       f"{min(threads, chunk)} threads" +
+                       ("" if rows_total is None else f"; extrapolated to {rows_total} rows (x{scale:.4g})")),
+            "seconds": elapsed}
 
 
 class ClockSampler:
@@ -187,105 +236,484 @@ class ClockSampler:
                 "source": "nvml" if self.nvml is not None else "nvidia-smi"}
 
 
-def measured_peaks():
-    try:
-        return json.loads((ROOT / "MEASURED_PEAKS.json").read_text()), "measured"
-    except (OSError, ValueError):
-        return {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0}, "fallback"
+def normal_rows(torch, device, rows, dim, seed, dtype, chunk=1 << 20):
+    """N(0,1) rows, L2-normalised in fp32, stored as `dtype`; generated chunk by chunk."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    out = torch.empty((rows, dim), dtype=dtype, device=device)
+    for start in range(0, rows, chunk):
+        x = torch.randn((min(chunk, rows - start), dim), generator=g, device=device, dtype=torch.float32)
+        out[start:start + x.shape[0]] = (x / x.norm(dim=1, keepdim=True)).to(dtype)
+    return out
 
 
-def profiled_traffic(workload: str):
-    """Per-launch DRAM bytes of the dominant kernel from the committed ncu summary, if any."""
-    path = ROOT / "profiles" / "traffic.json"
-    try:
-        return json.loads(path.read_text()).get(workload)
-    except (OSError, ValueError):
-        return None
+def int8_rows(torch, device, rows, dim, seed, chunk=1 << 17):
+    """N(0,1) rows, L2-normalised in fp32, per-row int8: s = max|x|/127, q = clamp(rint(x/s))."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    codes = torch.empty((rows, dim), dtype=torch.int8, device=device)
+    scales = torch.empty(rows, dtype=torch.float32, device=device)
+    for start in range(0, rows, chunk):
+        x = torch.randn((min(chunk, rows - start), dim), generator=g, device=device, dtype=torch.float32)
+        x = x / x.norm(dim=1, keepdim=True)
+        s = x.abs().amax(dim=1) / 127.0
+        s = torch.where(s > 0, s, torch.ones_like(s))
+        codes[start:start + x.shape[0]] = torch.round(x * (1.0 / s)[:, None]).clamp_(-127, 127).to(torch.int8)
+        scales[start:start + x.shape[0]] = s
+    return codes, scales
 
 
-def cpu_baseline(codes_host, scales_host, queries_host, budget_s=12.0):
-    """Times the reference CPU path on a bounded query sample; returns the cpu_baseline dict."""
-    sys.path.insert(0, str(ROOT / "oracle"))
-    import ctypes
+def pack_signs(torch, x):
+    """Sign bits of fp rows: bit b of word w = dim 32 w + b, set when x >= 0 (the reference's
+    launchPackBinary convention)."""
+    rows, dim = x.shape
+    bits = (x >= 0).to(torch.int64).reshape(rows, dim // 32, 32)
+    weights = torch.ones(32, dtype=torch.int64, device=x.device) << torch.arange(32, device=x.device)
+    words = (bits * weights).sum(dim=2)
+    return torch.where(words >= 2 ** 31, words - 2 ** 32, words).to(torch.int32).contiguous()
 
-    import oracle
 
-    threads = os.cpu_count() or 1
-    ref = oracle.ref_lib()
-    if ref is None:
-        try:
-            oracle.build()
-        except Exception:  # noqa: BLE001 - building the reference needs its tree
-            pass
-        ref = oracle.ref_lib()
-    if ref is not None:
-        corpus = codes_host.astype(np.float32) * scales_host[:, None]
-        # Chunks of one query per thread until about `budget_s` of CPU time (or the query set)
-        # is used up.
-        chunk = max(1, min(len(queries_host), threads))
-        out = np.empty((chunk, TOP_K), dtype=np.int32)
-        done, elapsed = 0, 0.0
-        while done < len(queries_host) and (done == 0 or elapsed < budget_s):
-            q = np.ascontiguousarray(queries_host[done:done + chunk])
-            elapsed += ref.refcpu_search(corpus.ctypes.data_as(ctypes.c_void_p), N_DOCS, DIM,
-                                         q.ctypes.data_as(ctypes.c_void_p), q.shape[0], TOP_K, threads,
-                                         out.ctypes.data_as(ctypes.c_void_p))
-            done += q.shape[0]
-        return {"value": done / elapsed, "unit": UNIT, "cores": min(threads, chunk), "kind": "reference",
-                "sample": f"{done} queries x full {N_DOCS}x{DIM} corpus (dequantised fp32), "
-                          f"cpuCosineSimilarity + cpuTopKIndices, {min(threads, chunk)} threads",
+# --------------------------------------------------------------------------------------------
+# Workloads
+# --------------------------------------------------------------------------------------------
+class Workload:
+    """A BASELINE configuration: inputs on the device, one step, an end-to-end step through host
+    buffers, and the roofline / CPU-baseline bookkeeping of its dominant kernel."""
+
+    scaling = "weak"
+    steps, warmup = 200, 10
+
+    @staticmethod
+    def tensor_peak(peaks, kind):
+        # int8 dense tensor peak: twice the measured bf16 burst (B200 int8 : bf16 = 2 : 1 dense).
+        if kind == "i8":
+            return 2.0 * float(peaks["bf16_tflops"]), "2 x measured bf16 burst (int8 dense = 2 x bf16 dense)"
+        return float(peaks["bf16_tflops"]), "measured bf16 burst"
+
+
+class Cfg2(Workload):
+    """per-row int8 1M x 768, top-100."""
+
+    N, D, K, NQ = 1_000_000, 768, 100, 1024
+    dtype = "int8"
+
+    def __init__(self, batch):
+        self.B = batch
+        self.name = f"cfg2_int8row_1Mx768_top100_b{batch}"
+        if batch >= 64:
+            self.steps, self.warmup = 20, 3
+
+    units = property(lambda self: self.B)
+    launches = property(lambda self: 12 if self.B >= 64 else 1)
+
+    def setup(self, torch, zc, device, rank, world):
+        self.torch, self.zc = torch, zc
+        self.codes, self.scales = int8_rows(torch, device, self.N, self.D, 2001)
+        self.queries = normal_rows(torch, device, self.NQ, self.D, 2002 + rank, torch.float32)
+        self.ws = zc.Workspace(device)
+        self.out = (torch.empty((self.B, self.K), dtype=torch.int32, device=device),
+                    torch.empty((self.B, self.K), dtype=torch.float32, device=device))
+        self.h_queries = self.queries.cpu().pin_memory()
+        self.h_out = (torch.empty((self.B, self.K), dtype=torch.int32).pin_memory(),
+                      torch.empty((self.B, self.K), dtype=torch.float32).pin_memory())
+        self.d_q = torch.empty((self.B, self.D), dtype=torch.float32, device=device)
+
+    def _q(self, i, src):
+        nb = max(1, self.NQ // self.B)
+        j = (i % nb) * self.B
+        return src[j:j + self.B]
+
+    def step(self, i, stream):
+        self.zc.scan_topk(self.codes, self.zc.DTYPE_I8_ROW, self.D, self._q(i, self.queries), self.K,
+                          row_scales=self.scales, workspace=self.ws, out=self.out, stream=stream)
+
+    def e2e_step(self, i, stream):
+        self.d_q.copy_(self._q(i, self.h_queries), non_blocking=True)
+        self.zc.scan_topk(self.codes, self.zc.DTYPE_I8_ROW, self.D, self.d_q, self.K, row_scales=self.scales,
+                          workspace=self.ws, out=self.out, stream=stream)
+        self.h_out[0].copy_(self.out[0], non_blocking=True)
+        self.h_out[1].copy_(self.out[1], non_blocking=True)
+        stream.synchronize()
+        return self.B * self.D * 4, self.B * self.K * 8
+
+    def config(self, world):
+        return {"workload": self.name, "docs": self.N, "dim": self.D, "k": self.K, "batch": self.B,
+                "storage": "int8 per-row scale", "parallelism": f"replicas{world}",
+                "l2": "inputs larger than L2 (772 MB corpus vs 126 MB L2)"}
+
+    def roofline(self, kernel_ms, peaks, peak_kind):
+        if self.B >= 64:
+            ops = 2.0 * self.B * self.N * self.D
+            achieved = ops / (kernel_ms * 1e-3) / 1e12
+            peak, src = self.tensor_peak(peaks, "i8")
+            return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s", "frac": achieved / peak,
+                    "traffic": profiled_traffic(self.name), "peak_source": f"{peak_kind}: {src}",
+                    "kernel": "zc::gemm::gemm_scan_kernel<kModeI8R,kFilter> (+ sample, threshold, select)",
+                    "algorithmic_ops_per_step": ops}
+        algo = self.N * (self.D + 4) + self.B * self.D * 4 + self.B * self.K * 8
+        achieved = algo / (kernel_ms * 1e-3) / 1e9
+        peak = float(peaks["hbm_gbs"])
+        return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "traffic": profiled_traffic(self.name), "peak_source": peak_kind,
+                "kernel": "zc::scan_fast_kernel<kModeI8R,3>" if self.B == 1 else "zc::scan_kernel<kModeI8R,QB>",
+                "algorithmic_bytes_per_launch": algo}
+
+    def reference_corpus(self):
+        return (self.codes.float() * self.scales[:, None]).cpu().numpy()
+
+    def cpu_baseline(self, budget_s):
+        return ref_search_rate(self.reference_corpus(), self.queries.cpu().numpy(), self.K, budget_s)
+
+
+class Cfg1(Workload):
+    """exact fp32 inner product, 5,183 x 384, top-10, 300 queries, batch 1."""
+
+    N, D, K, NQ, B = 5183, 384, 10, 300, 1
+    name = "cfg1_f32_5183x384_top10_b1"
+    dtype = "f32"
+    units = 1
+    launches = 1
+    steps, warmup = 300, 10
+
+    def setup(self, torch, zc, device, rank, world):
+        self.torch, self.zc = torch, zc
+        self.corpus = normal_rows(torch, device, self.N, self.D, 1001, torch.float32)
+        self.queries = normal_rows(torch, device, self.NQ, self.D, 1002 + rank, torch.float32)
+        self.ws = zc.Workspace(device)
+        self.out = (torch.empty((1, self.K), dtype=torch.int32, device=device),
+                    torch.empty((1, self.K), dtype=torch.float32, device=device))
+        self.h_queries = self.queries.cpu().pin_memory()
+        self.h_out = (torch.empty((1, self.K), dtype=torch.int32).pin_memory(),
+                      torch.empty((1, self.K), dtype=torch.float32).pin_memory())
+        self.d_q = torch.empty((1, self.D), dtype=torch.float32, device=device)
+
+    def step(self, i, stream):
+        j = i % self.NQ
+        self.zc.scan_topk(self.corpus, self.zc.DTYPE_F32, self.D, self.queries[j:j + 1], self.K,
+                          metric=self.zc.METRIC_COSINE, workspace=self.ws, out=self.out, stream=stream)
+
+    def e2e_step(self, i, stream):
+        j = i % self.NQ
+        self.d_q.copy_(self.h_queries[j:j + 1], non_blocking=True)
+        self.zc.scan_topk(self.corpus, self.zc.DTYPE_F32, self.D, self.d_q, self.K, metric=self.zc.METRIC_COSINE,
+                          workspace=self.ws, out=self.out, stream=stream)
+        self.h_out[0].copy_(self.out[0], non_blocking=True)
+        self.h_out[1].copy_(self.out[1], non_blocking=True)
+        stream.synchronize()
+        return self.D * 4, self.K * 8
+
+    def config(self, world):
+        return {"workload": self.name, "docs": self.N, "dim": self.D, "k": self.K, "batch": 1,
+                "storage": "fp32", "metric": "cosine", "parallelism": f"replicas{world}",
+                "l2": "corpus (7.96 MB) is L2-resident: latency-bound, no flush between steps"}
+
+    def roofline(self, kernel_ms, peaks, peak_kind):
+        algo = self.N * self.D * 4 + self.D * 4 + self.K * 8
+        achieved = algo / (kernel_ms * 1e-3) / 1e9
+        peak = float(peaks["hbm_gbs"])
+        return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "traffic": profiled_traffic(self.name), "peak_source": peak_kind,
+                "kernel": "zc::scan_fast_kernel<kModeF32,JC>", "algorithmic_bytes_per_launch": algo,
+                "note": "L2-resident corpus: the bound is launch latency, the fraction is not an HBM efficiency"}
+
+    def reference_corpus(self):
+        return self.corpus.cpu().numpy()
+
+    def cpu_baseline(self, budget_s):
+        return ref_search_rate(self.reference_corpus(), self.queries.cpu().numpy(), self.K, budget_s)
+
+
+class Cfg3(Workload):
+    """1-bit codes (128 B/row) of 10M x 1024 fp16 rows, Hamming top-1,000,
+    fp16 rescore to top-10, batch 64."""
+
+    N, D, M, K, B, NQ = 10_000_000, 1024, 1000, 10, 64, 4096
+    name = "cfg3_bin1024_10M_top1000_f16rescore_top10_b64"
+    dtype = "u32 (xor+popc) / f16"
+    units = 64
+    launches = 2
+    steps, warmup = 10, 3
+
+    def setup(self, torch, zc, device, rank, world):
+        self.torch, self.zc = torch, zc
+        self.store = normal_rows(torch, device, self.N, self.D, 3001, torch.float16)
+        self.codes = torch.empty((self.N, self.D // 32), dtype=torch.int32, device=device)
+        step = 1 << 20
+        for s in range(0, self.N, step):
+            self.codes[s:s + step] = pack_signs(torch, self.store[s:s + step])
+        self.queries = normal_rows(torch, device, self.NQ, self.D, 3002 + rank, torch.float32)
+        self.ws = zc.Workspace(device)
+        self.cand = (torch.empty((self.B, self.M), dtype=torch.int32, device=device),
+                     torch.empty((self.B, self.M), dtype=torch.float32, device=device))
+        self.out = (torch.empty((self.B, self.K), dtype=torch.int32, device=device),
+                    torch.empty((self.B, self.K), dtype=torch.float32, device=device))
+        self.h_queries = self.queries.cpu().pin_memory()
+        self.h_out = (torch.empty((self.B, self.K), dtype=torch.int32).pin_memory(),
+                      torch.empty((self.B, self.K), dtype=torch.float32).pin_memory())
+        self.d_q = torch.empty((self.B, self.D), dtype=torch.float32, device=device)
+        self.store_i16 = self.store.view(torch.int16)
+
+    def _run(self, q, stream):
+        self.zc.scan_topk(self.codes, self.zc.DTYPE_BINARY, self.D, q, self.M, workspace=self.ws, out=self.cand,
+                          stream=stream)
+        self.zc.rescore_topk(self.store_i16, self.zc.DTYPE_F16, self.D, q, self.cand[0], self.K,
+                             metric=self.zc.METRIC_COSINE, out=self.out, stream=stream)
+
+    def step(self, i, stream):
+        j = (i % (self.NQ // self.B)) * self.B
+        self._run(self.queries[j:j + self.B], stream)
+
+    def e2e_step(self, i, stream):
+        j = (i % (self.NQ // self.B)) * self.B
+        self.d_q.copy_(self.h_queries[j:j + self.B], non_blocking=True)
+        self._run(self.d_q, stream)
+        self.h_out[0].copy_(self.out[0], non_blocking=True)
+        self.h_out[1].copy_(self.out[1], non_blocking=True)
+        stream.synchronize()
+        return self.B * self.D * 4, self.B * self.K * 8
+
+    def config(self, world):
+        return {"workload": self.name, "docs": self.N, "dim": self.D, "candidates": self.M, "k": self.K,
+                "batch": self.B, "storage": "1-bit codes + fp16 rescore store", "parallelism": f"replicas{world}",
+                "l2": "inputs larger than L2 (1.28 GB codes, 20.5 GB rescore store)"}
+
+    def roofline(self, kernel_ms, peaks, peak_kind):
+        # Dominant: the Hamming scan; algorithmic bytes = the codes once + the gathered rows.
+        algo = self.N * (self.D // 8) + self.B * self.M * self.D * 2 + self.B * self.D * 4
+        achieved = algo / (kernel_ms * 1e-3) / 1e9
+        peak = float(peaks["hbm_gbs"])
+        return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "traffic": profiled_traffic(self.name), "peak_source": peak_kind,
+                "kernel": "zc::scan_kernel<kModeBin,8> + zc::rescore_kernel<kModeF16>",
+                "algorithmic_bytes_per_step": algo}
+
+    def cpu_baseline(self, budget_s):
+        # The reference CPU path scans fp32 rows; time it on a 200k-row prefix and scale.
+        prefix = 200_000
+        corpus = self.store[:prefix].float().cpu().numpy()
+        return ref_search_rate(corpus, self.queries[:256].cpu().numpy(), self.K, budget_s, rows_total=self.N)
+
+
+class Cfg4(Workload):
+    """fp16 50M x 768, batch 4,096, top-100 (tensor cores). With N ranks the
+    rows are split into N shards; each rank searches its shard (global ids via id_base), one NCCL
+    all-gather exchanges the [4096, 100] results and zcgvs_merge_topk merges them."""
+
+    N, D, K, B = 50_000_000, 768, 100, 4096
+    name = "cfg4_f16_50Mx768_top100_b4096"
+    dtype = "f16"
+    units = 4096
+    steps, warmup = 6, 3
+    scaling = "strong"
+
+    def setup(self, torch, zc, device, rank, world):
+        import sharded
+
+        self.torch, self.zc, self.world = torch, zc, world
+        self.begin, self.end = sharded.shard_bounds(self.N, world, rank)
+        rows = self.end - self.begin
+        # Each 1M-row block of the global corpus has its own seed, so a shard holds the same rows
+        # whatever the number of ranks.
+        self.shard = torch.empty((rows, self.D), dtype=torch.float16, device=device)
+        blk = 1 << 20
+        for b0 in range(self.begin // blk * blk, self.end, blk):
+            block = normal_rows(torch, device, min(blk, self.N - b0), self.D, 4001 + b0 // blk, torch.float16)
+            lo, hi = max(b0, self.begin), min(b0 + block.shape[0], self.end)
+            self.shard[lo - self.begin:hi - self.begin] = block[lo - b0:hi - b0]
+            del block
+        self.shard_i16 = self.shard.view(torch.int16)
+        self.queries = normal_rows(torch, device, self.B, self.D, 4002, torch.float16).float()
+        self.ws = zc.Workspace(device)
+
+        def gemm_local(q, k, id_base):
+            return zc.gemm_topk(self.shard_i16, zc.DTYPE_F16, self.D, q, k, metric=zc.METRIC_COSINE,
+                                id_base=id_base, workspace=self.ws)
+
+        self.gemm_local = gemm_local
+        self.search = sharded.ShardedSearch(self.begin, gemm_local) if world > 1 else None
+        self.h_queries = self.queries.cpu().pin_memory()
+        self.d_q = torch.empty_like(self.queries)
+
+    launches = property(lambda self: 12 if self.world == 1 else 13)
+
+    def _run(self, q):
+        if self.world == 1:
+            return self.gemm_local(q, self.K, 0)
+        return self.search.search(q, self.K)
+
+    def step(self, i, stream):
+        self._run(self.queries)
+
+    def e2e_step(self, i, stream):
+        self.d_q.copy_(self.h_queries, non_blocking=True)
+        ids, scores = self._run(self.d_q)
+        ids.cpu()
+        scores.cpu()
+        return self.B * self.D * 4, self.B * self.K * 8
+
+    def config(self, world):
+        return {"workload": self.name, "docs": self.N, "dim": self.D, "k": self.K, "batch": self.B,
+                "storage": "fp16", "metric": "cosine", "parallelism": f"rowshard{world}",
+                "l2": "inputs larger than L2 (77 GB corpus)"}
+
+    def roofline(self, kernel_ms, peaks, peak_kind):
+        rows = self.end - self.begin
+        flops = 2.0 * self.B * rows * self.D
+        achieved = flops / (kernel_ms * 1e-3) / 1e12
+        peak, src = self.tensor_peak(peaks, "f16")
+        return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
+                "traffic": profiled_traffic(self.name), "peak_source": f"{peak_kind}: {src}",
+                "kernel": "zc::gemm::gemm_scan_kernel<kModeF16,kFilter> (+ sample, threshold, select)",
+                "algorithmic_flops_per_step_per_gpu": flops}
+
+    def cpu_baseline(self, budget_s):
+        prefix = 200_000
+        corpus = self.shard[:prefix].float().cpu().numpy()
+        return ref_search_rate(corpus, self.queries[:256].cpu().numpy(), self.K, budget_s, rows_total=self.N)
+
+
+class Cfg5(Workload):
+    """hybrid BM25 + fp16 dense, 2M docs, d = 384, top-10, batch 1. Token
+    counts ~ Poisson(200), terms ~ Zipf(1.1) over 30,000, BM25 k1 = 0.9, b = 0.4; queries of
+    3-12 Zipf terms, de-duplicated; score = 0.5 * dense + 0.5 * lex / max(lex)."""
+
+    N, D, K, V, NQ = 2_000_000, 384, 10, 30_000, 1000
+    name = "cfg5_hybrid_bm25_f16_2Mx384_top10_b1"
+    dtype = "f16 + f32"
+    units = 1
+    launches = 2
+    steps, warmup = 200, 10
+
+    def setup(self, torch, zc, device, rank, world):
+        import lexical_index as li
+
+        self.torch, self.zc = torch, zc
+        offsets, docs, weights = li.synthetic_corpus(self.N, self.V, 200.0, 1.1, 5001, device=device, k1=0.9, b=0.4)
+        self.index = zc.LexicalIndex(offsets, docs, weights, device=device)
+        self.offsets_h = offsets.cpu().numpy()
+        self.dense = normal_rows(torch, device, self.N, self.D, 5002, torch.float16)
+        self.dense_i16 = self.dense.view(torch.int16)
+        self.queries = normal_rows(torch, device, self.NQ, self.D, 5003 + rank, torch.float32)
+        self.terms_h = li.synthetic_queries(self.NQ, self.V, 1.1, 5004 + rank)
+        self.terms = torch.from_numpy(self.terms_h).to(device)
+        self.ws = zc.Workspace(device)
+        self.out = (torch.empty((1, self.K), dtype=torch.int32, device=device),
+                    torch.empty((1, self.K), dtype=torch.float32, device=device))
+        self.h_queries = self.queries.cpu().pin_memory()
+        self.h_terms = torch.from_numpy(self.terms_h).pin_memory()
+        self.h_out = (torch.empty((1, self.K), dtype=torch.int32).pin_memory(),
+                      torch.empty((1, self.K), dtype=torch.float32).pin_memory())
+        self.d_q = torch.empty((1, self.D), dtype=torch.float32, device=device)
+        self.d_t = torch.empty((1, self.terms_h.shape[1]), dtype=torch.int32, device=device)
+        df = np.diff(self.offsets_h)
+        self.sum_df = [int(df[t[t >= 0]].sum()) for t in self.terms_h]
+
+    def _run(self, q, t, stream):
+        self.zc.hybrid_topk(self.dense_i16, self.zc.DTYPE_F16, self.D, q, self.K, self.index, t, 0.5,
+                            metric=self.zc.METRIC_COSINE, workspace=self.ws, out=self.out, stream=stream)
+
+    def step(self, i, stream):
+        j = i % self.NQ
+        self._run(self.queries[j:j + 1], self.terms[j:j + 1], stream)
+
+    def e2e_step(self, i, stream):
+        j = i % self.NQ
+        self.d_q.copy_(self.h_queries[j:j + 1], non_blocking=True)
+        self.d_t.copy_(self.h_terms[j:j + 1], non_blocking=True)
+        self._run(self.d_q, self.d_t, stream)
+        self.h_out[0].copy_(self.out[0], non_blocking=True)
+        self.h_out[1].copy_(self.out[1], non_blocking=True)
+        stream.synchronize()
+        return self.D * 4 + self.terms_h.shape[1] * 4, self.K * 8
+
+    def config(self, world):
+        return {"workload": self.name, "docs": self.N, "dim": self.D, "vocab": self.V, "k": self.K, "batch": 1,
+                "storage": "fp16 dense + CSR BM25 (k1 0.9, b 0.4)", "dense_weight": 0.5,
+                "mean_sum_df": float(np.mean(self.sum_df)), "parallelism": f"replicas{world}",
+                "l2": "inputs larger than L2 (1.54 GB dense)"}
+
+    def roofline(self, kernel_ms, peaks, peak_kind):
+        algo = self.N * self.D * 2 + 8 * float(np.mean(self.sum_df)) + self.N * 4 * 2 + self.D * 4
+        achieved = algo / (kernel_ms * 1e-3) / 1e9
+        peak = float(peaks["hbm_gbs"])
+        return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
+                "traffic": profiled_traffic(self.name), "peak_source": peak_kind,
+                "kernel": "zc::lexical_kernel + zc::scan_fast_kernel<kModeF16,JC> (blend)",
+                "algorithmic_bytes_per_step": algo,
+                "note": "bytes = dense rows + 8 B per posting of the query's terms + lexical scores written and read"}
+
+    def cpu_baseline(self, budget_s):
+        oracle = oracle_mod()
+        dense_bits = self.dense.view(self.torch.int16).cpu().numpy().view(np.uint16)
+        docs = self.index.docs.cpu().numpy()
+        weights = self.index.weights.cpu().numpy()
+        queries = self.queries.cpu().numpy()
+        done, t0 = 0, time.perf_counter()
+        while done < 64 and (done == 0 or time.perf_counter() - t0 < budget_s):
+            oracle.hybrid_topk(dense_bits, oracle.DTYPE_F16, self.D, queries[done:done + 1], self.K, self.offsets_h,
+                               docs, weights, self.V, self.terms_h[done:done + 1], 0.5,
+                               metric=oracle.METRIC_COSINE)
+            done += 1
+        elapsed = time.perf_counter() - t0
+        return {"value": done / elapsed, "unit": UNIT, "cores": 1, "kind": "port",
+                "sample": f"{done} queries over the full corpus, oracle hybrid (reference loops restated), 1 thread",
                 "seconds": elapsed}
-    # Oracle port fallback (single thread, exact per-row int8 arithmetic).
-    sample = 2
-    t0 = time.perf_counter()
-    oracle.scan_topk(codes_host, oracle.DTYPE_I8_ROW, DIM, queries_host[:sample], TOP_K, row_scales=scales_host)
-    elapsed = time.perf_counter() - t0
-    return {"value": sample / elapsed, "unit": UNIT, "cores": 1, "kind": "port",
-            "sample": f"{sample} queries x full corpus, oracle/oracle.c, 1 thread", "seconds": elapsed}
 
 
+def make_workload(args):
+    if args.workload == "cfg2":
+        return Cfg2(args.batch or 1)
+    if args.workload == "cfg2_b1024":
+        return Cfg2(args.batch or 1024)
+    return {"cfg1": Cfg1, "cfg3": Cfg3, "cfg4": Cfg4, "cfg5": Cfg5}[args.workload]()
+
+
+# --------------------------------------------------------------------------------------------
+# Arms
+# --------------------------------------------------------------------------------------------
 def run_reference(args):
+    """The reference's CPU search path (all host threads) on the workload's corpus, as fp32."""
     rank, _, world = dist_env()
     if rank != 0:
         return
-    import torch
-
-    device = "cuda" if torch.cuda.is_available() else "cpu"
-    codes, scales = make_corpus(torch, device, CORPUS_SEED)
-    queries = make_queries(torch, device, QUERY_SEED, NUM_QUERIES)
-    codes_h, scales_h, q_h = codes.cpu().numpy(), scales.cpu().numpy(), queries.cpu().numpy()
-    del codes, scales
-    sys.path.insert(0, str(ROOT / "oracle"))
     import ctypes
 
-    import oracle
+    import torch
 
-    ref = oracle.ref_lib()
-    threads = os.cpu_count() or 1
+    wl = make_workload(args)
+    steps = args.steps if args.steps is not None else wl.steps
+    warmup = args.warmup if args.warmup is not None else wl.warmup
+    if not isinstance(wl, (Cfg1, Cfg2)):
+        print(json.dumps({"impl": "reference", "unavailable":
+                          f"{wl.name}: the reference CPU path over the full corpus takes minutes per step; "
+                          "the ours line carries a bounded, extrapolated cpu_baseline"}))
+        return
+    ref = ref_cpu()
     if ref is None:
         print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libzcgvs_refcpu.so was not built"}))
         return
-    corpus = codes_h.astype(np.float32) * scales_h[:, None]
-    sample = max(1, min(NUM_QUERIES, threads))
+    device = "cuda" if torch.cuda.is_available() else "cpu"
+    import zcgvs_sm100 as zc
+
+    wl.setup(torch, zc, device, 0, 1)  # the seeded inputs are generated on the device
+    corpus = np.ascontiguousarray(wl.reference_corpus(), dtype=np.float32)
+    queries = wl.queries.cpu().numpy()
+    threads = os.cpu_count() or 1
+    sample = max(1, min(len(queries), threads))
+    out = np.empty((sample, wl.K), dtype=np.int32)
     times = []
-    out = np.empty((sample, TOP_K), dtype=np.int32)
-    for step in range(args.warmup + args.steps):
-        q = np.ascontiguousarray(q_h[(step * sample) % NUM_QUERIES:][:sample])
-        n = q.shape[0]
-        t = ref.refcpu_search(corpus.ctypes.data_as(ctypes.c_void_p), N_DOCS, DIM,
-                              q.ctypes.data_as(ctypes.c_void_p), n, TOP_K, threads,
+    for step in range(warmup + steps):
+        q = np.ascontiguousarray(np.roll(queries, -step * sample, axis=0)[:sample])
+        t = ref.refcpu_search(corpus.ctypes.data_as(ctypes.c_void_p), corpus.shape[0], corpus.shape[1],
+                              q.ctypes.data_as(ctypes.c_void_p), q.shape[0], wl.K, threads,
                               out.ctypes.data_as(ctypes.c_void_p))
-        if step >= args.warmup:
-            times.append((n, t))
-    total_q = sum(n for n, _ in times)
-    total_t = sum(t for _, t in times)
-    value = total_q / total_t
+        if step >= warmup:
+            times.append((q.shape[0], t))
+    value = sum(n for n, _ in times) / sum(t for _, t in times)
     line = {"metric": METRIC, "value": value, "unit": UNIT, "impl": "reference", "n_gpus": args.gpus,
-            "steps": args.steps, "warmup": args.warmup, "ms_per_step": 1e3 * total_t / len(times),
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32",
-            "data": "synthetic",
-            "config": {"workload": "cfg2_int8_1Mx768_top100", "batch": sample, "docs": N_DOCS, "dim": DIM,
-                       "k": TOP_K, "note": "reference CPU path on the corpus dequantised to fp32"},
+            "steps": steps, "warmup": warmup, "ms_per_step": 1e3 * sum(t for _, t in times) / len(times),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+            "config": dict(wl.config(1), note="reference CPU path on the corpus as fp32, all host threads"),
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": min(threads, sample), "kind": "reference",
                              "sample": f"{sample} queries per step over the full corpus"},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
@@ -302,40 +730,31 @@ def run_ours(args):
     torch.cuda.set_device(local_rank)
     device = torch.device("cuda", local_rank)
     if world > 1:
-        dist.init_process_group("nccl", init_method="env://", device_id=device,
-                                timeout=__import__("datetime").timedelta(seconds=120))
+        from datetime import timedelta
 
-    codes, scales = make_corpus(torch, device, CORPUS_SEED)
-    queries = make_queries(torch, device, QUERY_SEED + rank, NUM_QUERIES)
-    B = args.batch
-    k = TOP_K
+        dist.init_process_group("nccl", init_method="env://", device_id=device, timeout=timedelta(seconds=300))
+
+    wl = make_workload(args)
+    steps = args.steps if args.steps is not None else wl.steps
+    warmup = args.warmup if args.warmup is not None else wl.warmup
+    wl.setup(torch, zc, device, rank, world)
     stream = torch.cuda.current_stream()
-    ws = zc.Workspace(device)
-    out_idx = torch.empty((B, k), dtype=torch.int32, device=device)
-    out_val = torch.empty((B, k), dtype=torch.float32, device=device)
-    nbatches = max(1, NUM_QUERIES // B)
 
-    def step(i):
-        q = queries[(i % nbatches) * B:(i % nbatches) * B + B]
-        zc.scan_topk(codes, zc.DTYPE_I8_ROW, DIM, q, k, row_scales=scales, workspace=ws,
-                     out=(out_idx, out_val), stream=stream)
-
-    for i in range(args.warmup):
-        step(i)
+    for i in range(warmup):
+        wl.step(i, stream)
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     torch.cuda.synchronize()
 
-    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
-              for _ in range(args.steps)]
+    events = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(steps)]
     with ClockSampler(local_rank) as clocks:
         t_start = torch.cuda.Event(enable_timing=True)
         t_end = torch.cuda.Event(enable_timing=True)
         t_start.record(stream)
-        for i in range(args.steps):
+        for i in range(steps):
             events[i][0].record(stream)
-            step(i)
+            wl.step(i, stream)
             events[i][1].record(stream)
         t_end.record(stream)
         torch.cuda.synchronize()
@@ -345,35 +764,22 @@ def run_ours(args):
     per_step = sorted(a.elapsed_time(b) for a, b in events)
     kernel_ms = sum(per_step) / len(per_step)
     if world > 1:
-        t = torch.tensor([elapsed_ms], device=device)
+        t = torch.tensor([elapsed_ms, kernel_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
-        elapsed_ms = float(t.item())
-    status = ws.status()
+        elapsed_ms, kernel_ms = float(t[0].item()), float(t[1].item())
+    status = wl.ws.status()
 
-    # End to end through the public API with host buffers: pinned host queries -> device,
-    # fused scan + top-k, results -> pinned host, synchronised every step (what a caller sees).
-    h_queries = queries.cpu().pin_memory()
-    h_idx = torch.empty((B, k), dtype=torch.int32).pin_memory()
-    h_val = torch.empty((B, k), dtype=torch.float32).pin_memory()
-    d_q = torch.empty((B, DIM), dtype=torch.float32, device=device)
-    e2e_steps = max(10, args.steps // 2)
-
-    def e2e_step(i):
-        j = (i % nbatches) * B
-        d_q.copy_(h_queries[j:j + B], non_blocking=True)
-        zc.scan_topk(codes, zc.DTYPE_I8_ROW, DIM, d_q, k, row_scales=scales, workspace=ws,
-                     out=(out_idx, out_val), stream=stream)
-        h_idx.copy_(out_idx, non_blocking=True)
-        h_val.copy_(out_val, non_blocking=True)
-        stream.synchronize()
-
-    for i in range(3):
-        e2e_step(i)
+    # End to end through the public API with host buffers: pinned host inputs -> device, the
+    # search, results -> pinned host, synchronised every step (what a caller sees).
+    e2e_steps = max(3, steps // 2)
+    for i in range(2):
+        wl.e2e_step(i, stream)
     if world > 1:
         dist.barrier()
     t0 = time.perf_counter()
+    h2d = d2h = 0
     for i in range(e2e_steps):
-        e2e_step(i)
+        h2d, d2h = wl.e2e_step(i, stream)
     e2e_s = time.perf_counter() - t0
     if world > 1:
         t = torch.tensor([e2e_s], device=device)
@@ -382,32 +788,22 @@ def run_ours(args):
 
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
-        cpu = cpu_baseline(codes.cpu().numpy(), scales.cpu().numpy(), queries.cpu().numpy())
+        cpu = wl.cpu_baseline(12.0)
 
     if rank == 0:
         peaks, peak_kind = measured_peaks()
-        algo_bytes = N_DOCS * (DIM + 4) + B * DIM * 4 + B * k * 8
-        achieved_gbs = algo_bytes / (kernel_ms * 1e-3) / 1e9
-        peak = float(peaks["hbm_gbs"])
-        workload = f"cfg2_int8row_1Mx768_top100_b{B}"
-        traffic = profiled_traffic(workload)
+        total_units = (1 if wl.scaling == "strong" else world) * wl.units
         line = {
-            "metric": METRIC, "value": world * B * args.steps / (elapsed_ms * 1e-3), "unit": UNIT,
-            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
-            "ms_per_step": elapsed_ms / args.steps, "p50_ms": per_step[len(per_step) // 2],
-            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "int8",
+            "metric": METRIC, "value": total_units * steps / (elapsed_ms * 1e-3), "unit": UNIT,
+            "n_gpus": world, "steps": steps, "warmup": warmup,
+            "ms_per_step": elapsed_ms / steps, "p50_ms": per_step[len(per_step) // 2],
+            "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None, "dtype": wl.dtype,
             "data": "synthetic",
-            "config": {"workload": workload, "docs": N_DOCS, "dim": DIM, "k": TOP_K, "batch": B,
-                       "storage": "int8 per-row scale", "parallelism": f"replicas{world}",
-                       "l2": "inputs larger than L2 (772 MB corpus vs 126 MB L2)"},
-            "roofline": {"bound": "hbm", "achieved": achieved_gbs, "peak": peak, "unit": "GB/s",
-                         "frac": achieved_gbs / peak, "traffic": traffic,
-                         "peak_source": peak_kind,
-                         "kernel": "zc::scan_fast_kernel<kModeI8R,3>" if B == 1 else "zc::scan_kernel<kModeI8R,QB>",
-                         "algorithmic_bytes_per_launch": algo_bytes},
-            "e2e": {"value": world * B * e2e_steps / e2e_s, "unit": UNIT,
-                    "h2d_bytes_per_step": B * DIM * 4, "d2h_bytes_per_step": B * k * 8},
-            "gpu_launches": args.steps,
+            "config": wl.config(world),
+            "roofline": wl.roofline(kernel_ms, peaks, peak_kind),
+            "e2e": {"value": total_units * e2e_steps / e2e_s, "unit": UNIT,
+                    "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
+            "gpu_launches": wl.launches * steps,
             "clocks": clocks.summary(),
             "device_status": status,
             "cpu_baseline": cpu,

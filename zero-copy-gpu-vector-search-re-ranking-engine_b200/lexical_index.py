@@ -84,7 +84,8 @@ def synthetic_corpus(n_docs: int, vocab: int, mean_len: float, zipf_s: float, se
     gen.manual_seed(seed)
     rate = torch.full((n_docs,), float(mean_len), dtype=torch.float64, device=device)
     lengths = torch.poisson(rate, generator=gen).to(torch.int64)
-    probs = zipf_probs(vocab, zipf_s, device).to(torch.float32)
+    cdf = torch.cumsum(zipf_probs(vocab, zipf_s, device), 0)
+    cdf[-1] = 1.0
     starts = torch.cumsum(lengths, 0) - lengths
     pairs = []
     # Draw tokens in chunks of whole documents so the (doc, term) keys fit memory.
@@ -94,7 +95,9 @@ def synthetic_corpus(n_docs: int, vocab: int, mean_len: float, zipf_s: float, se
         doc1 = max(doc1, doc0 + 1)
         count = int(lengths[doc0:doc1].sum())
         if count:
-            tokens = torch.multinomial(probs, count, replacement=True, generator=gen)
+            # Inverse-CDF draws: term = first rank whose cumulative probability exceeds u.
+            u = torch.rand(count, dtype=torch.float64, device=device, generator=gen)
+            tokens = torch.searchsorted(cdf, u, right=True).clamp_(max=vocab - 1)
             owner = torch.repeat_interleave(torch.arange(doc0, doc1, device=device), lengths[doc0:doc1])
             key, tf = torch.unique(owner * vocab + tokens, return_counts=True)
             pairs.append((key // vocab, key % vocab, tf))
