@@ -1,0 +1,17 @@
+// Store converters (the reference's include/zcgvs/cuda/convert.cuh:10-20), implemented over
+// zcgvs_convert_f16 / zcgvs_convert_i8 / zcgvs_pack_binary.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+
+namespace zcgvs {
+namespace cuda {
+
+void launchConvertF32ToF16(const float* src, void* dst_half, std::size_t count, cudaStream_t stream);
+void launchConvertF32ToI8(const float* src, void* dst_int8, std::size_t count, float scale, cudaStream_t stream);
+void launchPackBinary(const float* src, void* dst_words, int rows, int dim, cudaStream_t stream);
+
+}  // namespace cuda
+}  // namespace zcgvs

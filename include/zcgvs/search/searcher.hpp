@@ -1,0 +1,105 @@
+// The search driver (the reference's Searcher, include/zcgvs/search/searcher.hpp:32-63), over the
+// fused kernels of this library: one zcgvs_scan_topk (or zcgvs_hybrid_topk with a lexical index)
+// per search, followed by zcgvs_rescore_topk when a rescore store is attached. Same public
+// interface and exceptions; optional CUDA-graph replay keyed by everything the launches capture.
+// Not thread-safe (one Searcher per thread / stream / GPU), like the reference.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstdint>
+
+#include "zcgvs/core/cuda_stream.hpp"
+#include "zcgvs/core/device_buffer.hpp"
+#include "zcgvs/core/pinned_buffer.hpp"
+#include "zcgvs/data/embedding_store.hpp"
+#include "zcgvs/data/lexical_index.hpp"
+#include "zcgvs/search/search_params.hpp"
+#include "zcgvs/search/search_result.hpp"
+
+namespace zcgvs {
+
+class Searcher {
+public:
+    explicit Searcher(const EmbeddingStore& store);
+    ~Searcher();
+
+    Searcher(const Searcher&) = delete;
+    Searcher& operator=(const Searcher&) = delete;
+
+    // Higher-precision copy of the corpus (same order) for rescoring; nullptr disables it.
+    void setRescoreStore(const EmbeddingStore* store);
+    // CSR inverted index enabling the hybrid lexical stage; nullptr disables it.
+    void setLexicalIndex(const LexicalIndex* index);
+
+    void search(const float* host_queries, int dim, int batch, const SearchParams& params, const CudaStream& stream);
+    HostTopK copyResultToHost(const CudaStream& stream);
+
+    int resultK() const { return current_k_; }
+    int resultBatch() const { return current_batch_; }
+    double lastSearchGpuMs() const { return last_gpu_ms_; }
+    bool lastSearchUsedGraph() const { return used_graph_; }
+    std::uint64_t graphCaptureCount() const { return graph_captures_; }
+    std::uint64_t graphLaunchCount() const { return graph_launches_; }
+    bool hasRescoreStore() const { return rescore_store_ != nullptr; }
+    bool hasLexicalIndex() const { return lexical_index_ != nullptr; }
+
+private:
+    struct GraphKey {
+        const void* corpus = nullptr;
+        const void* rescore_corpus = nullptr;
+        const void* lexical_index = nullptr;
+        const std::uint8_t* mask = nullptr;
+        std::uint64_t generation = 0;
+        std::int64_t doc_count = 0;
+        int k = 0;
+        int batch = 0;
+        int rescore_candidates = 0;
+        int lexical_stride = 0;
+        int metric = 0;
+        float dense_weight = 1.0f;
+
+        bool operator==(const GraphKey& other) const;
+    };
+
+    void validate(int dim, int batch, const SearchParams& params, std::int64_t doc_count) const;
+    void ensureCapacity(std::int64_t doc_count, int batch, const SearchParams& params);
+    void recordPipeline(std::int64_t doc_count, int batch, const SearchParams& params, cudaStream_t stream);
+    GraphKey makeKey(std::int64_t doc_count, int batch, const SearchParams& params) const;
+    bool lexicalEnabled(const SearchParams& params) const;
+    bool rescoreEnabled(const SearchParams& params) const;
+    void destroyGraph() noexcept;
+
+    const EmbeddingStore& store_;
+    const EmbeddingStore* rescore_store_ = nullptr;
+    const LexicalIndex* lexical_index_ = nullptr;
+    int dim_ = 0;
+
+    DeviceBuffer<float> d_queries_;
+    DeviceBuffer<int> d_query_terms_;
+    DeviceBuffer<std::uint8_t> d_workspace_;
+    DeviceBuffer<int> d_coarse_indices_;
+    DeviceBuffer<float> d_coarse_values_;
+    DeviceBuffer<int> d_out_indices_;
+    DeviceBuffer<float> d_out_values_;
+    PinnedBuffer<float> h_queries_;
+    PinnedBuffer<int> h_query_terms_;
+    PinnedBuffer<int> h_out_indices_;
+    PinnedBuffer<float> h_out_values_;
+
+    cudaEvent_t ev_start_ = nullptr;
+    cudaEvent_t ev_end_ = nullptr;
+    cudaGraphExec_t graph_exec_ = nullptr;
+    GraphKey graph_key_{};
+    bool graph_valid_ = false;
+    std::uint64_t generation_ = 0;
+    std::uint64_t graph_captures_ = 0;
+    std::uint64_t graph_launches_ = 0;
+
+    int current_k_ = 0;
+    int current_batch_ = 0;
+    double last_gpu_ms_ = 0.0;
+    bool used_graph_ = false;
+};
+
+}  // namespace zcgvs

@@ -77,6 +77,9 @@ int zcgvs_version(void);
 /* Thread-local description of the last error returned on this thread ("" if none). */
 const char* zcgvs_last_error_message(void);
 
+/* The cudaError_t value behind the last ZCGVS_ERR_CUDA returned on this thread (0 if none). */
+int zcgvs_last_cuda_error(void);
+
 /* Zero-fills `bytes` of a workspace on `stream` (a cudaMemsetAsync). */
 int zcgvs_workspace_init(void* workspace, size_t bytes, void* stream);
 
@@ -252,9 +255,11 @@ int zcgvs_hybrid_topk(const void* corpus, int dtype, float scale, const float* r
 
 /* The reference lexical launchers (include/zcgvs/cuda/lexical.cuh:20-40), same contracts:
  *   zcgvs_bm25         : scores[d] += weights of d's postings under the valid terms of one
- *                        query, summed in (slot, posting) order (deterministic; sorted posting
- *                        lists required). Term ids are trusted to be < the index's vocabulary,
- *                        as in the reference.
+ *                        query, summed in (slot, posting) order (deterministic), for postings
+ *                        in any order; every document range reads the query's whole lists, so
+ *                        zcgvs_hybrid_topk (sorted lists, each range reads its slice) is the fast
+ *                        path. Term ids are trusted to be < the index's vocabulary, as in the
+ *                        reference.
  *   zcgvs_max_positive : *out_max = max(*out_max, max(0, max_i values[i])) (zero it first).
  *   zcgvs_fuse_scores  : dense[i] = w * dense[i] + ((1 - w) * lexical[i]) * inv, inv =
  *                        1 / *lexical_max when positive, else 0. */
@@ -263,6 +268,26 @@ int zcgvs_bm25(const int64_t* offsets, const int* posting_docs, const float* pos
 int zcgvs_max_positive(const float* values, int count, float* out_max, void* stream);
 int zcgvs_fuse_scores(float* dense, const float* lexical, const float* lexical_max, float weight,
                       int count, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * The remaining reference launchers, same contracts (for callers that still build a score
+ * matrix or convert host matrices into stores):
+ *   zcgvs_topk          : launchTopK (include/zcgvs/cuda/topk.cuh:8-43): the top-k of every
+ *                         row of scores [batch, doc_count] into [batch, k], (score desc, id asc);
+ *                         1 <= k <= min(ZCGVS_MAX_K, doc_count); needs no scratch.
+ *   zcgvs_convert_f16   : launchConvertF32ToF16 (include/zcgvs/cuda/convert.cuh:10-20).
+ *   zcgvs_convert_i8    : launchConvertF32ToI8: clamp(rint(x * (1 / scale)), +-127) with the
+ *                         reciprocal taken on the host (0 when scale <= 0).
+ *   zcgvs_pack_binary   : launchPackBinary: bit b of word w = dim 32w+b, set when x >= 0.
+ *   zcgvs_remap_indices : launchRemapIndices (include/zcgvs/cuda/rescore.cuh:34-45).
+ * --------------------------------------------------------------------------------------- */
+int zcgvs_topk(const float* scores, int64_t doc_count, int k, int batch, int* out_indices,
+               float* out_scores, void* stream);
+int zcgvs_convert_f16(const float* src, void* dst_half, size_t count, void* stream);
+int zcgvs_convert_i8(const float* src, void* dst_int8, size_t count, float scale, void* stream);
+int zcgvs_pack_binary(const float* src, void* dst_words, int64_t rows, int dim, void* stream);
+int zcgvs_remap_indices(const int* candidates, const int* local_indices, int candidate_count,
+                        int k, int batch, int* out_indices, void* stream);
 
 #ifdef __cplusplus
 }  /* extern "C" */

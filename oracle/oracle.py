@@ -28,10 +28,14 @@ _ref = None
 
 
 def build() -> None:
-    """Compiles liboracle.so (gcc), and the reference CPU library when the tree is present."""
+    """Compiles liboracle.so (gcc) and, when the reference tree is present, the reference CPU
+    library and (once the CUDA library is built) the reference's C++ test programs linked
+    against it."""
     subprocess.run(["make", "-s", "-C", str(HERE), "liboracle.so"], check=True)
     if Path(os.environ.get("ZCGVS_REFERENCE", "/root/reference"), "tests", "cpp").is_dir():
         subprocess.run(["make", "-s", "-C", str(HERE), "ref"], check=True)
+        if (HERE.parent / "zero-copy-gpu-vector-search-re-ranking-engine_b200" / "libzcgvs_sm100.so").exists():
+            subprocess.run(["make", "-s", "-j8", "-C", str(HERE), "reftests"], check=True)
 
 
 def lib():

@@ -9,6 +9,7 @@ namespace zc {
 namespace {
 
 thread_local std::string g_last_error;
+thread_local int g_last_cuda_error = 0;
 
 constexpr int kMaxDevices = 64;
 
@@ -51,6 +52,7 @@ int fail(int status, const std::string& message) {
 }
 
 int fail_cuda(cudaError_t error, const char* what) {
+    g_last_cuda_error = static_cast<int>(error);
     g_last_error = std::string("zcgvs: CUDA error '") + cudaGetErrorName(error) + "' (" +
                    cudaGetErrorString(error) + ") in " + what;
     return ZCGVS_ERR_CUDA;
@@ -58,6 +60,7 @@ int fail_cuda(cudaError_t error, const char* what) {
 
 int ok() {
     g_last_error.clear();
+    g_last_cuda_error = 0;
     return ZCGVS_OK;
 }
 
@@ -93,6 +96,8 @@ extern "C" {
 int zcgvs_version(void) { return 100; }
 
 const char* zcgvs_last_error_message(void) { return zc::last_error_cstr(); }
+
+int zcgvs_last_cuda_error(void) { return zc::g_last_cuda_error; }
 
 int zcgvs_workspace_init(void* workspace, size_t bytes, void* stream) {
     if (bytes == 0) return zc::ok();

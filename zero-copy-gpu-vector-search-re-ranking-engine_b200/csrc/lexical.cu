@@ -17,6 +17,10 @@
 //   * Each CTA writes its documents' scores and its max(0, max score) to the workspace; the
 //     scan kernel reduces those partial maxima (src/cuda/lexical.cu:44-64 does it with a float
 //     atomicMax) and blends lexical and dense scores before its top-k.
+//   * Indexes whose postings are in any order (the reference launcher's contract, used by
+//     zcgvs_bm25) take a second path with the same sums: one warp per CTA walks each term's whole
+//     list in posting order, grouping equal documents of a 32-posting step (match_any) and adding
+//     them in lane order. It reads every posting once per CTA, so it is the slow path.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -49,6 +53,7 @@ struct LexParams {
     const float* init;      // [batch, n] scores to add onto, or nullptr (start at 0)
     float* out;             // [batch, n]
     float* part_max;        // [batch, gridDim.x] or nullptr
+    int sorted;             // postings sorted by document within each term (else: any order)
 };
 
 // First index in [lo, hi) whose document id is >= target (hi if none), for sorted docs[].
@@ -96,8 +101,13 @@ __global__ void __launch_bounds__(kLexThreads) lexical_kernel(const LexParams p)
             if (term >= 0 && term < p.vocab) {
                 const long long begin = __ldg(p.offsets + term);
                 const long long end = __ldg(p.offsets + term + 1);
-                lo = lower_bound_warp(p.docs, begin, end, static_cast<int>(d0), lane);
-                hi = lower_bound_warp(p.docs, lo, end, static_cast<int>(d0 + count), lane);
+                if (p.sorted) {
+                    lo = lower_bound_warp(p.docs, begin, end, static_cast<int>(d0), lane);
+                    hi = lower_bound_warp(p.docs, lo, end, static_cast<int>(d0 + count), lane);
+                } else {
+                    lo = begin;
+                    hi = end;
+                }
             }
             if (lane == 0) {
                 s_lo[t] = lo;
@@ -105,6 +115,34 @@ __global__ void __launch_bounds__(kLexThreads) lexical_kernel(const LexParams p)
             }
         }
         __syncthreads();
+        if (!p.sorted) {
+            // Any posting order: warp 0 walks each term's whole list in posting order, 32 at a time.
+            // Postings of one document inside a step are grouped (match_any) and added in lane
+            // order, so every sum keeps the sequential (slot, posting) order.
+            if (warp == 0) {
+                for (int t = 0; t < slots; ++t) {
+                    const long long lo = s_lo[t];
+                    const long long hi = s_hi[t];
+                    for (long long base = lo; base < hi; base += 32) {
+                        const long long i = base + lane;
+                        const int doc = i < hi ? __ldg(p.docs + i) : -1;
+                        const bool mine = doc >= d0 && doc < d0 + count;
+                        const float w = mine ? __ldg(p.weights + i) : 0.0f;
+                        const uint32_t peers = __match_any_sync(0xffffffffu, mine ? doc : -1 - lane);
+                        const int rank = __popc(peers & ((1u << lane) - 1u));
+                        int rounds = mine ? __popc(peers) : 0;
+#pragma unroll
+                        for (int off = 16; off > 0; off >>= 1) rounds = max(rounds, __shfl_xor_sync(0xffffffffu, rounds, off));
+                        for (int r = 0; r < rounds; ++r) {
+                            if (mine && rank == r) acc[doc - d0] = __fadd_rn(acc[doc - d0], w);
+                            __syncwarp();
+                        }
+                    }
+                }
+            }
+            __syncthreads();
+            continue;
+        }
         for (int t = 0; t < slots; ++t) {
             const long long lo = s_lo[t];
             const long long hi = s_hi[t];
@@ -177,7 +215,7 @@ int lexical_parts(long long n) {
 }
 
 int launch_lexical(const long long* offsets, const int* docs, const float* weights, int vocab, const int* terms,
-                   int stride, long long n, int batch, const float* init, float* out, float* part_max,
+                   int stride, long long n, int batch, const float* init, float* out, float* part_max, bool sorted,
                    cudaStream_t stream) {
     const int parts = lexical_parts(n);
     const long long per = (n + parts - 1) / parts;
@@ -193,6 +231,7 @@ int launch_lexical(const long long* offsets, const int* docs, const float* weigh
     p.init = init;
     p.out = out;
     p.part_max = part_max;
+    p.sorted = sorted ? 1 : 0;
     const size_t smem = static_cast<size_t>(per) * sizeof(float);
     cudaError_t e = ensure_smem_optin(reinterpret_cast<const void*>(lexical_kernel));
     if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(lexical_kernel)");
@@ -224,7 +263,7 @@ int zcgvs_bm25(const int64_t* offsets, const int* posting_docs, const float* pos
         return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs_bm25: null pointer");
     }
     return launch_lexical(reinterpret_cast<const long long*>(offsets), posting_docs, posting_weights, INT_MAX,
-                          query_terms, term_count, doc_count, 1, scores, scores, nullptr,
+                          query_terms, term_count, doc_count, 1, scores, scores, nullptr, false,
                           static_cast<cudaStream_t>(stream));
 }
 

@@ -516,7 +516,7 @@ int zcgvs_hybrid_topk(const void* corpus, int dtype, float scale, const float* r
         hy.dense_weight = dense_weight;
         status = launch_lexical(reinterpret_cast<const long long*>(offsets), posting_docs, posting_weights, vocab_size,
                                 query_terms, term_stride, doc_count, batch, nullptr, reinterpret_cast<float*>(ws + h.scan),
-                                reinterpret_cast<float*>(ws + h.scan + h.lex), st);
+                                reinterpret_cast<float*>(ws + h.scan + h.lex), true, st);
         if (status != ZCGVS_OK) return status;
     }
     return run_scan_topk(plan, corpus, scale, row_scales, doc_count, dim, queries, batch, mask, k, 0, out_indices,

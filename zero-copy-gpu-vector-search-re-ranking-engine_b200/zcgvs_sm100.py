@@ -28,6 +28,7 @@ _i32, _i64, _f32, _sz = ctypes.c_int, ctypes.c_int64, ctypes.c_float, ctypes.c_s
 SIGNATURES = {
     "zcgvs_version": (_i32, []),
     "zcgvs_last_error_message": (ctypes.c_char_p, []),
+    "zcgvs_last_cuda_error": (_i32, []),
     "zcgvs_workspace_init": (_i32, [_P, _sz, _P]),
     "zcgvs_workspace_status": (_i32, [_P, _sz, _P, _P]),
     "zcgvs_scan_topk_workspace_bytes": (_sz, [_i32, _i64, _i32, _i32, _i32]),
@@ -44,6 +45,11 @@ SIGNATURES = {
     "zcgvs_gemm_topk": (_i32, [_P, _i32, _P, _i64, _i32, _P, _i32, _P, _i32, _i32, _i32, _P, _P, _P, _sz, _P]),
     "zcgvs_gemm_similarity_workspace_bytes": (_sz, [_i32, _i64, _i32, _i32]),
     "zcgvs_gemm_similarity": (_i32, [_P, _i32, _P, _i64, _i32, _P, _i32, _P, _i32, _P, _P, _sz, _P]),
+    "zcgvs_topk": (_i32, [_P, _i64, _i32, _i32, _P, _P, _P]),
+    "zcgvs_convert_f16": (_i32, [_P, _P, _sz, _P]),
+    "zcgvs_convert_i8": (_i32, [_P, _P, _sz, _f32, _P]),
+    "zcgvs_pack_binary": (_i32, [_P, _P, _i64, _i32, _P]),
+    "zcgvs_remap_indices": (_i32, [_P, _P, _i32, _i32, _i32, _P, _P]),
     "zcgvs_merge_topk": (_i32, [_P, _P, _i32, _i32, _i32, _i32, _P, _P, _P]),
     "zcgvs_hybrid_topk_workspace_bytes": (_sz, [_i32, _i64, _i32, _i32, _i32]),
     "zcgvs_hybrid_topk": (_i32, [_P, _i32, _f32, _P, _i64, _i32, _P, _i32, _P, _i32, _P, _P, _P, _i32,
@@ -327,4 +333,16 @@ def gemm_similarity(corpus, dtype: int, dim: int, queries, *, row_scales=None, m
     buf = ws.get(nbytes, stream)
     check(lib().zcgvs_gemm_similarity(_ptr(corpus), dtype, _ptr(row_scales), doc_count, dim, _ptr(queries), batch,
                                       _ptr(mask), metric, _ptr(out), _ptr(buf), buf.numel(), _stream(stream)))
+    return out
+
+
+def topk(scores, k: int, out=None, stream=None):
+    """Top-k of every row of a [B, N] fp32 score matrix (the reference launchTopK)."""
+    import torch
+
+    batch, n = scores.shape
+    if out is None:
+        out = (torch.empty((batch, k), dtype=torch.int32, device=scores.device),
+               torch.empty((batch, k), dtype=torch.float32, device=scores.device))
+    check(lib().zcgvs_topk(_ptr(scores), n, k, batch, _ptr(out[0]), _ptr(out[1]), _stream(stream)))
     return out
