@@ -74,7 +74,7 @@ __device__ __forceinline__ uint32_t smem_u32(const void* p) {
 // mbarrier + bulk async copy (the TMA engine's 1-D form). A tile of whole corpus rows is one
 // contiguous byte range, so the un-tiled cp.async.bulk moves it global -> shared in a single
 // instruction issued by one thread, and completion is tracked by an mbarrier transaction
-// count. No cluster multicast is ever used.
+// count. Every copy lands in the issuing CTA's own shared memory only.
 // ---------------------------------------------------------------------------------------
 __device__ __forceinline__ void mbar_init(u64* bar, uint32_t count) {
     asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count)
