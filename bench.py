@@ -59,6 +59,8 @@ def parse_args():
                     choices=["cfg1", "cfg2", "cfg2_b1024", "cfg3", "cfg4", "cfg5"])
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--docs", type=int, default=None,
+                    help="corpus rows instead of the workload's (small cases for profiler captures)")
     return ap.parse_args()
 
 
@@ -282,6 +284,13 @@ class Workload:
 
     scaling = "weak"
     steps, warmup = 200, 10
+    # Library kernel-timing tags of the dominant kernel(s), each launched once per step: their
+    # CUDA-event durations (a second, instrumented pass over the same steps) divide the
+    # roofline's algorithmic work.
+    dominant = ("scan",)
+
+    def kernel_ms(self, kern, steps):
+        return sum(kern[t][0] for t in self.dominant) / steps
 
     @staticmethod
     def tensor_peak(peaks, kind):
@@ -296,6 +305,10 @@ class Cfg2(Workload):
 
     N, D, K, NQ = 1_000_000, 768, 100, 1024
     dtype = "int8"
+
+    @property
+    def dominant(self):
+        return ("gemm_filter",) if self.B >= 64 else ("scan",)
 
     def __init__(self, batch):
         self.B = batch
@@ -348,8 +361,8 @@ class Cfg2(Workload):
             peak, src = self.tensor_peak(peaks, "i8")
             return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s", "frac": achieved / peak,
                     "traffic": profiled_traffic(self.name), "peak_source": f"{peak_kind}: {src}",
-                    "kernel": "zc::gemm::gemm_scan_kernel<kModeI8R,kFilter> (+ sample, threshold, select)",
-                    "algorithmic_ops_per_step": ops}
+                    "kernel": "zc::gemm::gemm_scan_kernel<kModeI8R,kFilter>",
+                    "algorithmic_ops_per_launch": ops}
         algo = self.N * (self.D + 4) + self.B * self.D * 4 + self.B * self.K * 8
         achieved = algo / (kernel_ms * 1e-3) / 1e9
         peak = float(peaks["hbm_gbs"])
@@ -431,8 +444,9 @@ class Cfg3(Workload):
     name = "cfg3_bin1024_10M_top1000_f16rescore_top10_b64"
     dtype = "u32 (xor+popc) / f16"
     units = 64
-    launches = 2
+    launches = 13  # prep, sample, threshold, 3 x (filter, bucket, select), rescore
     steps, warmup = 10, 3
+    dominant = ("gemm_filter",)
 
     def setup(self, torch, zc, device, rank, world):
         self.torch, self.zc = torch, zc
@@ -478,14 +492,17 @@ class Cfg3(Workload):
                 "l2": "inputs larger than L2 (1.28 GB codes, 20.5 GB rescore store)"}
 
     def roofline(self, kernel_ms, peaks, peak_kind):
-        # Dominant: the Hamming scan; algorithmic bytes = the codes once + the gathered rows.
-        algo = self.N * (self.D // 8) + self.B * self.M * self.D * 2 + self.B * self.D * 4
-        achieved = algo / (kernel_ms * 1e-3) / 1e9
-        peak = float(peaks["hbm_gbs"])
-        return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
-                "traffic": profiled_traffic(self.name), "peak_source": peak_kind,
-                "kernel": "zc::scan_kernel<kModeBin,8> + zc::rescore_kernel<kModeF16>",
-                "algorithmic_bytes_per_step": algo}
+        # Dominant: the filtered tensor-core Hamming scan (1-bit rows expanded to int8 on chip).
+        # Its tensor work bounds it before its HBM reads do: 2 B N D int8 ops (0.41 ms at the
+        # int8 peak) against N D / 8 bytes of codes (0.20 ms at the HBM peak).
+        ops = 2.0 * self.B * self.N * self.D
+        achieved = ops / (kernel_ms * 1e-3) / 1e12
+        peak, src = self.tensor_peak(peaks, "i8")
+        return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s", "frac": achieved / peak,
+                "traffic": profiled_traffic(self.name), "peak_source": f"{peak_kind}: {src}",
+                "kernel": "zc::gemm::gemm_scan_kernel<kModeBin,kFilter>",
+                "algorithmic_ops_per_launch": ops,
+                "note": "the MMA runs 128-query blocks: a 64-query batch fills half of each, so frac <= 0.5"}
 
     def cpu_baseline(self, budget_s):
         # The reference CPU path scans fp32 rows; time it on a 200k-row prefix and scale.
@@ -535,6 +552,7 @@ class Cfg4(Workload):
         self.d_q = torch.empty_like(self.queries)
 
     launches = property(lambda self: 12 if self.world == 1 else 13)
+    dominant = ("gemm_filter",)
 
     def _run(self, q):
         if self.world == 1:
@@ -563,8 +581,8 @@ class Cfg4(Workload):
         peak, src = self.tensor_peak(peaks, "f16")
         return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                 "traffic": profiled_traffic(self.name), "peak_source": f"{peak_kind}: {src}",
-                "kernel": "zc::gemm::gemm_scan_kernel<kModeF16,kFilter> (+ sample, threshold, select)",
-                "algorithmic_flops_per_step_per_gpu": flops}
+                "kernel": "zc::gemm::gemm_scan_kernel<kModeF16,kFilter>",
+                "algorithmic_flops_per_launch": flops}
 
     def cpu_baseline(self, budget_s):
         prefix = 200_000
@@ -583,6 +601,7 @@ class Cfg5(Workload):
     units = 1
     launches = 2
     steps, warmup = 200, 10
+    dominant = ("lexical", "scan")
 
     def setup(self, torch, zc, device, rank, world):
         import lexical_index as li
@@ -638,8 +657,8 @@ class Cfg5(Workload):
         peak = float(peaks["hbm_gbs"])
         return {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s", "frac": achieved / peak,
                 "traffic": profiled_traffic(self.name), "peak_source": peak_kind,
-                "kernel": "zc::lexical_kernel + zc::scan_fast_kernel<kModeF16,JC> (blend)",
-                "algorithmic_bytes_per_step": algo,
+                "kernel": "zc::lexical_kernel + zc::scan_fast_kernel<kModeF16,JC> (blend), one launch each per step",
+                "algorithmic_bytes_per_launch_pair": algo,
                 "note": "bytes = dense rows + 8 B per posting of the query's terms + lexical scores written and read"}
 
     def cpu_baseline(self, budget_s):
@@ -662,10 +681,14 @@ class Cfg5(Workload):
 
 def make_workload(args):
     if args.workload == "cfg2":
-        return Cfg2(args.batch or 1)
-    if args.workload == "cfg2_b1024":
-        return Cfg2(args.batch or 1024)
-    return {"cfg1": Cfg1, "cfg3": Cfg3, "cfg4": Cfg4, "cfg5": Cfg5}[args.workload]()
+        wl = Cfg2(args.batch or 1)
+    elif args.workload == "cfg2_b1024":
+        wl = Cfg2(args.batch or 1024)
+    else:
+        wl = {"cfg1": Cfg1, "cfg3": Cfg3, "cfg4": Cfg4, "cfg5": Cfg5}[args.workload]()
+    if args.docs:
+        wl.N = args.docs
+    return wl
 
 
 # --------------------------------------------------------------------------------------------
@@ -762,7 +785,18 @@ def run_ours(args):
         dist.barrier()
     elapsed_ms = t_start.elapsed_time(t_end)
     per_step = sorted(a.elapsed_time(b) for a, b in events)
-    kernel_ms = sum(per_step) / len(per_step)
+
+    # The same steps again with the library's per-launch CUDA events on (kept out of the timed
+    # pass above): the duration of the dominant kernel(s) for the roofline.
+    tags = ("scan", "gemm_sample", "gemm_threshold", "gemm_filter", "gemm_bucket", "gemm_select", "gemm_retry",
+            "rescore", "lexical", "merge")
+    zc.kernel_timing(True)
+    for i in range(steps):
+        wl.step(i, stream)
+    torch.cuda.synchronize()
+    zc.kernel_timing(False)
+    kern = {t: zc.kernel_timing_read(t) for t in tags}
+    kernel_ms = wl.kernel_ms(kern, steps)
     if world > 1:
         t = torch.tensor([elapsed_ms, kernel_ms], device=device)
         dist.all_reduce(t, op=dist.ReduceOp.MAX)
@@ -800,7 +834,8 @@ def run_ours(args):
             "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None, "dtype": wl.dtype,
             "data": "synthetic",
             "config": wl.config(world),
-            "roofline": wl.roofline(kernel_ms, peaks, peak_kind),
+            "roofline": dict(wl.roofline(kernel_ms, peaks, peak_kind), kernel_ms=kernel_ms),
+            "kernels_ms_per_step": {t: v[0] / steps for t, v in kern.items() if v[1]},
             "e2e": {"value": total_units * e2e_steps / e2e_s, "unit": UNIT,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
             "gpu_launches": wl.launches * steps,

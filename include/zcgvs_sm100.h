@@ -87,6 +87,16 @@ int zcgvs_workspace_init(void* workspace, size_t bytes, void* stream);
  * 0 means every bounded wait of every call that used the workspace completed. */
 int zcgvs_workspace_status(const void* workspace, size_t bytes, uint32_t* status, void* stream);
 
+/* Diagnostics (no reference counterpart): CUDA-event timing of the library's main kernel
+ * launches, off by default. zcgvs_kernel_timing(1) clears earlier records and starts recording
+ * an event pair around every tagged launch on its own stream; zcgvs_kernel_timing(0) stops.
+ * zcgvs_kernel_timing_read synchronises the recorded events of `tag` and returns their summed
+ * duration and count. Tags: "scan" (streaming scan), "gemm_sample", "gemm_threshold",
+ * "gemm_filter", "gemm_bucket", "gemm_select", "gemm_retry", "gemm_emit", "rescore", "lexical",
+ * "merge". */
+int zcgvs_kernel_timing(int enable);
+int zcgvs_kernel_timing_read(const char* tag, double* total_ms, int* launches);
+
 /* ---------------------------------------------------------------------------------------
  * Fused scan + top-k. Replaces the launchSimilarity -> launchTopK chain of
  * Searcher::recordPipeline (src/search/searcher.cpp:230-232, :281-284): scores are kept on
@@ -179,10 +189,13 @@ int zcgvs_gather_rescore(const void* store, int dtype, float scale, const float*
  * Tensor-core batched search (tcgen05 MMA, TMEM accumulators, TMA). For large query batches
  * the scan is a dense contraction; the reference has no tensor-core path (it runs its CUDA-core
  * similarity kernel per 8 queries, src/cuda/similarity.cu:83-164, and writes the [batch, N]
- * score matrix). Corpora: ZCGVS_DTYPE_F16 (queries rounded to fp16, fp32 accumulation) and
+ * score matrix). Corpora: ZCGVS_DTYPE_F16 (queries rounded to fp16, fp32 accumulation),
  * ZCGVS_DTYPE_I8_ROW (queries quantised per row as in zcgvs_scan_topk, exact int32 dot, so the
- * result equals zcgvs_scan_topk bit for bit). Rows must be multiples of 128 bytes (dim % 64 == 0
- * for F16, dim % 128 == 0 for I8_ROW); metric dot or cosine.
+ * result equals zcgvs_scan_topk bit for bit) and ZCGVS_DTYPE_BINARY (sign bits expanded to int8
+ * on chip, the exact Hamming score (dim - 2 h) / dim, equal to zcgvs_scan_topk bit for bit).
+ * Rows must be multiples of 128 bytes of operand (dim % 64 == 0 for F16, dim % 128 == 0 for
+ * I8_ROW and BINARY); metric dot or cosine (BINARY: any metric, the score is Hamming's).
+ * zcgvs_scan_topk routes I8_ROW batches >= 64 and BINARY batches >= 16 over >= 65536 rows here.
  *
  * zcgvs_gemm_topk: a threshold pre-pass over a sample of document tiles (per query, the k-th
  * largest tile maximum, a lower bound of the k-th best score), a filtered pass over the whole

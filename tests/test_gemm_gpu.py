@@ -1,7 +1,8 @@
 """GPU tier: the tensor-core batched search (tcgen05 / TMEM / TMA) against the CPU oracle.
 
-Per-row int8 corpora score an exact int32 dot, so the tensor-core score matrix and top-k must
-equal the oracle (and zcgvs_scan_topk) bit for bit. fp16 corpora take fp16 queries (the tests
+Per-row int8 corpora score an exact int32 dot, and 1-bit corpora an exact integer dot of sign
+vectors (their Hamming score), so the tensor-core score matrix and top-k must equal the oracle
+(and zcgvs_scan_topk) bit for bit. fp16 corpora take fp16 queries (the tests
 round their queries to fp16 first, as BASELINE's fp16 workloads draw them) and accumulate in
 fp32 in the tensor core's order: scores within 1e-4, id sets equal modulo near-ties. Shapes cover
 partial query blocks (batch not a multiple of 128), partial document tiles (N not a multiple
@@ -26,6 +27,8 @@ def dev(a):
     a = np.ascontiguousarray(a)
     if a.dtype == np.uint16:
         a = a.view(np.int16)
+    elif a.dtype == np.uint32:
+        a = a.view(np.int32)
     return torch.from_numpy(a).cuda()
 
 
@@ -189,3 +192,93 @@ def test_scan_topk_dispatches_large_int8_batches_exactly(zc, orc):
     ref_i, ref_v = orc.scan_topk(storage, 4, dim, queries, k, row_scales=row_scales)
     np.testing.assert_array_equal(idx.cpu().numpy(), ref_i)
     np.testing.assert_array_equal(val.cpu().numpy(), ref_v)
+
+
+# ----------------------------------------------------------------------------------------
+# 1-bit corpora: sign bits expanded to int8 on chip, exact Hamming scores
+# ----------------------------------------------------------------------------------------
+BIN = 3
+
+
+@pytest.mark.parametrize("n,dim,batch", [(1000, 256, 200), (777, 128, 5), (3000, 1024, 130)])
+def test_gemm_similarity_binary_exact(zc, orc, n, dim, batch):
+    import torch
+
+    storage, _, queries = case(orc, BIN, n, dim, batch, 21)
+    mask = np.ones(n, dtype=np.uint8)
+    mask[::5] = 0
+    out = zc.gemm_similarity(dev(storage), BIN, dim, dev(queries), mask=dev(mask))
+    torch.cuda.synchronize()
+    ref = orc.scores(storage, BIN, dim, queries, mask=mask)
+    np.testing.assert_array_equal(out.cpu().numpy(), ref)
+
+
+@pytest.mark.parametrize("n,dim,batch,k", [(5000, 1024, 64, 1000), (20000, 384, 130, 10), (3000, 128, 7, 1),
+                                           (70000, 768, 20, 100), (4000, 256, 300, 1024)])
+def test_gemm_topk_binary_exact(zc, orc, n, dim, batch, k):
+    import torch
+
+    storage, _, queries = case(orc, BIN, n, dim, batch, 22)
+    ws = zc.Workspace()
+    idx, val = zc.gemm_topk(dev(storage), BIN, dim, dev(queries), k, workspace=ws)
+    torch.cuda.synchronize()
+    ref_i, ref_v = orc.scan_topk(storage, BIN, dim, queries, k)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ref_i)
+    np.testing.assert_array_equal(val.cpu().numpy(), ref_v)
+    assert ws.status() == 0
+
+
+def test_gemm_topk_binary_mask_id_base_and_l2(zc, orc):
+    """Masked documents never appear, ids are offset by id_base, and the L2 metric scores a
+    1-bit corpus by Hamming distance like any other metric."""
+    import torch
+
+    n, dim, batch, k = 9000, 256, 150, 40
+    storage, _, queries = case(orc, BIN, n, dim, batch, 23)
+    mask = np.ones(n, dtype=np.uint8)
+    mask[1::3] = 0
+    for metric in (zc.METRIC_DOT, zc.METRIC_L2):
+        idx, val = zc.gemm_topk(dev(storage), BIN, dim, dev(queries), k, mask=dev(mask), id_base=1000,
+                                metric=metric)
+        torch.cuda.synchronize()
+        ref_i, ref_v = orc.scan_topk(storage, BIN, dim, queries, k, mask=mask, id_base=1000)
+        np.testing.assert_array_equal(idx.cpu().numpy(), ref_i)
+        np.testing.assert_array_equal(val.cpu().numpy(), ref_v)
+
+
+def test_gemm_topk_binary_all_ties_is_exact(zc, orc):
+    """Every row holds the same bits: all documents tie, the candidate buffer overflows and the
+    raised bound of the retry must return ids 0 .. k-1 in order."""
+    import torch
+
+    n, dim, batch, k = 40000, 128, 3, 50
+    rng = np.random.default_rng(5)
+    row = rng.standard_normal(dim).astype(np.float32)
+    storage = orc.pack_binary(np.tile(row, (n, 1)))
+    queries = rng.standard_normal((batch, dim)).astype(np.float32)
+    ws = zc.Workspace()
+    idx, val = zc.gemm_topk(dev(storage), BIN, dim, dev(queries), k, workspace=ws)
+    torch.cuda.synchronize()
+    ref_i, ref_v = orc.scan_topk(storage, BIN, dim, queries, k)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ref_i)
+    np.testing.assert_array_equal(val.cpu().numpy(), ref_v)
+    assert ws.status() == 0
+
+
+def test_scan_topk_dispatches_binary_batches_exactly(zc, orc):
+    """zcgvs_scan_topk on a 1-bit corpus with >= 16 queries and >= 65536 rows runs on the tensor
+    cores (the BASELINE 1-bit shape: 1024 dimensions, top-1,000); bit-exact against the oracle
+    and against the streaming scan of the same queries one at a time."""
+    import torch
+
+    n, dim, batch, k = 100000, 1024, 64, 1000
+    storage, _, queries = case(orc, BIN, n, dim, batch, 24)
+    idx, val = zc.scan_topk(dev(storage), BIN, dim, dev(queries), k)
+    torch.cuda.synchronize()
+    ref_i, ref_v = orc.scan_topk(storage, BIN, dim, queries, k)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ref_i)
+    np.testing.assert_array_equal(val.cpu().numpy(), ref_v)
+    one_i, one_v = zc.scan_topk(dev(storage), BIN, dim, dev(queries[:8]), k)  # below the batch cut: streaming
+    torch.cuda.synchronize()
+    np.testing.assert_array_equal(one_i.cpu().numpy(), ref_i[:8])
+    np.testing.assert_array_equal(one_v.cpu().numpy(), ref_v[:8])

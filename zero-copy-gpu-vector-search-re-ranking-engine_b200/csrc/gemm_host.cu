@@ -1,8 +1,9 @@
 // Host side and helper kernels of the tensor-core batched search (gemm_scan.cuh).
 //
 // zcgvs_gemm_topk runs these kernels on one stream, all on the caller's workspace:
-//   1. prep      : queries -> fp16 (ZCGVS_DTYPE_F16) or per-row int8 + scale (ZCGVS_DTYPE_I8_ROW,
-//                  the quantiser of the streaming scan) in the layout the TMA loads read.
+//   1. prep      : queries -> fp16 (ZCGVS_DTYPE_F16), per-row int8 + scale (ZCGVS_DTYPE_I8_ROW,
+//                  the quantiser of the streaming scan), or int8 -2 / +2 per sign with the sum
+//                  of the signs (ZCGVS_DTYPE_BINARY) in the layout the TMA loads read.
 //   2. sample    : the tensor-core scan over the first T document tiles, writing each query's
 //                  maximum score per 32-document chunk.
 //   3. threshold : per query, from those chunk maxima: the safe bound, the k-th largest (k
@@ -48,15 +49,41 @@ constexpr int kSelectThreads = 512;
 constexpr int kSelectCap = 4096;  // selection buffer (32 KB): k (<= 1024) + 4 keys per thread per round
 constexpr size_t kAlign = 256;
 
+int operand_row_bytes(int mode, int dtype, int dim) {
+    return mode == kModeBin ? dim : static_cast<int>(row_bytes_of(dtype, dim));
+}
+
 // Queries -> the MMA operand layout: fp16 rows, or int8 rows with a per-row scale computed
-// exactly as the streaming scan's quantiser (scan_kernel.cuh, stage_queries).
+// exactly as the streaming scan's quantiser (scan_kernel.cuh, stage_queries), or for 1-bit
+// corpora the row q'[p] = -2 s (s = +1 where the query value is >= 0, the sign bit of
+// src/cuda/convert.cu:34-53, else -1) of dimension 32 w + 8 i + j at position 32 w + 4 j + i
+// (the expanders' byte order) and qscale = the sum of the signs.
 template <int MODE>
 __global__ void prep_queries_kernel(const float* __restrict__ queries, int dim, void* out, float* qscale) {
     __shared__ float s_red[8];
     __shared__ float s_scale;
+    __shared__ int s_sum[8];
     const int q = blockIdx.x;
     const float* src = queries + static_cast<size_t>(q) * dim;
-    if constexpr (MODE == kModeF16) {
+    if constexpr (MODE == kModeBin) {
+        int8_t* dst = static_cast<int8_t*>(out) + static_cast<size_t>(q) * dim;
+        int sum = 0;
+        for (int pos = threadIdx.x; pos < dim; pos += blockDim.x) {
+            const int r = pos & 31;
+            const int d = (pos & ~31) + 8 * (r & 3) + (r >> 2);
+            const bool set = src[d] >= 0.0f;
+            dst[pos] = static_cast<int8_t>(set ? -2 : 2);
+            sum += set ? 1 : -1;
+        }
+        for (int o = 16; o > 0; o >>= 1) sum += __shfl_xor_sync(0xffffffffu, sum, o);
+        if ((threadIdx.x & 31) == 0) s_sum[threadIdx.x >> 5] = sum;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            int total = 0;
+            for (int w = 0; w < static_cast<int>(blockDim.x >> 5); ++w) total += s_sum[w];
+            qscale[q] = static_cast<float>(total);
+        }
+    } else if constexpr (MODE == kModeF16) {
         __half* dst = static_cast<__half*>(out) + static_cast<size_t>(q) * dim;
         for (int j = threadIdx.x; j < dim; j += blockDim.x) dst[j] = __float2half_rn(src[j]);
     } else {
@@ -238,6 +265,34 @@ int make_map(CUtensorMap* map, const void* base, int mode, long long rows, int r
     return ZCGVS_OK;
 }
 
+// 2-D map over packed 1-bit rows [rows, row_bytes]: box = 128 bytes (1,024 dimensions, 8 K
+// slices) of 256 rows, 128-byte swizzle; bytes and rows past the end read as zero.
+int make_raw_map(CUtensorMap* map, const void* base, long long rows, int row_bytes) {
+    const auto fn = encode_fn();
+    if (fn == nullptr) return fail(ZCGVS_ERR_CUDA, "zcgvs gemm: cuTensorMapEncodeTiled is unavailable");
+    const cuuint64_t dims[2] = {static_cast<cuuint64_t>(row_bytes), static_cast<cuuint64_t>(rows)};
+    const cuuint64_t strides[1] = {static_cast<cuuint64_t>(row_bytes)};
+    const cuuint32_t box[2] = {128u, static_cast<cuuint32_t>(kBN)};
+    const cuuint32_t estr[2] = {1, 1};
+    const CUresult r = fn(map, CU_TENSOR_MAP_DATA_TYPE_UINT8, 2, const_cast<void*>(base), dims, strides, box, estr,
+                          CU_TENSOR_MAP_INTERLEAVE_NONE, CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                          CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    if (r != CUDA_SUCCESS) {
+        return fail(ZCGVS_ERR_CUDA, "zcgvs gemm: cuTensorMapEncodeTiled failed (" + std::to_string(static_cast<int>(r)) + ")");
+    }
+    return ZCGVS_OK;
+}
+
+// The operand maps of a search: queries (prepared in the workspace) and corpus.
+int make_maps(CUtensorMap* mq, CUtensorMap* mx, int mode, int dtype, const void* corpus, long long n, int dim,
+              const void* prepared, int batch) {
+    const int a_bytes = operand_row_bytes(mode, dtype, dim);
+    int status = make_map(mq, prepared, mode, batch, a_bytes, kBM);
+    if (status != ZCGVS_OK) return status;
+    if (mode == kModeBin) return make_raw_map(mx, corpus, n, static_cast<int>(row_bytes_of(dtype, dim)));
+    return make_map(mx, corpus, mode, n, a_bytes, kBN);
+}
+
 struct GemmLayout {
     int mode = 0;
     int kblocks = 0, mtiles = 0, ntiles = 0, sample_tiles = 0;
@@ -253,10 +308,14 @@ int plan_gemm(int dtype, long long n, int dim, int batch, int k, GemmLayout& g) 
         g.mode = kModeF16;
     } else if (dtype == ZCGVS_DTYPE_I8_ROW) {
         g.mode = kModeI8R;
+    } else if (dtype == ZCGVS_DTYPE_BINARY) {
+        g.mode = kModeBin;
     } else {
-        return fail(ZCGVS_ERR_UNSUPPORTED, "zcgvs gemm: the tensor-core scan takes float16 or per-row int8 corpora");
+        return fail(ZCGVS_ERR_UNSUPPORTED,
+                    "zcgvs gemm: the tensor-core scan takes float16, per-row int8 or 1-bit corpora");
     }
-    const int row_bytes = static_cast<int>(row_bytes_of(dtype, dim));
+    // Bytes of one row of the MMA operands (1-bit rows become one int8 per dimension).
+    const int row_bytes = operand_row_bytes(g.mode, dtype, dim);
     if (row_bytes % kBKBytes != 0) {
         return fail(ZCGVS_ERR_UNSUPPORTED, "zcgvs gemm: rows must be a multiple of 128 bytes (dim % " +
                                                std::to_string(g.mode == kModeF16 ? 64 : 128) + " == 0)");
@@ -310,17 +369,21 @@ int plan_gemm(int dtype, long long n, int dim, int batch, int k, GemmLayout& g) 
     return ZCGVS_OK;
 }
 
-int stage_count() {
-    const int budget = device_max_smem() - 2048;
-    const int side = 16 + kEpiWarps * 2 * (kHalf * 4 + 16);  // per epilogue warp and accumulator: scales, validity
-    const int fixed = 1024 + 8 * (2 * 8 + 5) + side;
-    return std::max(2, std::min(8, (budget - fixed) / kStageBytes));
-}
-
-size_t gemm_smem(int stages) {
-    return 1024 + static_cast<size_t>(stages) * kStageBytes + 8 * (2 * stages + 5) + 16 +
+// Shared memory past the stage ring: 1-bit raw slices and their barriers, the other barriers,
+// and per epilogue warp and accumulator the side data (scales, validity).
+size_t fixed_smem(int mode, int stages) {
+    const int raw = mode == kModeBin ? kRawSlots : 0;
+    return 1024 + static_cast<size_t>(raw) * kRawBytes + 8 * (2 * stages + 5 + raw) + 16 +
            kEpiWarps * 2 * (kHalf * 4 + 16);
 }
+
+int stage_count(int mode) {
+    const long long budget = device_max_smem() - 2048;
+    const long long room = budget - static_cast<long long>(fixed_smem(mode, 8));
+    return static_cast<int>(std::max<long long>(2, std::min<long long>(8, room / kStageBytes)));
+}
+
+size_t gemm_smem(int mode, int stages) { return static_cast<size_t>(stages) * kStageBytes + fixed_smem(mode, stages); }
 
 // Vector side-data loads need 16-byte aligned row scales and 4-byte aligned mask bytes.
 int side_vec_ok(const float* row_scales, const uint8_t* mask) {
@@ -331,21 +394,33 @@ using GemmFn = void (*)(const CUtensorMap, const CUtensorMap, const GemmParams);
 
 template <int EPI>
 GemmFn gemm_fn(int mode) {
-    return mode == kModeI8R ? gemm_scan_kernel<kModeI8R, EPI> : gemm_scan_kernel<kModeF16, EPI>;
+    switch (mode) {
+        case kModeI8R: return gemm_scan_kernel<kModeI8R, EPI>;
+        case kModeBin: return gemm_scan_kernel<kModeBin, EPI>;
+        default: return gemm_scan_kernel<kModeF16, EPI>;
+    }
 }
 
-int launch_gemm(GemmFn fn, const CUtensorMap& mq, const CUtensorMap& mx, GemmParams p, cudaStream_t stream) {
+int launch_gemm(GemmFn fn, int mode, const CUtensorMap& mq, const CUtensorMap& mx, GemmParams p,
+                cudaStream_t stream, const char* tag) {
     cudaError_t e = ensure_smem_optin(reinterpret_cast<const void*>(fn));
     if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(gemm_scan_kernel)");
     const long long items = static_cast<long long>(p.mtiles) * p.ntiles;
     const int grid = static_cast<int>(std::min<long long>(items, device_sm_count()));
-    fn<<<grid, kThreads, gemm_smem(p.stages), stream>>>(mq, mx, p);
+    const int threads = mode == kModeBin ? threads_of<kModeBin>() : kThreads;
+    {
+        KernelTimer timer(tag, stream);
+        fn<<<grid, threads, gemm_smem(mode, p.stages), stream>>>(mq, mx, p);
+    }
     e = cudaGetLastError();
     return e == cudaSuccess ? ok() : fail_cuda(e, "gemm_scan_kernel launch");
 }
 
 int prep(const GemmLayout& g, const float* queries, int batch, int dim, uint8_t* ws, cudaStream_t stream) {
-    if (g.mode == kModeI8R) {
+    if (g.mode == kModeBin) {
+        prep_queries_kernel<kModeBin><<<batch, 256, 0, stream>>>(queries, dim, ws + g.off_q,
+                                                                reinterpret_cast<float*>(ws + g.off_qscale));
+    } else if (g.mode == kModeI8R) {
         prep_queries_kernel<kModeI8R><<<batch, 256, 0, stream>>>(queries, dim, ws + g.off_q,
                                                                 reinterpret_cast<float*>(ws + g.off_qscale));
     } else {
@@ -362,9 +437,12 @@ int validate(const void* corpus, int dtype, const float* row_scales, long long n
         return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs gemm: null corpus, query or workspace pointer");
     }
     if (n > INT_MAX) return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs gemm: corpus exceeds the supported document count");
-    if (metric == ZCGVS_METRIC_L2) return fail(ZCGVS_ERR_UNSUPPORTED, "zcgvs gemm: the tensor-core scan scores dot/cosine");
-    if (metric != ZCGVS_METRIC_DOT && metric != ZCGVS_METRIC_COSINE) {
+    if (metric != ZCGVS_METRIC_DOT && metric != ZCGVS_METRIC_COSINE && metric != ZCGVS_METRIC_L2) {
         return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs gemm: unknown metric");
+    }
+    // 1-bit corpora score by Hamming distance whatever the metric (src/cuda/similarity.cu:380-390).
+    if (metric == ZCGVS_METRIC_L2 && dtype != ZCGVS_DTYPE_BINARY) {
+        return fail(ZCGVS_ERR_UNSUPPORTED, "zcgvs gemm: the tensor-core scan scores dot/cosine");
     }
     if (dtype == ZCGVS_DTYPE_I8_ROW && row_scales == nullptr) {
         return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs gemm: the per-row int8 store needs row_scales");
@@ -416,11 +494,8 @@ int zcgvs_gemm_topk(const void* corpus, int dtype, const float* row_scales, int6
     }
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const int row_bytes = static_cast<int>(row_bytes_of(dtype, dim));
     CUtensorMap mq, mx;
-    status = make_map(&mq, ws + g.off_q, g.mode, batch, row_bytes, kBM);
-    if (status != ZCGVS_OK) return status;
-    status = make_map(&mx, corpus, g.mode, doc_count, row_bytes, kBN);
+    status = make_maps(&mq, &mx, g.mode, dtype, corpus, doc_count, dim, ws + g.off_q, batch);
     if (status != ZCGVS_OK) return status;
     status = prep(g, queries, batch, dim, ws, st);
     if (status != ZCGVS_OK) return status;
@@ -430,6 +505,7 @@ int zcgvs_gemm_topk(const void* corpus, int dtype, const float* row_scales, int6
     p.batch = batch;
     p.kblocks = g.kblocks;
     p.mtiles = g.mtiles;
+    p.dim = dim;
     p.id_base = static_cast<unsigned>(id_base);
     p.qscale = reinterpret_cast<const float*>(ws + g.off_qscale);
     p.row_scales = row_scales;
@@ -443,14 +519,14 @@ int zcgvs_gemm_topk(const void* corpus, int dtype, const float* row_scales, int6
     p.mb_count = reinterpret_cast<unsigned int*>(ws + g.off_mb_count);
     p.mb_cap = g.mb_cap;
     p.status = reinterpret_cast<unsigned int*>(ws);
-    p.stages = stage_count();
+    p.stages = stage_count(g.mode);
     p.side_vec = side_vec_ok(row_scales, mask);
 
     // Threshold pre-pass over the first sample tiles.
     GemmParams ps = p;
     ps.ntiles = g.sample_tiles;
     ps.n = std::min<long long>(doc_count, static_cast<long long>(g.sample_tiles) * kBN);
-    status = launch_gemm(gemm_fn<kTileMax>(g.mode), mq, mx, ps, st);
+    status = launch_gemm(gemm_fn<kTileMax>(g.mode), g.mode, mq, mx, ps, st, "gemm_sample");
     if (status != ZCGVS_OK) return status;
     const int chunks = g.sample_tiles * kChunks;
     const int tcap = kSelectCap;
@@ -461,8 +537,11 @@ int zcgvs_gemm_topk(const void* corpus, int dtype, const float* row_scales, int6
     if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(threshold_kernel)");
     unsigned long long* thr_safe = reinterpret_cast<unsigned long long*>(ws + g.off_thr_safe);
     unsigned int* mneed = reinterpret_cast<unsigned int*>(ws + g.off_mneed);
-    threshold_kernel<<<batch, kSelectThreads, static_cast<size_t>(tcap) * 8, st>>>(
-        p.chunk_max, chunks, k, tcap, thr_key, thr_safe, cand_count, done, retry, mneed, g.mtiles);
+    {
+        KernelTimer timer("gemm_threshold", st);
+        threshold_kernel<<<batch, kSelectThreads, static_cast<size_t>(tcap) * 8, st>>>(
+            p.chunk_max, chunks, k, tcap, thr_key, thr_safe, cand_count, done, retry, mneed, g.mtiles);
+    }
     e = cudaGetLastError();
     if (e != cudaSuccess) return fail_cuda(e, "threshold_kernel launch");
     e = ensure_smem_optin(reinterpret_cast<const void*>(select_kernel));
@@ -477,15 +556,22 @@ int zcgvs_gemm_topk(const void* corpus, int dtype, const float* row_scales, int6
         p.retry = pass == 0 ? nullptr : retry + pass;
         p.mneed = pass == 0 ? nullptr : mneed + static_cast<size_t>(pass) * g.mtiles;
         p.mb_overflow = retry + kPasses + pass;
-        status = launch_gemm(gemm_fn<kFilter>(g.mode), mq, mx, p, st);
+        status = launch_gemm(gemm_fn<kFilter>(g.mode), g.mode, mq, mx, p, st, pass == 0 ? "gemm_filter" : "gemm_retry");
         if (status != ZCGVS_OK) return status;
-        bucket_kernel<<<dim3(8, filter_ctas * kEpiWarps), 256, 0, st>>>(p.mb_key, p.mb_query, p.mb_count, g.mb_cap, cand_count,
-                                                           cand, kCandCap, p.retry);
+        {
+            KernelTimer timer("gemm_bucket", st);
+            bucket_kernel<<<dim3(8, filter_ctas * kEpiWarps), 256, 0, st>>>(p.mb_key, p.mb_query, p.mb_count,
+                                                                            g.mb_cap, cand_count, cand, kCandCap,
+                                                                            p.retry);
+        }
         e = cudaGetLastError();
         if (e != cudaSuccess) return fail_cuda(e, "bucket_kernel launch");
-        select_kernel<<<batch, kSelectThreads, static_cast<size_t>(kSelectCap) * 8, st>>>(
-            cand, cand_count, kCandCap, k, thr_key, thr_safe, done, retry, mneed, g.mtiles, p.status, pass,
-            out_indices, out_scores);
+        {
+            KernelTimer timer("gemm_select", st);
+            select_kernel<<<batch, kSelectThreads, static_cast<size_t>(kSelectCap) * 8, st>>>(
+                cand, cand_count, kCandCap, k, thr_key, thr_safe, done, retry, mneed, g.mtiles, p.status, pass,
+                out_indices, out_scores);
+        }
         e = cudaGetLastError();
         if (e != cudaSuccess) return fail_cuda(e, "select_kernel launch");
     }
@@ -519,11 +605,8 @@ int zcgvs_gemm_similarity(const void* corpus, int dtype, const float* row_scales
     }
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
-    const int row_bytes = static_cast<int>(row_bytes_of(dtype, dim));
     CUtensorMap mq, mx;
-    status = make_map(&mq, ws + g.off_q, g.mode, batch, row_bytes, kBM);
-    if (status != ZCGVS_OK) return status;
-    status = make_map(&mx, corpus, g.mode, doc_count, row_bytes, kBN);
+    status = make_maps(&mq, &mx, g.mode, dtype, corpus, doc_count, dim, ws + g.off_q, batch);
     if (status != ZCGVS_OK) return status;
     status = prep(g, queries, batch, dim, ws, st);
     if (status != ZCGVS_OK) return status;
@@ -532,15 +615,16 @@ int zcgvs_gemm_similarity(const void* corpus, int dtype, const float* row_scales
     p.batch = batch;
     p.kblocks = g.kblocks;
     p.mtiles = g.mtiles;
+    p.dim = dim;
     p.ntiles = g.ntiles;
     p.qscale = reinterpret_cast<const float*>(ws + g.off_qscale);
     p.row_scales = row_scales;
     p.mask = mask;
     p.out_matrix = scores;
     p.status = reinterpret_cast<unsigned int*>(ws);
-    p.stages = stage_count();
+    p.stages = stage_count(g.mode);
     p.side_vec = side_vec_ok(row_scales, mask);
-    return launch_gemm(gemm_fn<kEmit>(g.mode), mq, mx, p, st);
+    return launch_gemm(gemm_fn<kEmit>(g.mode), g.mode, mq, mx, p, st, "gemm_emit");
 }
 
 }  // extern "C"

@@ -6,18 +6,32 @@
 //
 //   * Work items are (query block m of 128 rows, document tile n of 256 rows); a persistent CTA
 //     walks items m-fastest so the CTAs running at the same time share document tiles in L2.
-//   * Warp 4 (producer) moves 128-byte K slices of the query block (128 x 128 B) and of the
+//   * Warp 8 (producer) moves 128-byte K slices of the query block (128 x 128 B) and of the
 //     document tile (256 x 128 B) into a ring of shared-memory stages with 2-D TMA loads
 //     (128-byte swizzle, the canonical K-major layout of the tensor-core descriptors).
-//   * Warp 5 (one elected thread) issues tcgen05.mma (kind::f16: fp16 x fp16 -> fp32, or
+//   * Warp 9 (one elected thread) issues tcgen05.mma (kind::f16: fp16 x fp16 -> fp32, or
 //     kind::i8: int8 x int8 -> int32, both operands K-major) into one of two 128 x 256 fp32/int32
 //     accumulators in tensor memory, and commits each stage back to the producer and each
 //     finished accumulator to the epilogue through mbarriers.
-//   * Warps 0-3 (epilogue) read the accumulator with tcgen05.ld (warp w owns TMEM lanes
-//     32w..32w+31, i.e. query rows) while the next item's MMAs run in the other accumulator,
+//   * Warps 0-7 (epilogue) read the accumulator with tcgen05.ld (warp w owns TMEM lanes
+//     32 (w % 4) .. + 31, i.e. query rows, and column half w / 4) while the next item's MMAs
+//     run in the other accumulator,
 //     and either write the scores (EMIT), reduce each query's maximum over the tile (TILE_MAX,
 //     the threshold pre-pass) or keep only scores at or above a per-query threshold (FILTER),
 //     appending them as 64-bit selection keys to a per-query candidate buffer.
+//
+// 1-bit corpora (kModeBin, the Hamming score (d - 2 h) / d of src/cuda/similarity.cu:166-240)
+// run on the same int8 tensor-core path. A 2-D TMA brings 128 packed bytes (1,024 dimensions) of
+// 256 rows at a time into one of two raw slots (128-byte swizzle, so that reading one 16-byte
+// column of consecutive rows hits distinct banks), and four more warps (10-13, the expanders)
+// turn each 16-byte K slice (128 dimensions) of it into the int8 operand of a stage: bit b of a word becomes the byte 0xFF (-1) when set, else 0 (one shift
+// and one sign-replicating byte permute per 4 output bytes). The queries are prepared as
+// q' = -2 s (s = +1 for a set bit, else -1), so the accumulator holds 2 sum_i s_i b_i and the
+// exact integer dot product of the two sign vectors is acc - sum_i s_i = d - 2 h. Within each
+// 32-dimension word the expansion stores dimension 8 i + j at byte 4 j + i; the query rows use
+// the same order, which leaves the dot product unchanged. The epilogue compares these integers
+// with per-query integer bounds and divides (IEEE, as the reference) only for the values it
+// keeps.
 //
 // Every mbarrier wait is bounded; on a timeout the kernel records a status bit, stops issuing,
 // waits (bounded) for its own copies and MMAs in flight, frees its tensor memory and returns.
@@ -25,6 +39,8 @@
 
 #include <cuda.h>
 #include <cuda_fp16.h>
+
+#include <climits>
 
 #include "common.cuh"
 
@@ -45,6 +61,23 @@ constexpr int kMmaWarp = kEpiWarps + 1;
 constexpr int kHalf = kBN / 2;            // columns per epilogue warp
 constexpr int kTmemCols = 512;            // two 256-column accumulators
 constexpr int kChunks = kBN / 32;         // threshold granularity: 32-document chunks per tile
+// 1-bit corpora: expander warps and the raw slots (128 packed bytes = 8 K slices of 256 rows).
+constexpr int kExpWarps = 4;
+constexpr int kFirstExpWarp = kEpiWarps + 2;
+constexpr int kSlicesPerUnit = 8;
+constexpr int kRawBytes = kBN * 128;      // 32 KB per raw slot
+constexpr int kRawSlots = 2;
+constexpr int kExpBarrier = 1;            // named barrier of the expander warps
+
+template <int MODE>
+constexpr int threads_of() {
+    return 32 * (kEpiWarps + 2 + (MODE == kModeBin ? kExpWarps : 0));
+}
+
+template <int MODE>
+constexpr bool int8_operands() {
+    return MODE == kModeI8R || MODE == kModeBin;
+}
 
 enum Epilogue : int { kEmit = 0, kTileMax = 1, kFilter = 2 };
 
@@ -54,10 +87,11 @@ constexpr uint32_t kStatusOverflow = 8u;    // a candidate buffer overflowed
 struct GemmParams {
     long long n;                 // documents
     int batch;                   // queries
-    int kblocks;                 // d * elem_bytes / 128
+    int kblocks;                 // d * elem_bytes / 128 (1-bit: d / 128)
     int mtiles, ntiles;          // items = mtiles * ntiles
     unsigned id_base;
-    const float* qscale;         // I8R: [batch]
+    int dim;                     // 1-bit: the score divisor d
+    const float* qscale;         // I8R: [batch] query scales; 1-bit: [batch] sum of the query's signs
     const float* row_scales;     // I8R: [n]
     const uint8_t* mask;         // optional [n]
     float* out_matrix;           // kEmit: [batch][n]
@@ -87,7 +121,7 @@ __device__ __forceinline__ uint64_t smem_desc_sw128(uint32_t smem_addr) {
 // N >> 3 at bit 17, M >> 4 at bit 24.
 template <int MODE>
 __device__ __forceinline__ constexpr uint32_t instr_desc() {
-    return MODE == kModeI8R ? ((2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kBN >> 3) << 17) |
+    return int8_operands<MODE>() ? ((2u << 4) | (1u << 7) | (1u << 10) | (static_cast<uint32_t>(kBN >> 3) << 17) |
                                (static_cast<uint32_t>(kBM >> 4) << 24))
                             : ((1u << 4) | (static_cast<uint32_t>(kBN >> 3) << 17) |
                                (static_cast<uint32_t>(kBM >> 4) << 24));
@@ -96,7 +130,7 @@ __device__ __forceinline__ constexpr uint32_t instr_desc() {
 template <int MODE>
 __device__ __forceinline__ void mma_issue(uint32_t tmem_d, uint64_t a_desc, uint64_t b_desc, uint32_t accumulate) {
     constexpr uint32_t idesc = instr_desc<MODE>();
-    if constexpr (MODE == kModeI8R) {
+    if constexpr (int8_operands<MODE>()) {
         asm volatile(
             "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
             "tcgen05.mma.cta_group::1.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
@@ -137,6 +171,53 @@ __device__ __forceinline__ void tma_load_2d(void* smem_dst, const CUtensorMap* m
         : "memory");
 }
 
+// Byte i of the result = 0xFF when bit 8 i + 7 of x is set, else 0 (prmt with the
+// sign-replicate flag on each selector nibble).
+__device__ __forceinline__ uint32_t sign_bytes(uint32_t x) {
+    uint32_t r;
+    asm("prmt.b32 %0, %1, 0, 0xBA98;" : "=r"(r) : "r"(x));
+    return r;
+}
+
+// One packed word -> 32 int8 operand bytes: o[j] byte i = -(bit 8 i + j of w).
+__device__ __forceinline__ void expand_word(uint32_t w, uint4& lo, uint4& hi) {
+    lo = make_uint4(sign_bytes(w << 7), sign_bytes(w << 6), sign_bytes(w << 5), sign_bytes(w << 4));
+    hi = make_uint4(sign_bytes(w << 3), sign_bytes(w << 2), sign_bytes(w << 1), sign_bytes(w));
+}
+
+// Named barrier over `count` threads that also ANDs a predicate across them.
+__device__ __forceinline__ bool bar_and(int id, int count, bool pred) {
+    uint32_t r;
+    asm volatile(
+        "{\n\t.reg .pred p, q;\n\tsetp.ne.b32 p, %1, 0;\n\t"
+        "bar.red.and.pred q, %2, %3, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+        : "=r"(r)
+        : "r"(pred ? 1 : 0), "r"(id), "r"(count)
+        : "memory");
+    return r != 0u;
+}
+
+// 1-bit score of an integer dot product of sign vectors, as the reference rounds it.
+__device__ __forceinline__ float bin_score(int d, float dimf) { return __fdiv_rn(__int2float_rn(d), dimf); }
+
+// Integer bounds of a float threshold for 1-bit scores (strictly increasing in d):
+// bin_score(d) > thr exactly when d >= d_gt, and bin_score(d) == thr exactly when d == d_eq
+// (INT_MAX when no d scores thr).
+__device__ __forceinline__ void bin_bounds(float thr, int dim, int& d_gt, int& d_eq) {
+    const float dimf = static_cast<float>(dim);
+    const float lim = dimf + 2.0f;
+    const int d0 = __float2int_rn(fminf(fmaxf(__fmul_rn(thr, dimf), -lim), lim));
+    // thr * d is within 1 of the boundary, so [d0 - 2, d0 + 2] brackets it.
+    d_gt = d0 + 3;
+    d_eq = INT_MAX;
+#pragma unroll
+    for (int d = d0 + 2; d >= d0 - 2; --d) {
+        const float s = bin_score(d, dimf);
+        if (s > thr) d_gt = d;
+        if (s == thr) d_eq = d;
+    }
+}
+
 // v[j] for a warp-uniform runtime j without indexing the register array (which would move
 // it to local memory): a uniform branch over the 32 cases.
 __device__ __forceinline__ float pick32(const float (&v)[32], int j) {
@@ -159,22 +240,38 @@ __device__ __forceinline__ bool item_skipped(const GemmParams& p, long long w) {
     return p.mneed != nullptr && p.mneed[w % p.mtiles] == 0u;
 }
 
+// The CTA's walk over the items: blockIdx.x, then every gridDim.x-th item, skipping items.
+__device__ __forceinline__ long long walk_next(const GemmParams& p, long long w, long long items) {
+    do {
+        w += gridDim.x;
+    } while (w < items && item_skipped(p, w));
+    return w;
+}
+
+__device__ __forceinline__ long long walk_first(const GemmParams& p, long long items) {
+    const long long w = blockIdx.x;
+    return (w < items && item_skipped(p, w)) ? walk_next(p, w, items) : w;
+}
+
 template <int MODE, int EPI>
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(threads_of<MODE>(), 1)
     gemm_scan_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_x,
                      const GemmParams p) {
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // Stage ring first, 1024-aligned (the swizzle pattern and base offset 0 assume it).
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
     const int S = p.stages;
-    u64* full = reinterpret_cast<u64*>(smem + static_cast<size_t>(S) * kStageBytes);
+    constexpr int R = MODE == kModeBin ? kRawSlots : 0;
+    uint8_t* raw = smem + static_cast<size_t>(S) * kStageBytes;  // 1-bit: [R][kBN][128] packed, swizzled
+    u64* full = reinterpret_cast<u64*>(raw + static_cast<size_t>(R) * kRawBytes);
     u64* empty = full + S;
     u64* acc_full = empty + S;        // [2]
     u64* acc_empty = acc_full + 2;    // [2]
     u64* drain = acc_empty + 2;       // [1]
+    u64* raw_full = drain + 1;        // [R]
     // Per epilogue warp and accumulator: the tile's row scales and validity bytes.
     // 16-byte aligned: the epilogue stores float4s here.
-    float* side = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(drain + 1) + 15) & ~uintptr_t(15));  // [8][2][kHalf]
+    float* side = reinterpret_cast<float*>((reinterpret_cast<uintptr_t>(raw_full + R) + 15) & ~uintptr_t(15));  // [8][2][kHalf]
     uint32_t* side_bits = reinterpret_cast<uint32_t*>(side + kEpiWarps * 2 * kHalf);  // [8][2][4] validity
     __shared__ uint32_t s_tmem;
     __shared__ int s_abort;
@@ -188,9 +285,11 @@ __global__ void __launch_bounds__(kThreads, 1)
 
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
-            mbar_init(&full[s], 1);
+            // 1-bit: the query copy and one arrival per expander warp fill a stage.
+            mbar_init(&full[s], MODE == kModeBin ? 1 + kExpWarps : 1);
             mbar_init(&empty[s], 1);
         }
+        for (int r = 0; r < R; ++r) mbar_init(&raw_full[r], 1);
         for (int a = 0; a < 2; ++a) {
             mbar_init(&acc_full[a], 1);
             mbar_init(&acc_empty[a], kEpiWarps);
@@ -230,9 +329,16 @@ __global__ void __launch_bounds__(kThreads, 1)
                         }
                     }
                     uint8_t* st = smem + static_cast<size_t>(s) * kStageBytes;
-                    mbar_arrive_expect_tx(&full[s], kStageBytes);
-                    tma_load_2d(st, &map_q, kb * (kBKBytes / (MODE == kModeI8R ? 1 : 2)), m * kBM, &full[s]);
-                    tma_load_2d(st + kStageA, &map_x, kb * (kBKBytes / (MODE == kModeI8R ? 1 : 2)), n * kBN, &full[s]);
+                    constexpr int kElems = int8_operands<MODE>() ? kBKBytes : kBKBytes / 2;
+                    if constexpr (MODE == kModeBin) {
+                        // The expander warps write the document half of the stage.
+                        mbar_arrive_expect_tx(&full[s], kStageA);
+                        tma_load_2d(st, &map_q, kb * kElems, m * kBM, &full[s]);
+                    } else {
+                        mbar_arrive_expect_tx(&full[s], kStageBytes);
+                        tma_load_2d(st, &map_q, kb * kElems, m * kBM, &full[s]);
+                        tma_load_2d(st + kStageA, &map_x, kb * kElems, n * kBN, &full[s]);
+                    }
                     ++issued;
                     if (++s == S) {
                         s = 0;
@@ -298,6 +404,100 @@ __global__ void __launch_bounds__(kThreads, 1)
             // Make sure no MMA is in flight before the tensor memory is released.
             mma_commit(drain);
             mbar_wait_bounded(drain, 0u, p.status, kStatusDrainTimeout);
+        }
+    } else if (warp >= kFirstExpWarp) {
+        if constexpr (MODE == kModeBin) {
+            // ---------------- expander warps 10-13 (1-bit corpora) ----------------
+            // Thread et expands rows et and et + 128 of each K slice. Thread 0 fetches the raw
+            // units (128 packed bytes of the tile's rows) into the two slots, the next one as soon
+            // as every expander is done with a slot. A wait that runs out makes the warp skip the
+            // rest of the unit; the four warps agree at the unit's end whether to go on, so the
+            // named barrier always sees all of them.
+            constexpr int kExpThreads = kExpWarps * 32;
+            const int et = tid - kFirstExpWarp * 32;
+            const int units_per_item = (p.kblocks + kSlicesPerUnit - 1) / kSlicesPerUnit;
+            long long pw = walk_first(p, items);  // next unit to fetch: item pw, unit pu
+            int pu = 0;
+            long long fetched = 0;
+            auto fetch = [&]() {
+                if (pw >= items) return;
+                const int slot = static_cast<int>(fetched % R);
+                mbar_arrive_expect_tx(&raw_full[slot], kRawBytes);
+                tma_load_2d(raw + static_cast<size_t>(slot) * kRawBytes, &map_x, pu * 128,
+                            static_cast<int>(pw / p.mtiles) * kBN, &raw_full[slot]);
+                ++fetched;
+                if (++pu == units_per_item) {
+                    pu = 0;
+                    pw = walk_next(p, pw, items);
+                }
+            };
+            if (et == 0) {
+                for (int i = 0; i < R; ++i) fetch();
+            }
+            long long u = 0;  // raw units expanded
+            long long c = 0;  // slices expanded (= stages filled)
+            int s = 0;
+            uint32_t phase = 0;
+            bool ok = true;
+            for (long long w = walk_first(p, items); w < items && ok; w = walk_next(p, w, items)) {
+                for (int kb0 = 0; kb0 < p.kblocks; kb0 += kSlicesPerUnit) {
+                    const int slot = static_cast<int>(u % R);
+                    const uint8_t* src = raw + static_cast<size_t>(slot) * kRawBytes;
+                    bool good = !*abort_flag && mbar_wait_bounded(&raw_full[slot], static_cast<uint32_t>((u / R) & 1),
+                                                                  p.status, kStatusTileWaitTimeout);
+                    good = __all_sync(0xffffffffu, good);
+                    const int kb_end = min(kb0 + kSlicesPerUnit, p.kblocks);
+                    for (int kb = kb0; kb < kb_end; ++kb) {
+                        if (good && c >= S) {
+                            good = !*abort_flag &&
+                                   mbar_wait_bounded(&empty[s], phase ^ 1u, p.status, kStatusTileWaitTimeout);
+                            good = __all_sync(0xffffffffu, good);
+                        }
+                        if (good) {
+                            const int col = kb - kb0;  // 16-byte column of the raw rows
+                            uint8_t* dst = smem + static_cast<size_t>(s) * kStageBytes + kStageA;
+#pragma unroll
+                            for (int h = 0; h < 2; ++h) {
+                                const int r = et + h * kExpThreads;
+                                // Both the raw slot and the stage are 128-byte swizzled K-major
+                                // tiles: 16-byte unit x of row r sits at x ^ (r % 8).
+                                const uint4 bits =
+                                    *reinterpret_cast<const uint4*>(src + r * 128 + ((col ^ (r & 7)) << 4));
+                                uint8_t* out = dst + (r >> 3) * 1024 + (r & 7) * 128;
+                                const uint32_t words[4] = {bits.x, bits.y, bits.z, bits.w};
+#pragma unroll
+                                for (int wi = 0; wi < 4; ++wi) {
+                                    uint4 lo, hi;
+                                    expand_word(words[wi], lo, hi);
+                                    *reinterpret_cast<uint4*>(out + (((2 * wi) ^ (r & 7)) << 4)) = lo;
+                                    *reinterpret_cast<uint4*>(out + (((2 * wi + 1) ^ (r & 7)) << 4)) = hi;
+                                }
+                            }
+                            fence_proxy_async_shared();  // the tensor core reads these bytes
+                            __syncwarp();
+                            if (lane == 0) mbar_arrive_cta(&full[s]);
+                        }
+                        ++c;
+                        if (++s == S) {
+                            s = 0;
+                            phase ^= 1u;
+                        }
+                    }
+                    // Every expander is done with the slot, and all agree whether to go on.
+                    ok = bar_and(kExpBarrier, kExpThreads, good);
+                    if (!ok) break;
+                    if (et == 0) fetch();
+                    ++u;
+                }
+            }
+            if (!ok && et == 0) {
+                *abort_flag = 1;
+                // Wait (bounded) for the units still in flight before the CTA can retire.
+                for (long long i = u; i < fetched; ++i) {
+                    mbar_wait_bounded(&raw_full[i % R], static_cast<uint32_t>((i / R) & 1), p.status,
+                                      kStatusDrainTimeout);
+                }
+            }
         }
     } else {
         // ---------------- epilogue warps 0-7 ----------------
@@ -386,14 +586,25 @@ __global__ void __launch_bounds__(kThreads, 1)
             float qs = 1.0f, thr = INFINITY;
             unsigned long long thr_key = ~0ull;
             bool live = q_ok;
+            // 1-bit: the query's sign sum, and the integer form of its threshold.
+            int sq = 0, d_gt = INT_MAX, d_eq = INT_MAX;
             if (q_ok) {
                 if constexpr (MODE == kModeI8R) qs = __ldg(p.qscale + q);
+                if constexpr (MODE == kModeBin) sq = __float2int_rn(__ldg(p.qscale + q));
                 if constexpr (EPI == kFilter) {
                     live = p.done == nullptr || p.done[q] == 0;
                     thr_key = p.thr_key[q];
                     thr = thr_key == 0ull ? -INFINITY : score_from_bits(static_cast<uint32_t>(thr_key >> 32));
+                    if constexpr (MODE == kModeBin) {
+                        if (thr_key == 0ull) {
+                            d_gt = INT_MIN;
+                        } else {
+                            bin_bounds(thr, p.dim, d_gt, d_eq);
+                        }
+                    }
                 }
             }
+            const float dimf = static_cast<float>(p.dim);
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16) +
                                    static_cast<uint32_t>(a * kBN + half * kHalf);
 #pragma unroll 1
@@ -404,10 +615,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                 const uint32_t valid = vbits[cl];
                 const long long dchunk = doc0 + cl * 32;
                 float sc[32];
+                int dv[32];  // 1-bit: integer dot products of the sign vectors
 #pragma unroll
                 for (int j = 0; j < 32; ++j) {
                     if constexpr (MODE == kModeI8R) {
                         sc[j] = __fmul_rn(__fmul_rn(__int2float_rn(static_cast<int>(v[j])), qs), scales[cl * 32 + j]);
+                    } else if constexpr (MODE == kModeBin) {
+                        dv[j] = static_cast<int>(v[j]) - sq;
                     } else {
                         sc[j] = __uint_as_float(v[j]);
                     }
@@ -418,14 +632,22 @@ __global__ void __launch_bounds__(kThreads, 1)
                         for (int j = 0; j < 32; ++j) {
                             const long long d = dchunk + j;
                             if (d < p.n) {
-                                p.out_matrix[static_cast<size_t>(q) * p.n + d] = ((valid >> j) & 1u) ? sc[j] : -FLT_MAX;
+                                const float val = MODE == kModeBin ? bin_score(dv[j], dimf) : sc[j];
+                                p.out_matrix[static_cast<size_t>(q) * p.n + d] = ((valid >> j) & 1u) ? val : -FLT_MAX;
                             }
                         }
                     }
                 } else if constexpr (EPI == kTileMax) {
                     float best = -INFINITY;
+                    if constexpr (MODE == kModeBin) {
+                        int dbest = INT_MIN;
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) best = fmaxf(best, ((valid >> j) & 1u) ? sc[j] : -INFINITY);
+                        for (int j = 0; j < 32; ++j) dbest = max(dbest, ((valid >> j) & 1u) ? dv[j] : INT_MIN);
+                        if (dbest != INT_MIN) best = bin_score(dbest, dimf);
+                    } else {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) best = fmaxf(best, ((valid >> j) & 1u) ? sc[j] : -INFINITY);
+                    }
                     if (q_ok) p.chunk_max[(static_cast<size_t>(q) * p.ntiles + n) * kChunks + half * 4 + cl] = best;
                 } else {
                     // Candidates go to this warp's own mailbox segment at a register counter:
@@ -433,8 +655,13 @@ __global__ void __launch_bounds__(kThreads, 1)
                     uint32_t pass = 0u, ties = 0u;
 #pragma unroll
                     for (int j = 0; j < 32; ++j) {
-                        pass |= (sc[j] > thr ? 1u : 0u) << j;
-                        ties |= (sc[j] == thr ? 1u : 0u) << j;
+                        if constexpr (MODE == kModeBin) {
+                            pass |= (dv[j] >= d_gt ? 1u : 0u) << j;
+                            ties |= (dv[j] == d_eq ? 1u : 0u) << j;
+                        } else {
+                            pass |= (sc[j] > thr ? 1u : 0u) << j;
+                            ties |= (sc[j] == thr ? 1u : 0u) << j;
+                        }
                     }
                     pass = live ? (pass & valid) : 0u;
                     ties = live ? (ties & valid) : 0u;
@@ -469,9 +696,17 @@ __global__ void __launch_bounds__(kThreads, 1)
                     while (bits != 0u) {
                         const int j = __ffs(bits) - 1;
                         bits &= bits - 1u;
-                        float val = sc[0];
+                        float val;
+                        if constexpr (MODE == kModeBin) {
+                            int dsel = dv[0];
 #pragma unroll
-                        for (int jj = 1; jj < 32; ++jj) val = (j == jj) ? sc[jj] : val;
+                            for (int jj = 1; jj < 32; ++jj) dsel = (j == jj) ? dv[jj] : dsel;
+                            val = bin_score(dsel, dimf);
+                        } else {
+                            val = sc[0];
+#pragma unroll
+                            for (int jj = 1; jj < 32; ++jj) val = (j == jj) ? sc[jj] : val;
+                        }
                         const unsigned long long key = make_key(val, p.id_base + static_cast<unsigned>(dchunk + j));
                         if (slot < static_cast<uint32_t>(p.mb_cap)) {
                             p.mb_key[seg + slot] = key;

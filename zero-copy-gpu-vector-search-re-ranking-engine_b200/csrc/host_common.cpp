@@ -1,8 +1,12 @@
 #include "host_common.h"
 
+#include <atomic>
+#include <cstring>
 #include <mutex>
 #include <set>
+#include <string>
 #include <utility>
+#include <vector>
 
 namespace zc {
 
@@ -44,7 +48,47 @@ DeviceCache& cache_for(int device) {
     return entry;
 }
 
+struct TimedLaunch {
+    std::string tag;
+    cudaEvent_t start = nullptr;
+    cudaEvent_t stop = nullptr;
+};
+
+std::atomic<bool> g_timing{false};
+std::mutex g_timing_mutex;
+std::vector<TimedLaunch> g_timed;
+
+void clear_timed() {
+    for (TimedLaunch& t : g_timed) {
+        if (t.start != nullptr) cudaEventDestroy(t.start);
+        if (t.stop != nullptr) cudaEventDestroy(t.stop);
+    }
+    g_timed.clear();
+}
+
 }  // namespace
+
+KernelTimer::KernelTimer(const char* tag, cudaStream_t stream) : stream_(stream) {
+    if (!g_timing.load(std::memory_order_relaxed)) return;
+    TimedLaunch t;
+    t.tag = tag;
+    if (cudaEventCreate(&t.start) != cudaSuccess || cudaEventCreate(&t.stop) != cudaSuccess ||
+        cudaEventRecord(t.start, stream) != cudaSuccess) {
+        if (t.start != nullptr) cudaEventDestroy(t.start);
+        if (t.stop != nullptr) cudaEventDestroy(t.stop);
+        cudaGetLastError();
+        return;
+    }
+    std::lock_guard<std::mutex> lock(g_timing_mutex);
+    slot_ = static_cast<int>(g_timed.size());
+    g_timed.push_back(t);
+}
+
+KernelTimer::~KernelTimer() {
+    if (slot_ < 0) return;
+    std::lock_guard<std::mutex> lock(g_timing_mutex);
+    if (slot_ < static_cast<int>(g_timed.size())) cudaEventRecord(g_timed[slot_].stop, stream_);
+}
 
 int fail(int status, const std::string& message) {
     g_last_error = message;
@@ -116,6 +160,38 @@ int zcgvs_workspace_status(const void* workspace, size_t bytes, uint32_t* status
     cudaError_t e = cudaMemcpyAsync(status, workspace, sizeof(uint32_t), cudaMemcpyDeviceToHost, s);
     if (e == cudaSuccess) e = cudaStreamSynchronize(s);
     if (e != cudaSuccess) return zc::fail_cuda(e, "zcgvs_workspace_status");
+    return zc::ok();
+}
+
+}  // extern "C"
+
+extern "C" {
+
+int zcgvs_kernel_timing(int enable) {
+    std::lock_guard<std::mutex> lock(zc::g_timing_mutex);
+    if (enable) zc::clear_timed();
+    zc::g_timing.store(enable != 0);
+    return zc::ok();
+}
+
+int zcgvs_kernel_timing_read(const char* tag, double* total_ms, int* launches) {
+    if (tag == nullptr || total_ms == nullptr || launches == nullptr) {
+        return zc::fail(ZCGVS_ERR_INVALID_ARG, "zcgvs_kernel_timing_read: null argument");
+    }
+    std::lock_guard<std::mutex> lock(zc::g_timing_mutex);
+    double sum = 0.0;
+    int count = 0;
+    for (const zc::TimedLaunch& t : zc::g_timed) {
+        if (t.tag != tag) continue;
+        cudaError_t e = cudaEventSynchronize(t.stop);
+        float ms = 0.0f;
+        if (e == cudaSuccess) e = cudaEventElapsedTime(&ms, t.start, t.stop);
+        if (e != cudaSuccess) return zc::fail_cuda(e, "zcgvs_kernel_timing_read");
+        sum += ms;
+        ++count;
+    }
+    *total_ms = sum;
+    *launches = count;
     return zc::ok();
 }
 

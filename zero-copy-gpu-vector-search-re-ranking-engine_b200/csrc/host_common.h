@@ -31,6 +31,21 @@ int device_max_smem();
 // shared memory, once per device.
 cudaError_t ensure_smem_optin(const void* kernel);
 
+// CUDA-event timing of one kernel launch under a tag (a diagnostics switch, off by default):
+// when zcgvs_kernel_timing(1) is on, the constructor records an event on `stream` before the
+// launch and the destructor one after it; zcgvs_kernel_timing_read sums them per tag.
+class KernelTimer {
+   public:
+    KernelTimer(const char* tag, cudaStream_t stream);
+    ~KernelTimer();
+    KernelTimer(const KernelTimer&) = delete;
+    KernelTimer& operator=(const KernelTimer&) = delete;
+
+   private:
+    int slot_ = -1;
+    cudaStream_t stream_ = nullptr;
+};
+
 inline std::size_t round_up(std::size_t value, std::size_t to) {
     return (value + to - 1) / to * to;
 }

@@ -243,7 +243,10 @@ int launch_lexical(const long long* offsets, const int* docs, const float* weigh
         pc.out += static_cast<size_t>(q0) * n;
         if (pc.part_max != nullptr) pc.part_max += static_cast<size_t>(q0) * parts;
         const dim3 grid(static_cast<unsigned>(parts), static_cast<unsigned>(std::min(kMaxY, batch - q0)));
-        lexical_kernel<<<grid, kLexThreads, smem, stream>>>(pc);
+        {
+            KernelTimer timer("lexical", stream);
+            lexical_kernel<<<grid, kLexThreads, smem, stream>>>(pc);
+        }
         e = cudaGetLastError();
         if (e != cudaSuccess) return fail_cuda(e, "lexical_kernel launch");
     }

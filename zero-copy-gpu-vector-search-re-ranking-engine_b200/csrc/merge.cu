@@ -81,8 +81,12 @@ int zcgvs_merge_topk(const int* list_indices, const float* list_scores, int list
     const int cap = next_pow2(std::max(lists * k_in, 2));
     const cudaError_t opt = ensure_smem_optin(reinterpret_cast<const void*>(merge_lists_kernel));
     if (opt != cudaSuccess) return fail_cuda(opt, "cudaFuncSetAttribute(merge_lists_kernel)");
-    merge_lists_kernel<<<batch, kMergeThreads, static_cast<size_t>(cap) * 8, static_cast<cudaStream_t>(stream)>>>(
-        list_indices, list_scores, lists, batch, k_in, k, cap, out_indices, out_scores);
+    {
+        KernelTimer timer("merge", static_cast<cudaStream_t>(stream));
+        merge_lists_kernel<<<batch, kMergeThreads, static_cast<size_t>(cap) * 8,
+                             static_cast<cudaStream_t>(stream)>>>(list_indices, list_scores, lists, batch, k_in, k,
+                                                                  cap, out_indices, out_scores);
+    }
     const cudaError_t e = cudaGetLastError();
     return e == cudaSuccess ? ok() : fail_cuda(e, "merge_lists_kernel launch");
 }

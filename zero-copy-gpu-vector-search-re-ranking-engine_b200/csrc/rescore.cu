@@ -365,7 +365,11 @@ int launch_rescore(RescorePlan& plan, int dtype, int metric, int batch, bool emi
         attr[0].val.clusterDim.z = 1;
         cfg.attrs = attr;
         cfg.numAttrs = 1;
-        const cudaError_t e = cudaLaunchKernelEx(&cfg, fn, p);
+        cudaError_t e;
+        {
+            KernelTimer timer("rescore", stream);
+            e = cudaLaunchKernelEx(&cfg, fn, p);
+        }
         if (e != cudaSuccess) return fail_cuda(e, "zcgvs rescore launch");
     }
     return ok();

@@ -290,7 +290,10 @@ int launch(const ScanPlan& plan, ScanParams& params, cudaStream_t stream) {
     const dim3 grid(static_cast<unsigned>(plan.passes), static_cast<unsigned>(plan.grid_rows));
     const int threads = plan.fast ? kFastThreads : kScanThreads;
     const int smem = plan.fast ? plan.fast_smem : plan.smem_total;
-    kernel<<<grid, threads, smem, stream>>>(params);
+    {
+        KernelTimer timer("scan", stream);
+        kernel<<<grid, threads, smem, stream>>>(params);
+    }
     status = cudaGetLastError();
     if (status != cudaSuccess) return fail_cuda(status, "scan_kernel launch");
     return ok();
@@ -303,14 +306,18 @@ int launch(const ScanPlan& plan, ScanParams& params, cudaStream_t stream) {
 namespace zc {
 namespace {
 
-// Large batches over per-row int8 corpora run on the tensor cores (zcgvs_gemm_topk): the same
-// exact int32 dot products, so the same results bit for bit. Smaller problems stay on the
-// streaming scan, whose single pass has no fixed cost.
+// Large batches over per-row int8 and 1-bit corpora run on the tensor cores (zcgvs_gemm_topk):
+// the same exact integer dot products, so the same results bit for bit. Smaller problems stay on
+// the streaming scan, whose single pass has no fixed cost. A 1-bit row costs the streaming scan
+// 32 popcounts per 1,024 dimensions and query, so the tensor cores take over at smaller batches.
 constexpr int kGemmMinBatch = 64;
+constexpr int kGemmMinBatchBinary = 16;
 constexpr long long kGemmMinDocs = 65536;
 
 bool gemm_eligible(int dtype, long long n, int dim, int batch, int metric) {
-    return dtype == ZCGVS_DTYPE_I8_ROW && batch >= kGemmMinBatch && n >= kGemmMinDocs && dim % 128 == 0 &&
+    if (n < kGemmMinDocs || dim % 128 != 0) return false;
+    if (dtype == ZCGVS_DTYPE_BINARY) return batch >= kGemmMinBatchBinary;  // every metric scores Hamming
+    return dtype == ZCGVS_DTYPE_I8_ROW && batch >= kGemmMinBatch &&
            (metric == ZCGVS_METRIC_DOT || metric == ZCGVS_METRIC_COSINE);
 }
 

@@ -31,6 +31,8 @@ SIGNATURES = {
     "zcgvs_last_cuda_error": (_i32, []),
     "zcgvs_workspace_init": (_i32, [_P, _sz, _P]),
     "zcgvs_workspace_status": (_i32, [_P, _sz, _P, _P]),
+    "zcgvs_kernel_timing": (_i32, [_i32]),
+    "zcgvs_kernel_timing_read": (_i32, [ctypes.c_char_p, _P, _P]),
     "zcgvs_scan_topk_workspace_bytes": (_sz, [_i32, _i64, _i32, _i32, _i32]),
     "zcgvs_scan_topk": (_i32, [_P, _i32, _f32, _P, _i64, _i32, _P, _i32, _P, _i32, _i32, _i32,
                                _P, _P, _P, _sz, _P]),
@@ -136,6 +138,19 @@ class Workspace:
         check(lib().zcgvs_workspace_status(_ptr(self.buffer), self.buffer.numel(), ctypes.byref(value),
                                            _stream(stream)))
         return int(value.value)
+
+
+def kernel_timing(enable: bool) -> None:
+    """Starts (clearing earlier records) or stops CUDA-event timing of the library's kernels."""
+    check(lib().zcgvs_kernel_timing(1 if enable else 0))
+
+
+def kernel_timing_read(tag: str) -> tuple[float, int]:
+    """(summed milliseconds, launches) of the recorded launches tagged `tag`."""
+    total = ctypes.c_double(0.0)
+    count = ctypes.c_int(0)
+    check(lib().zcgvs_kernel_timing_read(tag.encode(), ctypes.byref(total), ctypes.byref(count)))
+    return float(total.value), int(count.value)
 
 
 def scan_topk_workspace_bytes(dtype: int, doc_count: int, dim: int, batch: int, k: int) -> int:
@@ -300,7 +315,7 @@ def merge_topk(list_indices, list_scores, k: int, out=None, stream=None):
 def gemm_topk(corpus, dtype: int, dim: int, queries, k: int, *, row_scales=None, mask=None,
               metric: int = METRIC_DOT, id_base: int = 0, workspace: Workspace | None = None, out=None,
               stream=None):
-    """Tensor-core batched top-k (F16 or I8_ROW corpora). Returns (ids [B, k], scores [B, k])."""
+    """Tensor-core batched top-k (F16, I8_ROW or BINARY corpora). Returns (ids [B, k], scores [B, k])."""
     import torch
 
     doc_count = corpus.shape[0]
