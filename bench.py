@@ -292,12 +292,59 @@ class Workload:
     def kernel_ms(self, kern, steps):
         return sum(kern[t][0] for t in self.dominant) / steps
 
+    # Batch-1 workloads replay CUDA graphs, as a serving loop does (the reference's Searcher
+    # captures its pipeline the same way): one graph per query of a pool for the device-resident
+    # steps, and one over the device staging buffers for the end-to-end steps. The graphs hold
+    # the same library launches as a direct call; the kernel-timing pass makes direct calls.
+    graphs = False
+    pool = 64
+
+    def step(self, i, stream):
+        g = getattr(self, "g_step", None)
+        if g:
+            g[i % len(g)].replay()
+        else:
+            self.step_direct(i, stream)
+
+    def search_staged(self, stream):
+        g = getattr(self, "g_e2e", None)
+        if g is not None:
+            g.replay()
+        else:
+            self.search_staged_direct(stream)
+
+    def capture(self, torch):
+        if not self.graphs:
+            return
+        s = torch.cuda.Stream()
+        s.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(s):
+            for i in range(self.pool):
+                self.step_direct(i, s)
+            self.search_staged_direct(s)
+        s.synchronize()
+        self.g_step = []
+        for i in range(self.pool):
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=s):
+                self.step_direct(i, s)
+            self.g_step.append(g)
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g, stream=s):
+            self.search_staged_direct(s)
+        self.g_e2e = g
+        torch.cuda.synchronize()
+
     @staticmethod
-    def tensor_peak(peaks, kind):
-        # int8 dense tensor peak: twice the measured bf16 burst (B200 int8 : bf16 = 2 : 1 dense).
+    def tensor_peak(peaks, kind, sustained=False):
+        # The burst figure for a kernel timed on its own, the sustained one (seconds of
+        # back-to-back GEMMs under the power cap) for a kernel that runs for seconds; int8 dense
+        # = twice bf16 dense on B200.
+        key, what = ("bf16_tflops_sustained", "sustained") if sustained and "bf16_tflops_sustained" in peaks else (
+            "bf16_tflops", "burst")
         if kind == "i8":
-            return 2.0 * float(peaks["bf16_tflops"]), "2 x measured bf16 burst (int8 dense = 2 x bf16 dense)"
-        return float(peaks["bf16_tflops"]), "measured bf16 burst"
+            return 2.0 * float(peaks[key]), f"2 x measured bf16 {what} (int8 dense = 2 x bf16 dense)"
+        return float(peaks[key]), f"measured bf16 {what}"
 
 
 class Cfg2(Workload):
@@ -336,14 +383,19 @@ class Cfg2(Workload):
         j = (i % nb) * self.B
         return src[j:j + self.B]
 
-    def step(self, i, stream):
+    graphs = property(lambda self: self.B == 1)
+
+    def step_direct(self, i, stream):
         self.zc.scan_topk(self.codes, self.zc.DTYPE_I8_ROW, self.D, self._q(i, self.queries), self.K,
                           row_scales=self.scales, workspace=self.ws, out=self.out, stream=stream)
 
-    def e2e_step(self, i, stream):
-        self.d_q.copy_(self._q(i, self.h_queries), non_blocking=True)
+    def search_staged_direct(self, stream):
         self.zc.scan_topk(self.codes, self.zc.DTYPE_I8_ROW, self.D, self.d_q, self.K, row_scales=self.scales,
                           workspace=self.ws, out=self.out, stream=stream)
+
+    def e2e_step(self, i, stream):
+        self.d_q.copy_(self._q(i, self.h_queries), non_blocking=True)
+        self.search_staged(stream)
         self.h_out[0].copy_(self.out[0], non_blocking=True)
         self.h_out[1].copy_(self.out[1], non_blocking=True)
         stream.synchronize()
@@ -400,16 +452,21 @@ class Cfg1(Workload):
                       torch.empty((1, self.K), dtype=torch.float32).pin_memory())
         self.d_q = torch.empty((1, self.D), dtype=torch.float32, device=device)
 
-    def step(self, i, stream):
+    graphs = True
+
+    def step_direct(self, i, stream):
         j = i % self.NQ
         self.zc.scan_topk(self.corpus, self.zc.DTYPE_F32, self.D, self.queries[j:j + 1], self.K,
                           metric=self.zc.METRIC_COSINE, workspace=self.ws, out=self.out, stream=stream)
 
+    def search_staged_direct(self, stream):
+        self.zc.scan_topk(self.corpus, self.zc.DTYPE_F32, self.D, self.d_q, self.K, metric=self.zc.METRIC_COSINE,
+                          workspace=self.ws, out=self.out, stream=stream)
+
     def e2e_step(self, i, stream):
         j = i % self.NQ
         self.d_q.copy_(self.h_queries[j:j + 1], non_blocking=True)
-        self.zc.scan_topk(self.corpus, self.zc.DTYPE_F32, self.D, self.d_q, self.K, metric=self.zc.METRIC_COSINE,
-                          workspace=self.ws, out=self.out, stream=stream)
+        self.search_staged(stream)
         self.h_out[0].copy_(self.out[0], non_blocking=True)
         self.h_out[1].copy_(self.out[1], non_blocking=True)
         stream.synchronize()
@@ -473,7 +530,7 @@ class Cfg3(Workload):
         self.zc.rescore_topk(self.store_i16, self.zc.DTYPE_F16, self.D, q, self.cand[0], self.K,
                              metric=self.zc.METRIC_COSINE, out=self.out, stream=stream)
 
-    def step(self, i, stream):
+    def step_direct(self, i, stream):
         j = (i % (self.NQ // self.B)) * self.B
         self._run(self.queries[j:j + self.B], stream)
 
@@ -559,7 +616,7 @@ class Cfg4(Workload):
             return self.gemm_local(q, self.K, 0)
         return self.search.search(q, self.K)
 
-    def step(self, i, stream):
+    def step_direct(self, i, stream):
         self._run(self.queries)
 
     def e2e_step(self, i, stream):
@@ -578,7 +635,9 @@ class Cfg4(Workload):
         rows = self.end - self.begin
         flops = 2.0 * self.B * rows * self.D
         achieved = flops / (kernel_ms * 1e-3) / 1e12
-        peak, src = self.tensor_peak(peaks, "f16")
+        # One filter launch runs for a third of a second and the steps run back to back for
+        # seconds under the 1 kW power cap: the sustained GEMM figure is its denominator.
+        peak, src = self.tensor_peak(peaks, "f16", sustained=True)
         return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TFLOP/s", "frac": achieved / peak,
                 "traffic": profiled_traffic(self.name), "peak_source": f"{peak_kind}: {src}",
                 "kernel": "zc::gemm::gemm_scan_kernel<kModeF16,kFilter>",
@@ -631,15 +690,20 @@ class Cfg5(Workload):
         self.zc.hybrid_topk(self.dense_i16, self.zc.DTYPE_F16, self.D, q, self.K, self.index, t, 0.5,
                             metric=self.zc.METRIC_COSINE, workspace=self.ws, out=self.out, stream=stream)
 
-    def step(self, i, stream):
+    graphs = True
+
+    def step_direct(self, i, stream):
         j = i % self.NQ
         self._run(self.queries[j:j + 1], self.terms[j:j + 1], stream)
+
+    def search_staged_direct(self, stream):
+        self._run(self.d_q, self.d_t, stream)
 
     def e2e_step(self, i, stream):
         j = i % self.NQ
         self.d_q.copy_(self.h_queries[j:j + 1], non_blocking=True)
         self.d_t.copy_(self.h_terms[j:j + 1], non_blocking=True)
-        self._run(self.d_q, self.d_t, stream)
+        self.search_staged(stream)
         self.h_out[0].copy_(self.out[0], non_blocking=True)
         self.h_out[1].copy_(self.out[1], non_blocking=True)
         stream.synchronize()
@@ -761,6 +825,7 @@ def run_ours(args):
     steps = args.steps if args.steps is not None else wl.steps
     warmup = args.warmup if args.warmup is not None else wl.warmup
     wl.setup(torch, zc, device, rank, world)
+    wl.capture(torch)
     stream = torch.cuda.current_stream()
 
     for i in range(warmup):
@@ -792,7 +857,7 @@ def run_ours(args):
             "rescore", "lexical", "merge")
     zc.kernel_timing(True)
     for i in range(steps):
-        wl.step(i, stream)
+        wl.step_direct(i, stream)
     torch.cuda.synchronize()
     zc.kernel_timing(False)
     kern = {t: zc.kernel_timing_read(t) for t in tags}
@@ -833,7 +898,7 @@ def run_ours(args):
             "ms_per_step": elapsed_ms / steps, "p50_ms": per_step[len(per_step) // 2],
             "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None, "dtype": wl.dtype,
             "data": "synthetic",
-            "config": wl.config(world),
+            "config": dict(wl.config(world), launch="cuda-graph replay per query" if wl.graphs else "direct calls"),
             "roofline": dict(wl.roofline(kernel_ms, peaks, peak_kind), kernel_ms=kernel_ms),
             "kernels_ms_per_step": {t: v[0] / steps for t, v in kern.items() if v[1]},
             "e2e": {"value": total_units * e2e_steps / e2e_s, "unit": UNIT,

@@ -157,21 +157,34 @@ __global__ void __launch_bounds__(kSelectThreads) threshold_kernel(const float* 
     }
 }
 
-// Moves the mailbox entries of every filter epilogue warp (blockIdx.y) into per-query
-// candidate buffers.
+// Moves the mailbox entries of every filter epilogue warp (one mailbox segment per warp of
+// this kernel) into per-query candidate buffers. The lanes of a warp holding entries of the
+// same query take their slots with one atomic (few queries with many candidates each would
+// otherwise serialise on their counters).
 // On a retry pass (retry != nullptr) it runs only when some query is being retried.
-__global__ void bucket_kernel(const unsigned long long* __restrict__ mb_key, const unsigned int* __restrict__ mb_query,
-                              const unsigned int* __restrict__ mb_count, int mb_cap, unsigned int* cand_count,
-                              unsigned long long* cand, int cap, const unsigned int* retry) {
+constexpr int kBucketThreads = 256;
+
+__global__ void __launch_bounds__(kBucketThreads) bucket_kernel(
+    const unsigned long long* __restrict__ mb_key, const unsigned int* __restrict__ mb_query,
+    const unsigned int* __restrict__ mb_count, int segments, int mb_cap, unsigned int* cand_count,
+    unsigned long long* cand, int cap, const unsigned int* retry) {
     if (retry != nullptr && *reinterpret_cast<const volatile unsigned int*>(retry) == 0u) return;
-    const int c = blockIdx.y;
+    const int c = blockIdx.x * (kBucketThreads / 32) + static_cast<int>(threadIdx.x >> 5);
+    if (c >= segments) return;
     const unsigned int n = mb_count[c];
     const size_t base = static_cast<size_t>(c) * mb_cap;
-    for (unsigned int i = blockIdx.x * blockDim.x + threadIdx.x; i < n; i += gridDim.x * blockDim.x) {
-        if (mb_key[base + i] == 0ull) continue;  // a tie rejected by its key
-        const unsigned int q = mb_query[base + i];
-        const unsigned int slot = atomicAdd(cand_count + q, 1u);
-        if (slot < static_cast<unsigned int>(cap)) cand[static_cast<size_t>(q) * cap + slot] = mb_key[base + i];
+    const unsigned int lane = threadIdx.x & 31u;
+    for (unsigned int i0 = 0; i0 < n; i0 += 32u) {
+        const unsigned int i = i0 + lane;
+        const unsigned long long key = i < n ? mb_key[base + i] : 0ull;  // 0: empty, or a tie rejected by its key
+        const unsigned int q = key != 0ull ? mb_query[base + i] : 0xFFFFFFFFu;
+        const unsigned int peers = __match_any_sync(0xffffffffu, q);
+        if (q == 0xFFFFFFFFu) continue;
+        const int leader = __ffs(peers) - 1;
+        unsigned int slot = 0u;
+        if (static_cast<int>(lane) == leader) slot = atomicAdd(cand_count + q, static_cast<unsigned int>(__popc(peers)));
+        slot = __shfl_sync(peers, slot, leader) + static_cast<unsigned int>(__popc(peers & ((1u << lane) - 1u)));
+        if (slot < static_cast<unsigned int>(cap)) cand[static_cast<size_t>(q) * cap + slot] = key;
     }
 }
 
@@ -560,9 +573,10 @@ int zcgvs_gemm_topk(const void* corpus, int dtype, const float* row_scales, int6
         if (status != ZCGVS_OK) return status;
         {
             KernelTimer timer("gemm_bucket", st);
-            bucket_kernel<<<dim3(8, filter_ctas * kEpiWarps), 256, 0, st>>>(p.mb_key, p.mb_query, p.mb_count,
-                                                                            g.mb_cap, cand_count, cand, kCandCap,
-                                                                            p.retry);
+            const int segments = filter_ctas * kEpiWarps;
+            const int blocks = (segments + kBucketThreads / 32 - 1) / (kBucketThreads / 32);
+            bucket_kernel<<<blocks, kBucketThreads, 0, st>>>(p.mb_key, p.mb_query, p.mb_count, segments, g.mb_cap,
+                                                             cand_count, cand, kCandCap, p.retry);
         }
         e = cudaGetLastError();
         if (e != cudaSuccess) return fail_cuda(e, "bucket_kernel launch");

@@ -23,7 +23,7 @@
 // 1-bit corpora (kModeBin, the Hamming score (d - 2 h) / d of src/cuda/similarity.cu:166-240)
 // run on the same int8 tensor-core path. A 2-D TMA brings 128 packed bytes (1,024 dimensions) of
 // 256 rows at a time into one of two raw slots (128-byte swizzle, so that reading one 16-byte
-// column of consecutive rows hits distinct banks), and four more warps (10-13, the expanders)
+// column of consecutive rows hits distinct banks), and eight more warps (10-17, the expanders)
 // turn each 16-byte K slice (128 dimensions) of it into the int8 operand of a stage: bit b of a word becomes the byte 0xFF (-1) when set, else 0 (one shift
 // and one sign-replicating byte permute per 4 output bytes). The queries are prepared as
 // q' = -2 s (s = +1 for a set bit, else -1), so the accumulator holds 2 sum_i s_i b_i and the
@@ -62,7 +62,7 @@ constexpr int kHalf = kBN / 2;            // columns per epilogue warp
 constexpr int kTmemCols = 512;            // two 256-column accumulators
 constexpr int kChunks = kBN / 32;         // threshold granularity: 32-document chunks per tile
 // 1-bit corpora: expander warps and the raw slots (128 packed bytes = 8 K slices of 256 rows).
-constexpr int kExpWarps = 4;
+constexpr int kExpWarps = 8;
 constexpr int kFirstExpWarp = kEpiWarps + 2;
 constexpr int kSlicesPerUnit = 8;
 constexpr int kRawBytes = kBN * 128;      // 32 KB per raw slot
@@ -179,10 +179,21 @@ __device__ __forceinline__ uint32_t sign_bytes(uint32_t x) {
     return r;
 }
 
-// One packed word -> 32 int8 operand bytes: o[j] byte i = -(bit 8 i + j of w).
-__device__ __forceinline__ void expand_word(uint32_t w, uint4& lo, uint4& hi) {
-    lo = make_uint4(sign_bytes(w << 7), sign_bytes(w << 6), sign_bytes(w << 5), sign_bytes(w << 4));
-    hi = make_uint4(sign_bytes(w << 3), sign_bytes(w << 2), sign_bytes(w << 1), sign_bytes(w));
+// w * m as an integer multiply (the FMA pipe), for a multiplier the compiler cannot see.
+__device__ __forceinline__ uint32_t mul_lo(uint32_t w, uint32_t m) {
+    uint32_t r;
+    asm("mul.lo.u32 %0, %1, %2;" : "=r"(r) : "r"(w), "r"(m));
+    return r;
+}
+
+// One packed word -> 32 int8 operand bytes: o[j] byte i = -(bit 8 i + j of w). pow2[k] = 2^k
+// held in registers: the seven shifts run as multiplies on the FMA pipe, leaving the integer
+// ALU to the byte permutes (and to the epilogue).
+__device__ __forceinline__ void expand_word(uint32_t w, const uint32_t (&pow2)[8], uint4& lo, uint4& hi) {
+    lo = make_uint4(sign_bytes(mul_lo(w, pow2[7])), sign_bytes(mul_lo(w, pow2[6])), sign_bytes(mul_lo(w, pow2[5])),
+                    sign_bytes(mul_lo(w, pow2[4])));
+    hi = make_uint4(sign_bytes(mul_lo(w, pow2[3])), sign_bytes(mul_lo(w, pow2[2])), sign_bytes(mul_lo(w, pow2[1])),
+                    sign_bytes(w));
 }
 
 // Named barrier over `count` threads that also ANDs a predicate across them.
@@ -407,14 +418,18 @@ __global__ void __launch_bounds__(threads_of<MODE>(), 1)
         }
     } else if (warp >= kFirstExpWarp) {
         if constexpr (MODE == kModeBin) {
-            // ---------------- expander warps 10-13 (1-bit corpora) ----------------
-            // Thread et expands rows et and et + 128 of each K slice. Thread 0 fetches the raw
+            // ---------------- expander warps 10-17 (1-bit corpora) ----------------
+            // Thread et expands row et of each K slice. Thread 0 fetches the raw
             // units (128 packed bytes of the tile's rows) into the two slots, the next one as soon
             // as every expander is done with a slot. A wait that runs out makes the warp skip the
             // rest of the unit; the four warps agree at the unit's end whether to go on, so the
             // named barrier always sees all of them.
             constexpr int kExpThreads = kExpWarps * 32;
             const int et = tid - kFirstExpWarp * 32;
+            uint32_t pow2[8];
+            const uint32_t one = p.kblocks > 0 ? 1u : 0u;  // 1, as a runtime value
+#pragma unroll
+            for (int k = 0; k < 8; ++k) pow2[k] = one << k;
             const int units_per_item = (p.kblocks + kSlicesPerUnit - 1) / kSlicesPerUnit;
             long long pw = walk_first(p, items);  // next unit to fetch: item pw, unit pu
             int pu = 0;
@@ -457,7 +472,7 @@ __global__ void __launch_bounds__(threads_of<MODE>(), 1)
                             const int col = kb - kb0;  // 16-byte column of the raw rows
                             uint8_t* dst = smem + static_cast<size_t>(s) * kStageBytes + kStageA;
 #pragma unroll
-                            for (int h = 0; h < 2; ++h) {
+                            for (int h = 0; h < kBN / kExpThreads; ++h) {
                                 const int r = et + h * kExpThreads;
                                 // Both the raw slot and the stage are 128-byte swizzled K-major
                                 // tiles: 16-byte unit x of row r sits at x ^ (r % 8).
@@ -468,7 +483,7 @@ __global__ void __launch_bounds__(threads_of<MODE>(), 1)
 #pragma unroll
                                 for (int wi = 0; wi < 4; ++wi) {
                                     uint4 lo, hi;
-                                    expand_word(words[wi], lo, hi);
+                                    expand_word(words[wi], pow2, lo, hi);
                                     *reinterpret_cast<uint4*>(out + (((2 * wi) ^ (r & 7)) << 4)) = lo;
                                     *reinterpret_cast<uint4*>(out + (((2 * wi + 1) ^ (r & 7)) << 4)) = hi;
                                 }
@@ -607,8 +622,11 @@ __global__ void __launch_bounds__(threads_of<MODE>(), 1)
             const float dimf = static_cast<float>(p.dim);
             const uint32_t taddr = tmem_base + (static_cast<uint32_t>((warp & 3) * 32) << 16) +
                                    static_cast<uint32_t>(a * kBN + half * kHalf);
+            // A warp whose 32 rows are all padding (or answered) queries only hands the
+            // accumulator back.
+            const int chunks = __any_sync(0xffffffffu, EPI == kFilter ? live : q_ok) ? 4 : 0;
 #pragma unroll 1
-            for (int cl = 0; cl < 4; ++cl) {
+            for (int cl = 0; cl < chunks; ++cl) {
                 uint32_t v[32];
                 __syncwarp();  // tcgen05.ld is warp-collective; the append branch below diverges
                 tmem_ld32(taddr + static_cast<uint32_t>(cl * 32), v);

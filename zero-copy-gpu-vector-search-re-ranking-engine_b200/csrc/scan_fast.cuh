@@ -200,17 +200,7 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
                 scount += __popc(ballot);
                 if (scount > kSelCap - 32 || (sthr == 0ull && scount >= k + 32)) {
                     __syncwarp();
-                    u64 v[kSelE];
-#pragma unroll
-                    for (int e = 0; e < kSelE; ++e) {
-                        const int at = lane * kSelE + e;
-                        v[e] = at < scount ? sbuf[at] : 0ull;
-                    }
-                    warp_sort_desc_regs<kSelE>(v, lane);
-                    __syncwarp();
-#pragma unroll
-                    for (int e = 0; e < kSelE; ++e) sbuf[lane * kSelE + e] = v[e];
-                    __syncwarp();
+                    warp_sort_buffer(sbuf, scount, lane);
                     if (scount >= k) {
                         sthr = sbuf[k - 1];
                         if (lane == 0) *cta_thr = sthr;
@@ -228,19 +218,8 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
         // Keep the selector's state for the end of the kernel: sort it once more so sbuf holds
         // the exact top of every key it saw.
         __syncwarp();
-        {
-            u64 v[kSelE];
-#pragma unroll
-            for (int e = 0; e < kSelE; ++e) {
-                const int at = lane * kSelE + e;
-                v[e] = at < scount ? sbuf[at] : 0ull;
-            }
-            warp_sort_desc_regs<kSelE>(v, lane);
-            __syncwarp();
-#pragma unroll
-            for (int e = 0; e < kSelE; ++e) sbuf[lane * kSelE + e] = v[e];
-            if (lane == 0) s_merge_count = min(scount, k);
-        }
+        warp_sort_buffer(sbuf, scount, lane);
+        if (lane == 0) s_merge_count = min(scount, k);
     } else {
         // ---------------- consumer warps ----------------
         const int grp = lane / LPR;

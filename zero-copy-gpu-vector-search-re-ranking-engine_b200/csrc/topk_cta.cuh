@@ -82,6 +82,38 @@ __device__ __forceinline__ void warp_sort_desc_regs(u64 (&v)[E], int lane) {
     }
 }
 
+// Sorts the first n (<= 32 * E) keys of a shared buffer descending with one warp; entries
+// [n, 32 * E) become 0.
+template <int E>
+__device__ __forceinline__ void warp_sort_buffer_e(u64* buf, int n, int lane) {
+    u64 v[E];
+#pragma unroll
+    for (int e = 0; e < E; ++e) {
+        const int at = lane * E + e;
+        v[e] = at < n ? buf[at] : 0ull;
+    }
+    warp_sort_desc_regs<E>(v, lane);
+    __syncwarp();
+#pragma unroll
+    for (int e = 0; e < E; ++e) buf[lane * E + e] = v[e];
+    __syncwarp();
+}
+
+// One warp sorts the first n (<= 256) keys of a shared buffer descending, with a network only
+// as wide as n needs (32, 64, 128 or 256 keys): a single warp's sort is a chain of dependent
+// shuffles, so its cost follows the width.
+__device__ __forceinline__ void warp_sort_buffer(u64* buf, int n, int lane) {
+    if (n <= 32) {
+        warp_sort_buffer_e<1>(buf, n, lane);
+    } else if (n <= 64) {
+        warp_sort_buffer_e<2>(buf, n, lane);
+    } else if (n <= 128) {
+        warp_sort_buffer_e<4>(buf, n, lane);
+    } else {
+        warp_sort_buffer_e<8>(buf, n, lane);
+    }
+}
+
 // Sorts the buffers of the queries selected by `mask` (bit q) descending and truncates them
 // to k. Only the filled prefix is sorted (rounded up to a power of two), with shift-only index
 // arithmetic. Must be called by every thread of the CTA, after a __syncthreads() that follows
@@ -210,9 +242,60 @@ __device__ void topk_offer_all(const TopkSmem& t, int q, int total, u64 floor_ke
 // the merged k-th key is >= F and only keys >= F are offered. For many short lists (one per
 // CTA) j = 0: F is the k-th largest list head, which leaves a few hundred candidates out of
 // lists * k.
+//
+// Small k (<= 16, at most 256 lists, all lists fitting the buffer next to 256 candidates): the
+// lists are copied into the buffer, one warp sorts their heads for F (the k-th largest head, so
+// exactly k lists hold keys >= F and at most k * k keys pass), the CTA keeps the keys >= F and
+// one warp sorts them. This replaces two CTA-wide bitonic sorts (a barrier per stage) with two
+// short single-warp ones.
+__device__ inline bool topk_merge_lists_small(const TopkSmem& t, int q_local, const u64* src, int lists,
+                                              int nthreads, u64* s_scratch) {
+    const int k = t.k;
+    const int total = lists * k;
+    if (k > 16 || lists > 256 || total + 256 > t.cap) return false;
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    u64* all = t.buf + q_local * t.cap;  // [total] list keys
+    u64* cand = all + total;             // [256] heads, then the keys >= F
+    for (int i = tid; i < total; i += nthreads) all[i] = __ldcg(src + i);
+    if (tid == 0) t.count[q_local] = 0;
+    __syncthreads();
+    if (tid < 32) {
+        for (int c = lane; c < lists; c += 32) cand[c] = all[c * k];
+        __syncwarp();
+        warp_sort_buffer(cand, lists, lane);
+        // With fewer than k non-empty lists the floor is 1: every non-empty key (fewer than
+        // k * k of them) passes.
+        if (lane == 0) s_scratch[0] = (lists >= k && cand[k - 1] > 1ull) ? cand[k - 1] : 1ull;
+    }
+    __syncthreads();
+    const u64 floor_key = s_scratch[0];
+    for (int i = tid; i < total; i += nthreads) {
+        const u64 key = all[i];
+        if (key >= floor_key) {
+            const int slot = atomicAdd(&t.count[q_local], 1);
+            if (slot < 256) cand[slot] = key;
+        }
+    }
+    __syncthreads();
+    if (tid < 32) {
+        const int n = min(t.count[q_local], 256);
+        warp_sort_buffer(cand, n, lane);
+        const int kept = min(n, k);
+        if (lane < kept) all[lane] = cand[lane];
+        __syncwarp();
+        if (lane == 0) {
+            t.count[q_local] = kept;
+            t.thr[q_local] = n >= k ? cand[k - 1] : 0ull;
+        }
+    }
+    __syncthreads();
+    return true;
+}
+
 __device__ inline void topk_merge_lists(const TopkSmem& t, int q_local, const u64* src, int lists,
                                         int nthreads, u64* s_scratch /* >= 32 entries */) {
-    (void)s_scratch;
+    if (topk_merge_lists_small(t, q_local, src, lists, nthreads, s_scratch)) return;
     const int tid = threadIdx.x;
     const int k = t.k;
     const int j = (k + lists - 1) / lists - 1;
