@@ -161,3 +161,36 @@ def test_hybrid_without_terms_is_dense_search(zc, orc):
     ref_idx, ref_val = orc.scan_topk(storage, 4, dim, queries, 20, row_scales=row_scales)
     np.testing.assert_array_equal(idx.cpu().numpy(), ref_idx)
     np.testing.assert_array_equal(val.cpu().numpy(), ref_val)
+
+
+def test_hybrid_sorted_postings_with_runs_and_ragged_tail(zc, orc):
+    """Sorted posting lists holding runs of equal documents (a hand-made index), list lengths
+    that are not multiples of 4 and a total that is not either: the 16-byte posting loads, the
+    run heads found across lanes and groups, and the element loads at the index's end must give
+    the oracle's sequential sums bit for bit."""
+    import torch
+
+    n, dim, vocab, k, batch = 7000, 128, 40, 50, 5
+    rng = np.random.default_rng(77)
+    lists = []
+    for t in range(vocab):
+        df = int(rng.integers(1, 900)) | 1  # odd lengths
+        lists.append(np.sort(rng.integers(0, n, size=df)).astype(np.int32))  # with repeats
+    offsets = np.zeros(vocab + 1, dtype=np.int64)
+    offsets[1:] = np.cumsum([len(x) for x in lists])
+    docs = np.concatenate(lists)
+    weights = rng.uniform(0.1, 3.0, size=docs.shape[0]).astype(np.float32)
+    assert docs.shape[0] % 4 != 0
+    terms = np.full((batch, 6), -1, dtype=np.int32)
+    for q in range(batch):
+        terms[q, :3 + q % 3] = rng.choice(vocab, size=3 + q % 3, replace=False)
+    corpus = orc.normal_rows(n, dim, 31)
+    queries = orc.normal_rows(batch, dim, 32)
+    storage, _, row_scales = orc.encode(corpus, 4)
+    idx, val = zc.hybrid_topk(dev(storage), 4, dim, dev(queries), k, zc.LexicalIndex(offsets, docs, weights),
+                              dev(terms), 0.0, row_scales=dev(row_scales))
+    torch.cuda.synchronize()
+    ref_idx, ref_val = orc.hybrid_topk(storage, 4, dim, queries, k, offsets, docs, weights, vocab, terms, 0.0,
+                                       row_scales=row_scales)
+    np.testing.assert_array_equal(idx.cpu().numpy(), ref_idx)
+    np.testing.assert_array_equal(val.cpu().numpy(), ref_val)

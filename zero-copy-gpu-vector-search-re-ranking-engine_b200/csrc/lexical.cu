@@ -54,6 +54,7 @@ struct LexParams {
     float* out;             // [batch, n]
     float* part_max;        // [batch, gridDim.x] or nullptr
     int sorted;             // postings sorted by document within each term (else: any order)
+    int vec;                // sorted, docs and weights 16-byte aligned: 16-byte posting loads
 };
 
 // First index in [lo, hi) whose document id is >= target (hi if none), for sorted docs[].
@@ -89,6 +90,8 @@ __global__ void __launch_bounds__(kLexThreads) lexical_kernel(const LexParams p)
     const int count = static_cast<int>(min(static_cast<long long>(p.docs_per_cta), p.n - d0));
     const size_t row = static_cast<size_t>(q) * p.n;
     const int* terms = p.terms + static_cast<size_t>(q) * p.stride;
+    // Postings in the index (CSR end): the 16-byte loads never reach past it.
+    const long long total = p.vec ? __ldg(p.offsets + p.vocab) : 0;
 
     for (int i = tid; i < count; i += kLexThreads) acc[i] = p.init != nullptr ? p.init[row + d0 + i] : 0.0f;
 
@@ -146,13 +149,76 @@ __global__ void __launch_bounds__(kLexThreads) lexical_kernel(const LexParams p)
         for (int t = 0; t < slots; ++t) {
             const long long lo = s_lo[t];
             const long long hi = s_hi[t];
-            for (long long i = lo + tid; i < hi; i += kLexThreads) {
-                const int doc = __ldg(p.docs + i);
-                if (i > lo && __ldg(p.docs + i - 1) == doc) continue;  // not the head of its run
-                float a = acc[doc - d0];
-                a = __fadd_rn(a, __ldg(p.weights + i));
-                for (long long j = i + 1; j < hi && __ldg(p.docs + j) == doc; ++j) a = __fadd_rn(a, __ldg(p.weights + j));
-                acc[doc - d0] = a;
+            if (p.vec) {
+                // Thread tid of a round owns the 4 postings of 16-byte group g = g0 + tid (two
+                // groups per round, loaded before either is used); a posting is the head of its
+                // run unless the posting before it (the same thread's, the previous lane's last
+                // one, or for lane 0 a load) holds the same document.
+                const long long g_lo = lo >> 2;
+                const long long g_hi = (hi + 3) >> 2;
+                for (long long g0 = g_lo; g0 < g_hi; g0 += 2 * kLexThreads) {
+                    int4 dv[2];
+                    float4 wv[2];
+                    int before[2];
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const long long g = g0 + u * kLexThreads + tid;
+                        if (g < g_hi && 4 * g + 3 < total) {
+                            dv[u] = __ldg(reinterpret_cast<const int4*>(p.docs) + g);
+                            wv[u] = __ldg(reinterpret_cast<const float4*>(p.weights) + g);
+                        } else {
+                            // Past the slice, or the index's last partial group: element loads.
+                            int dd[4] = {-1, -1, -1, -1};
+                            float ww[4] = {0.f, 0.f, 0.f, 0.f};
+                            if (g < g_hi) {
+#pragma unroll
+                                for (int e = 0; e < 4; ++e) {
+                                    if (4 * g + e < total) {
+                                        dd[e] = __ldg(p.docs + 4 * g + e);
+                                        ww[e] = __ldg(p.weights + 4 * g + e);
+                                    }
+                                }
+                            }
+                            dv[u] = make_int4(dd[0], dd[1], dd[2], dd[3]);
+                            wv[u] = make_float4(ww[0], ww[1], ww[2], ww[3]);
+                        }
+                        before[u] = (lane == 0 && g < g_hi && 4 * g > lo) ? __ldg(p.docs + 4 * g - 1) : -1;
+                    }
+#pragma unroll
+                    for (int u = 0; u < 2; ++u) {
+                        const long long g = g0 + u * kLexThreads + tid;
+                        const int up = __shfl_up_sync(0xffffffffu, dv[u].w, 1);
+                        if (g >= g_hi) continue;
+                        const int d[4] = {dv[u].x, dv[u].y, dv[u].z, dv[u].w};
+                        const float w[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
+                        int prev = lane == 0 ? before[u] : up;
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const long long i = 4 * g + e;
+                            const int doc = d[e];
+                            const bool head = i >= lo && i < hi && (i == lo || prev != doc);
+                            prev = doc;
+                            if (!head) continue;
+                            float a = __fadd_rn(acc[doc - d0], w[e]);
+                            // The rest of a run of equal documents, in posting order (rare).
+                            for (long long j = i + 1; j < hi && __ldg(p.docs + j) == doc; ++j) {
+                                a = __fadd_rn(a, __ldg(p.weights + j));
+                            }
+                            acc[doc - d0] = a;
+                        }
+                    }
+                }
+            } else {
+                for (long long i = lo + tid; i < hi; i += kLexThreads) {
+                    const int doc = __ldg(p.docs + i);
+                    if (i > lo && __ldg(p.docs + i - 1) == doc) continue;  // not the head of its run
+                    float a = acc[doc - d0];
+                    a = __fadd_rn(a, __ldg(p.weights + i));
+                    for (long long j = i + 1; j < hi && __ldg(p.docs + j) == doc; ++j) {
+                        a = __fadd_rn(a, __ldg(p.weights + j));
+                    }
+                    acc[doc - d0] = a;
+                }
             }
             __syncthreads();  // slot t's additions land before slot t + 1's
         }
@@ -232,6 +298,10 @@ int launch_lexical(const long long* offsets, const int* docs, const float* weigh
     p.out = out;
     p.part_max = part_max;
     p.sorted = sorted ? 1 : 0;
+    p.vec = (sorted && vocab != INT_MAX && reinterpret_cast<uintptr_t>(docs) % 16 == 0 &&
+             reinterpret_cast<uintptr_t>(weights) % 16 == 0)
+                ? 1
+                : 0;
     const size_t smem = static_cast<size_t>(per) * sizeof(float);
     cudaError_t e = ensure_smem_optin(reinterpret_cast<const void*>(lexical_kernel));
     if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(lexical_kernel)");
