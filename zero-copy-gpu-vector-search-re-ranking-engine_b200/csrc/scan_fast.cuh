@@ -200,7 +200,8 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
                 scount += __popc(ballot);
                 if (scount > kSelCap - 32 || (sthr == 0ull && scount >= k + 32)) {
                     __syncwarp();
-                    warp_sort_buffer(sbuf, scount, lane);
+                    // One fixed-width network inside the polling loop (the loop stays small).
+                    warp_sort_buffer_e<kSelE>(sbuf, scount, lane);
                     if (scount >= k) {
                         sthr = sbuf[k - 1];
                         if (lane == 0) *cta_thr = sthr;

@@ -102,7 +102,7 @@ __device__ __forceinline__ void warp_sort_buffer_e(u64* buf, int n, int lane) {
 // One warp sorts the first n (<= 256) keys of a shared buffer descending, with a network only
 // as wide as n needs (32, 64, 128 or 256 keys): a single warp's sort is a chain of dependent
 // shuffles, so its cost follows the width.
-__device__ __forceinline__ void warp_sort_buffer(u64* buf, int n, int lane) {
+static __device__ __noinline__ void warp_sort_buffer(u64* buf, int n, int lane) {
     if (n <= 32) {
         warp_sort_buffer_e<1>(buf, n, lane);
     } else if (n <= 64) {
