@@ -194,6 +194,18 @@ __global__ void __launch_bounds__(kBucketThreads) bucket_kernel(
 // its bound and none were lost, or on the last pass (then an overflow is recorded in the status
 // word). Otherwise it asks for the next pass with the safe bound (a statistical bound let fewer
 // than k through) or a raised bound (the k-th largest key it captured, after an overflow).
+//
+// Selection by radix: passes over 8-bit digits from the top (the query's candidates re-read
+// each pass, from L1 after the first) find the prefix of the k-th largest key, stopping once
+// the keys sharing the prefix are exactly the ones still needed. Each warp counts digits in its
+// own histogram (one leader lane per group of equal digits adds the group's size: no shared
+// atomics, which serialise when every candidate shares the top digits). The selected keys, k
+// in all (keys are distinct), land at per-warp offsets and are sorted in shared memory. A
+// network over all candidates would cost a compare-exchange per key and stage of a sort k to
+// 16 times wider.
+constexpr int kSelectSort = 1024;  // >= ZCGVS_MAX_K, a power of two
+constexpr int kSelectWarps = kSelectThreads / 32;
+
 __global__ void __launch_bounds__(kSelectThreads) select_kernel(const unsigned long long* __restrict__ cand,
                                                                 unsigned int* cand_count, int cap, int k,
                                                                 unsigned long long* thr_key,
@@ -201,34 +213,137 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(const unsigned l
                                                                 unsigned int* flags, unsigned int* mneed, int mtiles,
                                                                 unsigned int* status, int pass, int* out_idx,
                                                                 float* out_scores) {
-    extern __shared__ __align__(16) u64 keys[];
+    __shared__ u64 keys[kSelectSort];
+    __shared__ unsigned int whist[kSelectWarps][256];
+    __shared__ unsigned int hist[256];
+    __shared__ int s_wbase[kSelectWarps];
     __shared__ int s_count;
     __shared__ u64 s_thr;
+    __shared__ int s_digit, s_above, s_group;
     const int q = blockIdx.x;
     if (pass > 0 && (*reinterpret_cast<const volatile unsigned int*>(flags + pass) == 0u || done[q])) return;
     const bool final = pass == kPasses - 1;
     const unsigned int total = cand_count[q];
     const bool overflow = total > static_cast<unsigned int>(cap) || flags[kPasses + pass] != 0u;
     // Only the entries this pass wrote (the buffer may hold older ones past them).
-    const int n = static_cast<int>(min(total, static_cast<unsigned int>(cap)));
+    const int n = static_cast<int>(min(total, static_cast<unsigned int>(min(cap, kCandCap))));
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const unsigned long long* mine = cand + static_cast<size_t>(q) * cap;  // non-zero keys
+    // Candidate i of a round: every warp runs the same number of rounds (warp-wide shuffles).
+    const int rounds = (n + kSelectThreads - 1) / kSelectThreads;
+    // Prefix (under mask) of the k-th largest key; with n <= k every candidate is kept.
+    u64 prefix = 0ull, mask = 0ull;
+    if (n > k) {
+        int rem = k;
+        for (int shift = 56; shift >= 0; shift -= 8) {
+#pragma unroll
+            for (int j = 0; j < 8; ++j) whist[warp][lane + 32 * j] = 0u;
+            __syncwarp();
+#pragma unroll 4
+            for (int r = 0; r < rounds; ++r) {
+                const int i = r * kSelectThreads + tid;
+                const u64 key = i < n ? __ldg(mine + i) : 0ull;
+                const bool in = key != 0ull && (key & mask) == prefix;
+                const unsigned int digit = in ? static_cast<unsigned int>(key >> shift) & 0xFFu : 0x100u + lane;
+                const unsigned int peers = __match_any_sync(0xffffffffu, digit);
+                if (in && lane == __ffs(peers) - 1) whist[warp][digit] += static_cast<unsigned int>(__popc(peers));
+                __syncwarp();
+            }
+            __syncthreads();
+            if (tid < 256) {
+                unsigned int c = 0u;
+#pragma unroll
+                for (int w = 0; w < kSelectWarps; ++w) c += whist[w][tid];
+                hist[tid] = c;
+            }
+            __syncthreads();
+            if (tid < 32) {
+                // Lane l holds digits 255 - 8 l down to 248 - 8 l; counts above each from a scan.
+                unsigned int c[8];
+                unsigned int sum = 0u;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    c[j] = hist[255 - 8 * lane - j];
+                    sum += c[j];
+                }
+                unsigned int incl = sum;
+#pragma unroll
+                for (int o = 1; o < 32; o <<= 1) {
+                    const unsigned int t = __shfl_up_sync(0xffffffffu, incl, o);
+                    if (lane >= o) incl += t;
+                }
+                unsigned int above = incl - sum;  // keys with a larger digit than this lane's first
+                int found = -1;
+                unsigned int found_above = 0u, found_group = 0u;
+#pragma unroll
+                for (int j = 0; j < 8; ++j) {
+                    if (found < 0 && above + c[j] >= static_cast<unsigned int>(rem)) {
+                        found = 255 - 8 * lane - j;
+                        found_above = above;
+                        found_group = c[j];
+                    }
+                    above += c[j];
+                }
+                const unsigned int hit = __ballot_sync(0xffffffffu, found >= 0);
+                const int src = __ffs(hit) - 1;  // the highest digit reaching rem
+                if (lane == src) {
+                    s_digit = found;
+                    s_above = static_cast<int>(found_above);
+                    s_group = static_cast<int>(found_group);
+                }
+            }
+            __syncthreads();
+            prefix |= static_cast<u64>(s_digit) << shift;
+            mask |= 0xFFull << shift;
+            rem -= s_above;
+            if (s_group == rem) break;  // every key with this prefix is in
+        }
+    }
+    // Gather the selected keys (k of them, or all n) at per-warp offsets and sort them.
+    int wsel = 0;  // this warp's selected keys (the same in every lane)
+#pragma unroll 4
+    for (int r = 0; r < rounds; ++r) {
+        const int i = r * kSelectThreads + tid;
+        const u64 key = i < n ? __ldg(mine + i) : 0ull;
+        wsel += __popc(__ballot_sync(0xffffffffu, key != 0ull && (key & mask) >= prefix));
+    }
+    if (lane == 0) s_wbase[warp] = wsel;
+    __syncthreads();
+    if (tid == 0) {
+        int run = 0;
+        for (int w = 0; w < kSelectWarps; ++w) {
+            const int c = s_wbase[w];
+            s_wbase[w] = run;
+            run += c;
+        }
+        s_count = min(run, kSelectSort);  // min(n, k)
+        s_thr = 0ull;
+    }
+    __syncthreads();
+    int slot = s_wbase[warp];
+#pragma unroll 4
+    for (int r = 0; r < rounds; ++r) {
+        const int i = r * kSelectThreads + tid;
+        const u64 key = i < n ? __ldg(mine + i) : 0ull;
+        const bool take = key != 0ull && (key & mask) >= prefix;
+        const unsigned int ballot = __ballot_sync(0xffffffffu, take);
+        const int at = slot + __popc(ballot & ((1u << lane) - 1u));
+        if (take && at < kSelectSort) keys[at] = key;
+        slot += __popc(ballot);
+    }
+    __syncthreads();
     TopkSmem t;
     t.buf = keys;
     t.count = &s_count;
     t.thr = &s_thr;
-    t.cap = kSelectCap;
+    t.cap = kSelectSort;
     t.k = k;
-    if (threadIdx.x == 0) {
-        s_count = 0;
-        s_thr = 0ull;
-    }
-    __syncthreads();
-    const unsigned long long* mine = cand + static_cast<size_t>(q) * cap;
-    topk_offer_all<4>(t, 0, n, 0ull, [&](int i) { return mine[i]; }, kSelectThreads);
-    topk_flush_mask(t, 1u, kSelectThreads);
-    __syncthreads();
+    topk_flush_mask(t, 1u, kSelectThreads);  // sorts the selected keys; keeps min(count, k)
     const bool short_list = !overflow && n < k && thr_key[q] != thr_safe[q];
     if ((overflow || short_list) && !final) {
-        if (threadIdx.x == 0) {
+        if (tid == 0) {
             if (short_list) {
                 thr_key[q] = thr_safe[q];
             } else if (n >= k) {
@@ -240,9 +355,9 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(const unsigned l
         }
         return;
     }
-    if ((overflow || short_list) && threadIdx.x == 0) atomicOr(status, kStatusOverflow);
+    if ((overflow || short_list) && tid == 0) atomicOr(status, kStatusOverflow);
     topk_write(t, 0, out_idx + static_cast<size_t>(q) * k, out_scores + static_cast<size_t>(q) * k, kSelectThreads);
-    if (threadIdx.x == 0) done[q] = 1;
+    if (tid == 0) done[q] = 1;
 }
 
 PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
@@ -582,7 +697,7 @@ int zcgvs_gemm_topk(const void* corpus, int dtype, const float* row_scales, int6
         if (e != cudaSuccess) return fail_cuda(e, "bucket_kernel launch");
         {
             KernelTimer timer("gemm_select", st);
-            select_kernel<<<batch, kSelectThreads, static_cast<size_t>(kSelectCap) * 8, st>>>(
+            select_kernel<<<batch, kSelectThreads, 0, st>>>(
                 cand, cand_count, kCandCap, k, thr_key, thr_safe, done, retry, mneed, g.mtiles, p.status, pass,
                 out_indices, out_scores);
         }
