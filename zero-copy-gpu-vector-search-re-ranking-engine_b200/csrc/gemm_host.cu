@@ -211,7 +211,7 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(const unsigned l
                                                                 unsigned long long* thr_key,
                                                                 const unsigned long long* thr_safe, int* done,
                                                                 unsigned int* flags, unsigned int* mneed, int mtiles,
-                                                                int mrows, unsigned int* status, int pass, int* out_idx,
+                                                                unsigned int* status, int pass, int* out_idx,
                                                                 float* out_scores) {
     __shared__ u64 keys[kSelectSort];
     __shared__ unsigned int whist[kSelectWarps][256];
@@ -350,7 +350,7 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(const unsigned l
                 thr_key[q] = keys[k - 1];  // k captured documents bound the k-th best
             }
             cand_count[q] = 0u;
-            mneed[(pass + 1) * mtiles + q / mrows] = 1u;
+            mneed[(pass + 1) * mtiles + q / kBM] = 1u;
             atomicOr(flags + pass + 1, 1u);
         }
         return;
@@ -413,12 +413,12 @@ int make_raw_map(CUtensorMap* map, const void* base, long long rows, int row_byt
 
 // The operand maps of a search: queries (prepared in the workspace) and corpus.
 int make_maps(CUtensorMap* mq, CUtensorMap* mx, int mode, int dtype, const void* corpus, long long n, int dim,
-              const void* prepared, int batch, bool pair) {
+              const void* prepared, int batch) {
     const int a_bytes = operand_row_bytes(mode, dtype, dim);
     int status = make_map(mq, prepared, mode, batch, a_bytes, kBM);
     if (status != ZCGVS_OK) return status;
     if (mode == kModeBin) return make_raw_map(mx, corpus, n, static_cast<int>(row_bytes_of(dtype, dim)));
-    return make_map(mx, corpus, mode, n, a_bytes, pair ? kBM : kBN);  // a pair CTA loads half a tile
+    return make_map(mx, corpus, mode, n, a_bytes, kBN);
 }
 
 struct GemmLayout {
@@ -429,8 +429,6 @@ struct GemmLayout {
     size_t off_mb_key = 0, off_mb_query = 0, off_mb_count = 0, total = 0;
     int mb_cap = 0, mb_ctas = 0, expected = 0;
     size_t off_thr_safe = 0, off_mneed = 0;
-    bool pair = false;  // 2-CTA clusters, M = 256 (fp16 / per-row int8 batches of more than 128)
-    int mrows = kBM;    // query rows per item
 };
 
 int plan_gemm(int dtype, long long n, int dim, int batch, int k, GemmLayout& g) {
@@ -451,9 +449,7 @@ int plan_gemm(int dtype, long long n, int dim, int batch, int k, GemmLayout& g) 
                                                std::to_string(g.mode == kModeF16 ? 64 : 128) + " == 0)");
     }
     g.kblocks = row_bytes / kBKBytes;
-    g.pair = g.mode != kModeBin && batch > kBM && device_sm_count() >= 2;
-    g.mrows = g.pair ? 2 * kBM : kBM;
-    g.mtiles = (batch + g.mrows - 1) / g.mrows;
+    g.mtiles = (batch + kBM - 1) / kBM;
     g.ntiles = static_cast<int>((n + kBN - 1) / kBN);
     // Expected candidates per query E; the statistical bound (rank 16) needs a sample of 16 / E
     // of the tiles for about E documents of the corpus to pass it.
@@ -482,9 +478,7 @@ int plan_gemm(int dtype, long long n, int dim, int batch, int k, GemmLayout& g) 
     // document when the sample has fewer than k chunks).
     g.mb_ctas = device_sm_count();
     const long long items = static_cast<long long>(g.mtiles) * g.ntiles;
-    // A pair's CTAs each take every item of the pair (128 of its rows).
-    const long long walkers = g.pair ? g.mb_ctas / 2 : g.mb_ctas;
-    const long long per_cta = (items + walkers - 1) / walkers;
+    const long long per_cta = (items + g.mb_ctas - 1) / g.mb_ctas;
     const double frac = g.sample_tiles * kChunks < k
                             ? 1.0
                             : std::min(1.0, std::max(static_cast<double>(g.expected),
@@ -511,17 +505,13 @@ size_t fixed_smem(int mode, int stages) {
            kEpiWarps * 2 * (kHalf * 4 + 16);
 }
 
-int stage_bytes(bool pair) { return pair ? 2 * kStageA : kStageBytes; }
-
-int stage_count(int mode, bool pair) {
+int stage_count(int mode) {
     const long long budget = device_max_smem() - 2048;
     const long long room = budget - static_cast<long long>(fixed_smem(mode, 8));
-    return static_cast<int>(std::max<long long>(2, std::min<long long>(8, room / stage_bytes(pair))));
+    return static_cast<int>(std::max<long long>(2, std::min<long long>(8, room / kStageBytes)));
 }
 
-size_t gemm_smem(int mode, int stages, bool pair) {
-    return static_cast<size_t>(stages) * stage_bytes(pair) + fixed_smem(mode, stages);
-}
+size_t gemm_smem(int mode, int stages) { return static_cast<size_t>(stages) * kStageBytes + fixed_smem(mode, stages); }
 
 // Vector side-data loads need 16-byte aligned row scales and 4-byte aligned mask bytes.
 int side_vec_ok(const float* row_scales, const uint8_t* mask) {
@@ -531,43 +521,26 @@ int side_vec_ok(const float* row_scales, const uint8_t* mask) {
 using GemmFn = void (*)(const CUtensorMap, const CUtensorMap, const GemmParams);
 
 template <int EPI>
-GemmFn gemm_fn(int mode, bool pair) {
-    if (pair) return mode == kModeI8R ? gemm_scan_kernel<kModeI8R, EPI, true> : gemm_scan_kernel<kModeF16, EPI, true>;
+GemmFn gemm_fn(int mode) {
     switch (mode) {
-        case kModeI8R: return gemm_scan_kernel<kModeI8R, EPI, false>;
-        case kModeBin: return gemm_scan_kernel<kModeBin, EPI, false>;
-        default: return gemm_scan_kernel<kModeF16, EPI, false>;
+        case kModeI8R: return gemm_scan_kernel<kModeI8R, EPI>;
+        case kModeBin: return gemm_scan_kernel<kModeBin, EPI>;
+        default: return gemm_scan_kernel<kModeF16, EPI>;
     }
 }
 
-// One persistent CTA per SM (pairs: one 2-CTA cluster per two SMs), never more than the items.
-int gemm_grid(long long items, bool pair) {
-    const long long sms = device_sm_count();
-    return pair ? static_cast<int>(2 * std::min<long long>(items, sms / 2)) : static_cast<int>(std::min<long long>(items, sms));
-}
-
-int launch_gemm(GemmFn fn, int mode, bool pair, const CUtensorMap& mq, const CUtensorMap& mx, GemmParams p,
+int launch_gemm(GemmFn fn, int mode, const CUtensorMap& mq, const CUtensorMap& mx, GemmParams p,
                 cudaStream_t stream, const char* tag) {
     cudaError_t e = ensure_smem_optin(reinterpret_cast<const void*>(fn));
     if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(gemm_scan_kernel)");
     const long long items = static_cast<long long>(p.mtiles) * p.ntiles;
-    cudaLaunchConfig_t cfg{};
-    cfg.gridDim = dim3(static_cast<unsigned>(gemm_grid(items, pair)));
-    cfg.blockDim = dim3(static_cast<unsigned>(mode == kModeBin ? threads_of<kModeBin>() : kThreads));
-    cfg.dynamicSmemBytes = gemm_smem(mode, p.stages, pair);
-    cfg.stream = stream;
-    cudaLaunchAttribute attr[1];
-    attr[0].id = cudaLaunchAttributeClusterDimension;
-    attr[0].val.clusterDim.x = pair ? 2u : 1u;
-    attr[0].val.clusterDim.y = 1;
-    attr[0].val.clusterDim.z = 1;
-    cfg.attrs = attr;
-    cfg.numAttrs = 1;
+    const int grid = static_cast<int>(std::min<long long>(items, device_sm_count()));
+    const int threads = mode == kModeBin ? threads_of<kModeBin>() : kThreads;
     {
         KernelTimer timer(tag, stream);
-        e = cudaLaunchKernelEx(&cfg, fn, mq, mx, p);
+        fn<<<grid, threads, gemm_smem(mode, p.stages), stream>>>(mq, mx, p);
     }
-    if (e == cudaSuccess) e = cudaGetLastError();
+    e = cudaGetLastError();
     return e == cudaSuccess ? ok() : fail_cuda(e, "gemm_scan_kernel launch");
 }
 
@@ -650,7 +623,7 @@ int zcgvs_gemm_topk(const void* corpus, int dtype, const float* row_scales, int6
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     CUtensorMap mq, mx;
-    status = make_maps(&mq, &mx, g.mode, dtype, corpus, doc_count, dim, ws + g.off_q, batch, g.pair);
+    status = make_maps(&mq, &mx, g.mode, dtype, corpus, doc_count, dim, ws + g.off_q, batch);
     if (status != ZCGVS_OK) return status;
     status = prep(g, queries, batch, dim, ws, st);
     if (status != ZCGVS_OK) return status;
@@ -674,14 +647,14 @@ int zcgvs_gemm_topk(const void* corpus, int dtype, const float* row_scales, int6
     p.mb_count = reinterpret_cast<unsigned int*>(ws + g.off_mb_count);
     p.mb_cap = g.mb_cap;
     p.status = reinterpret_cast<unsigned int*>(ws);
-    p.stages = stage_count(g.mode, g.pair);
+    p.stages = stage_count(g.mode);
     p.side_vec = side_vec_ok(row_scales, mask);
 
     // Threshold pre-pass over the first sample tiles.
     GemmParams ps = p;
     ps.ntiles = g.sample_tiles;
     ps.n = std::min<long long>(doc_count, static_cast<long long>(g.sample_tiles) * kBN);
-    status = launch_gemm(gemm_fn<kTileMax>(g.mode, g.pair), g.mode, g.pair, mq, mx, ps, st, "gemm_sample");
+    status = launch_gemm(gemm_fn<kTileMax>(g.mode), g.mode, mq, mx, ps, st, "gemm_sample");
     if (status != ZCGVS_OK) return status;
     const int chunks = g.sample_tiles * kChunks;
     const int tcap = kSelectCap;
@@ -706,13 +679,12 @@ int zcgvs_gemm_topk(const void* corpus, int dtype, const float* row_scales, int6
     p.ntiles = g.ntiles;
     p.done = done;
     const long long items = static_cast<long long>(p.mtiles) * p.ntiles;
-    const int filter_ctas = gemm_grid(items, g.pair);
+    const int filter_ctas = static_cast<int>(std::min<long long>(items, g.mb_ctas));
     for (int pass = 0; pass < kPasses; ++pass) {
         p.retry = pass == 0 ? nullptr : retry + pass;
         p.mneed = pass == 0 ? nullptr : mneed + static_cast<size_t>(pass) * g.mtiles;
         p.mb_overflow = retry + kPasses + pass;
-        status = launch_gemm(gemm_fn<kFilter>(g.mode, g.pair), g.mode, g.pair, mq, mx, p, st,
-                             pass == 0 ? "gemm_filter" : "gemm_retry");
+        status = launch_gemm(gemm_fn<kFilter>(g.mode), g.mode, mq, mx, p, st, pass == 0 ? "gemm_filter" : "gemm_retry");
         if (status != ZCGVS_OK) return status;
         {
             KernelTimer timer("gemm_bucket", st);
@@ -726,7 +698,7 @@ int zcgvs_gemm_topk(const void* corpus, int dtype, const float* row_scales, int6
         {
             KernelTimer timer("gemm_select", st);
             select_kernel<<<batch, kSelectThreads, 0, st>>>(
-                cand, cand_count, kCandCap, k, thr_key, thr_safe, done, retry, mneed, g.mtiles, g.mrows, p.status, pass,
+                cand, cand_count, kCandCap, k, thr_key, thr_safe, done, retry, mneed, g.mtiles, p.status, pass,
                 out_indices, out_scores);
         }
         e = cudaGetLastError();
@@ -763,7 +735,7 @@ int zcgvs_gemm_similarity(const void* corpus, int dtype, const float* row_scales
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
     CUtensorMap mq, mx;
-    status = make_maps(&mq, &mx, g.mode, dtype, corpus, doc_count, dim, ws + g.off_q, batch, g.pair);
+    status = make_maps(&mq, &mx, g.mode, dtype, corpus, doc_count, dim, ws + g.off_q, batch);
     if (status != ZCGVS_OK) return status;
     status = prep(g, queries, batch, dim, ws, st);
     if (status != ZCGVS_OK) return status;
@@ -779,9 +751,9 @@ int zcgvs_gemm_similarity(const void* corpus, int dtype, const float* row_scales
     p.mask = mask;
     p.out_matrix = scores;
     p.status = reinterpret_cast<unsigned int*>(ws);
-    p.stages = stage_count(g.mode, g.pair);
+    p.stages = stage_count(g.mode);
     p.side_vec = side_vec_ok(row_scales, mask);
-    return launch_gemm(gemm_fn<kEmit>(g.mode, g.pair), g.mode, g.pair, mq, mx, p, st, "gemm_emit");
+    return launch_gemm(gemm_fn<kEmit>(g.mode), g.mode, mq, mx, p, st, "gemm_emit");
 }
 
 }  // extern "C"

@@ -148,63 +148,6 @@ __device__ __forceinline__ void mma_commit(u64* bar) {
                  : "memory");
 }
 
-// ---- CTA pairs (cta_group::2): one MMA over two SMs, M = 256 ----
-// The pair is a 2-CTA cluster. The even CTA (rank 0) issues every MMA; each CTA holds its own
-// 128 query rows (A) and half of the document tile (B) at the same shared-memory offsets, and
-// its 128 accumulator rows in its own tensor memory.
-__device__ __forceinline__ uint32_t cluster_rank() {
-    uint32_t r;
-    asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
-    return r;
-}
-
-// Shared-memory address of the same variable in CTA `rank` of the cluster.
-__device__ __forceinline__ uint32_t cluster_addr(const void* p, uint32_t rank) {
-    uint32_t r;
-    asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(smem_u32(p)), "r"(rank));
-    return r;
-}
-
-__device__ __forceinline__ void mbar_arrive_cluster(uint32_t addr) {
-    asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr) : "memory");
-}
-
-__device__ __forceinline__ void cluster_sync_all() {
-    asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
-}
-
-// Commit of the pair's MMAs issued so far, arriving on the barrier at `addr` (either CTA).
-__device__ __forceinline__ void mma_commit_pair(uint32_t addr) {
-    asm volatile("tcgen05.commit.cta_group::2.mbarrier::arrive::one.shared::cluster.b64 [%0];" ::"r"(addr)
-                 : "memory");
-}
-
-template <int MODE>
-__device__ __forceinline__ void mma_issue_pair(uint32_t tmem_d, uint64_t a_desc, uint64_t b_desc, uint32_t accumulate) {
-    constexpr uint32_t idesc = instr_desc<MODE>() + (static_cast<uint32_t>(kBM >> 4) << 24);  // M = 256
-    if constexpr (int8_operands<MODE>()) {
-        asm volatile(
-            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-            "tcgen05.mma.cta_group::2.kind::i8 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
-            "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
-    } else {
-        asm volatile(
-            "{\n\t.reg .pred p;\n\tsetp.ne.b32 p, %4, 0;\n\t"
-            "tcgen05.mma.cta_group::2.kind::f16 [%0], %1, %2, %3, p;\n\t}\n" ::"r"(tmem_d),
-            "l"(a_desc), "l"(b_desc), "r"(idesc), "r"(accumulate));
-    }
-}
-
-// 2-D TMA load into this CTA's shared memory whose completion is counted on the barrier at
-// `bar` (a cluster address: the pair leader's barrier). No multicast.
-__device__ __forceinline__ void tma_load_2d_pair(void* smem_dst, const CUtensorMap* map, int x, int y, uint32_t bar) {
-    asm volatile(
-        "cp.async.bulk.tensor.2d.cta_group::2.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
-        "[%4];" ::"r"(smem_u32(smem_dst)),
-        "l"(reinterpret_cast<uint64_t>(map)), "r"(x), "r"(y), "r"(bar)
-        : "memory");
-}
-
 __device__ __forceinline__ void tc_fence_before() { asm volatile("tcgen05.fence::before_thread_sync;" ::: "memory"); }
 __device__ __forceinline__ void tc_fence_after() { asm volatile("tcgen05.fence::after_thread_sync;" ::: "memory"); }
 
@@ -321,24 +264,16 @@ __device__ __forceinline__ long long walk_first(const GemmParams& p, long long i
     return (w < items && item_skipped(p, w)) ? walk_next(p, w, items) : w;
 }
 
-// PAIR: a 2-CTA cluster runs each item as one M = 256 MMA (cta_group::2): items are (256-query
-// block, 256-document tile), CTA rank r holds queries 128 r .. 128 r + 127 and documents
-// 128 r .. 128 r + 127 of the tile, stages are 32 KB, and the rank-0 CTA's MMA thread issues
-// every MMA and commits to the barriers of both CTAs. Per SM this halves the document operand
-// each stage moves through shared memory and L2 for the same multiply-adds.
-template <int MODE, int EPI, bool PAIR>
+template <int MODE, int EPI>
 __global__ void __launch_bounds__(threads_of<MODE>(), 1)
     gemm_scan_kernel(const __grid_constant__ CUtensorMap map_q, const __grid_constant__ CUtensorMap map_x,
                      const GemmParams p) {
-    static_assert(!PAIR || MODE != kModeBin, "1-bit corpora run on single CTAs");
     extern __shared__ __align__(1024) uint8_t smem_raw[];
     // Stage ring first, 1024-aligned (the swizzle pattern and base offset 0 assume it).
     uint8_t* smem = smem_raw + ((1024u - (smem_u32(smem_raw) & 1023u)) & 1023u);
-    constexpr int kStage = PAIR ? 2 * kStageA : kStageBytes;  // bytes per stage
-    constexpr int kRowsM = PAIR ? 2 * kBM : kBM;              // query rows per item
     const int S = p.stages;
     constexpr int R = MODE == kModeBin ? kRawSlots : 0;
-    uint8_t* raw = smem + static_cast<size_t>(S) * kStage;  // 1-bit: [R][kBN][128] packed, swizzled
+    uint8_t* raw = smem + static_cast<size_t>(S) * kStageBytes;  // 1-bit: [R][kBN][128] packed, swizzled
     u64* full = reinterpret_cast<u64*>(raw + static_cast<size_t>(R) * kRawBytes);
     u64* empty = full + S;
     u64* acc_full = empty + S;        // [2]
@@ -358,9 +293,6 @@ __global__ void __launch_bounds__(threads_of<MODE>(), 1)
     // A retry pass with nothing to retry returns before allocating anything.
     if (EPI == kFilter && p.retry != nullptr && *reinterpret_cast<const volatile unsigned int*>(p.retry) == 0u) return;
     const long long items = static_cast<long long>(p.mtiles) * p.ntiles;
-    const uint32_t rank = PAIR ? cluster_rank() : 0u;
-    const long long wstart = PAIR ? blockIdx.x / 2 : blockIdx.x;   // this CTA's (pair's) first item
-    const long long wstride = PAIR ? gridDim.x / 2 : gridDim.x;
 
     if (tid == 0) {
         for (int s = 0; s < S; ++s) {
@@ -371,31 +303,20 @@ __global__ void __launch_bounds__(threads_of<MODE>(), 1)
         for (int r = 0; r < R; ++r) mbar_init(&raw_full[r], 1);
         for (int a = 0; a < 2; ++a) {
             mbar_init(&acc_full[a], 1);
-            mbar_init(&acc_empty[a], PAIR ? 2 * kEpiWarps : kEpiWarps);  // both CTAs' epilogues
+            mbar_init(&acc_empty[a], kEpiWarps);
         }
         mbar_init(drain, 1);
         fence_mbarrier_init();
         s_abort = 0;
     }
     if (warp == kMmaWarp) {
-        if constexpr (PAIR) {
-            asm volatile("tcgen05.alloc.cta_group::2.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
-                         "r"(kTmemCols)
-                         : "memory");
-            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::2.sync.aligned;" ::: "memory");
-        } else {
-            asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
-                         "r"(kTmemCols)
-                         : "memory");
-            asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
-        }
+        asm volatile("tcgen05.alloc.cta_group::1.sync.aligned.shared::cta.b32 [%0], %1;" ::"r"(smem_u32(&s_tmem)),
+                     "r"(kTmemCols)
+                     : "memory");
+        asm volatile("tcgen05.relinquish_alloc_permit.cta_group::1.sync.aligned;" ::: "memory");
     }
     tc_fence_before();
-    if constexpr (PAIR) {
-        cluster_sync_all();  // both CTAs' barriers are initialised before either uses the other's
-    } else {
-        __syncthreads();
-    }
+    __syncthreads();
     tc_fence_after();
     const uint32_t tmem_base = s_tmem;
     volatile int* abort_flag = &s_abort;
@@ -406,7 +327,7 @@ __global__ void __launch_bounds__(threads_of<MODE>(), 1)
             uint32_t phase = 0;
             long long issued = 0;
             bool ok = true;
-            for (long long w = wstart; w < items && ok; w += wstride) {
+            for (long long w = blockIdx.x; w < items && ok; w += gridDim.x) {
                 if (item_skipped(p, w)) continue;
                 const int m = static_cast<int>(w % p.mtiles);
                 const int n = static_cast<int>(w / p.mtiles);
@@ -418,15 +339,9 @@ __global__ void __launch_bounds__(threads_of<MODE>(), 1)
                             break;
                         }
                     }
-                    uint8_t* st = smem + static_cast<size_t>(s) * kStage;
+                    uint8_t* st = smem + static_cast<size_t>(s) * kStageBytes;
                     constexpr int kElems = int8_operands<MODE>() ? kBKBytes : kBKBytes / 2;
-                    if constexpr (PAIR) {
-                        // Both CTAs' copies complete on the leader's barrier, which expects them all.
-                        const uint32_t bar = cluster_addr(&full[s], 0);
-                        if (rank == 0) mbar_arrive_expect_tx(&full[s], 2 * kStage);
-                        tma_load_2d_pair(st, &map_q, kb * kElems, m * kRowsM + static_cast<int>(rank) * kBM, bar);
-                        tma_load_2d_pair(st + kStageA, &map_x, kb * kElems, n * kBN + static_cast<int>(rank) * kBM, bar);
-                    } else if constexpr (MODE == kModeBin) {
+                    if constexpr (MODE == kModeBin) {
                         // The expander warps write the document half of the stage.
                         mbar_arrive_expect_tx(&full[s], kStageA);
                         tma_load_2d(st, &map_q, kb * kElems, m * kBM, &full[s]);
@@ -442,22 +357,20 @@ __global__ void __launch_bounds__(threads_of<MODE>(), 1)
                     }
                 }
             }
-            // Wait (bounded) for the copies still in flight before the CTA can retire. A pair's
-            // copies complete on the leader's barriers: the leader drains them, and the cluster
-            // barrier at the end holds the other CTA until then.
-            if (*abort_flag && rank == 0) {
+            // Wait (bounded) for the copies still in flight before the CTA can retire.
+            if (*abort_flag) {
                 for (long long i = issued > S ? issued - S : 0; i < issued; ++i) {
                     mbar_wait_bounded(&full[i % S], static_cast<uint32_t>((i / S) & 1), p.status, kStatusDrainTimeout);
                 }
             }
         }
     } else if (warp == kMmaWarp) {
-        if (lane == 0 && rank == 0) {
+        if (lane == 0) {
             int s = 0;
             uint32_t phase = 0;
             long long local = 0;
             bool ok = true;
-            for (long long w = wstart; w < items && ok; w += wstride) {
+            for (long long w = blockIdx.x; w < items && ok; w += gridDim.x) {
                 if (item_skipped(p, w)) continue;
                 const int a = static_cast<int>(local & 1);
                 if (local >= 2) {
@@ -478,7 +391,7 @@ __global__ void __launch_bounds__(threads_of<MODE>(), 1)
                         break;
                     }
                     tc_fence_after();
-                    const uint32_t a_addr = smem_u32(smem + static_cast<size_t>(s) * kStage);
+                    const uint32_t a_addr = smem_u32(smem + static_cast<size_t>(s) * kStageBytes);
                     const uint32_t b_addr = a_addr + kStageA;
                     const uint64_t a_desc = smem_desc_sw128(a_addr);
                     const uint64_t b_desc = smem_desc_sw128(b_addr);
@@ -486,42 +399,21 @@ __global__ void __launch_bounds__(threads_of<MODE>(), 1)
                     for (int kk = 0; kk < kBKBytes / 32; ++kk) {
                         // Each MMA consumes 32 bytes of K (16 fp16 or 32 int8): advance both start
                         // addresses by 32 bytes (2 units of 16 B) inside the swizzled row.
-                        if constexpr (PAIR) {
-                            mma_issue_pair<MODE>(tmem_d, a_desc + static_cast<uint64_t>(2 * kk),
-                                                 b_desc + static_cast<uint64_t>(2 * kk), (kb > 0 || kk > 0) ? 1u : 0u);
-                        } else {
-                            mma_issue<MODE>(tmem_d, a_desc + static_cast<uint64_t>(2 * kk),
-                                            b_desc + static_cast<uint64_t>(2 * kk), (kb > 0 || kk > 0) ? 1u : 0u);
-                        }
+                        mma_issue<MODE>(tmem_d, a_desc + static_cast<uint64_t>(2 * kk),
+                                        b_desc + static_cast<uint64_t>(2 * kk), (kb > 0 || kk > 0) ? 1u : 0u);
                     }
-                    // Frees the stage (in both CTAs of a pair) when these MMAs have read it.
-                    if constexpr (PAIR) {
-                        mma_commit_pair(cluster_addr(&empty[s], 0));
-                        mma_commit_pair(cluster_addr(&empty[s], 1));
-                    } else {
-                        mma_commit(&empty[s]);
-                    }
+                    mma_commit(&empty[s]);  // frees the stage when these MMAs have read it
                     if (++s == S) {
                         s = 0;
                         phase ^= 1u;
                     }
                 }
                 if (!ok) break;
-                // Accumulator a is complete (in both CTAs of a pair).
-                if constexpr (PAIR) {
-                    mma_commit_pair(cluster_addr(&acc_full[a], 0));
-                    mma_commit_pair(cluster_addr(&acc_full[a], 1));
-                } else {
-                    mma_commit(&acc_full[a]);
-                }
+                mma_commit(&acc_full[a]);  // accumulator a is complete
                 ++local;
             }
             // Make sure no MMA is in flight before the tensor memory is released.
-            if constexpr (PAIR) {
-                mma_commit_pair(cluster_addr(drain, 0));
-            } else {
-                mma_commit(drain);
-            }
+            mma_commit(drain);
             mbar_wait_bounded(drain, 0u, p.status, kStatusDrainTimeout);
         }
     } else if (warp >= kFirstExpWarp) {
@@ -636,7 +528,7 @@ __global__ void __launch_bounds__(threads_of<MODE>(), 1)
         // ahead so the latency overlaps the previous item's epilogue.
         auto next_item = [&](long long w) {
             do {
-                w += wstride;
+                w += gridDim.x;
             } while (w < items && item_skipped(p, w));
             return w;
         };
@@ -661,7 +553,7 @@ __global__ void __launch_bounds__(threads_of<MODE>(), 1)
                 sv = make_float4(t[0], t[1], t[2], t[3]);
             }
         };
-        long long w = wstart;
+        long long w = blockIdx.x;
         if (w < items && item_skipped(p, w)) w = next_item(w);
         float4 sv;
         uint32_t mv;
@@ -670,7 +562,7 @@ __global__ void __launch_bounds__(threads_of<MODE>(), 1)
             const int m = static_cast<int>(w % p.mtiles);
             const int n = static_cast<int>(w / p.mtiles);
             const int a = static_cast<int>(local & 1);
-            const int q = m * kRowsM + static_cast<int>(rank) * kBM + row;
+            const int q = m * kBM + row;
             const bool q_ok = q < p.batch;
             const long long doc0 = static_cast<long long>(n) * kBN + half * kHalf;  // this warp's first column
             // This warp's copy of the side data (the epilogue warps never wait on one another):
@@ -767,30 +659,58 @@ __global__ void __launch_bounds__(threads_of<MODE>(), 1)
                     float best = -INFINITY;
                     if constexpr (MODE == kModeBin) {
                         int dbest = INT_MIN;
+                        if (valid == 0xffffffffu) {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) dbest = max(dbest, ((valid >> j) & 1u) ? dv[j] : INT_MIN);
+                            for (int j = 0; j < 32; ++j) dbest = max(dbest, dv[j]);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) dbest = max(dbest, ((valid >> j) & 1u) ? dv[j] : INT_MIN);
+                        }
                         if (dbest != INT_MIN) best = bin_score(dbest, dimf);
                     } else {
+                        // fmaxf ignores the NaN scores of invalid per-row int8 documents.
+                        if (valid == 0xffffffffu) {
 #pragma unroll
-                        for (int j = 0; j < 32; ++j) best = fmaxf(best, ((valid >> j) & 1u) ? sc[j] : -INFINITY);
+                            for (int j = 0; j < 32; ++j) best = fmaxf(best, sc[j]);
+                        } else {
+#pragma unroll
+                            for (int j = 0; j < 32; ++j) best = fmaxf(best, ((valid >> j) & 1u) ? sc[j] : -INFINITY);
+                        }
                     }
                     if (q_ok) p.chunk_max[(static_cast<size_t>(q) * p.ntiles + n) * kChunks + half * 4 + cl] = best;
                 } else {
                     // Candidates go to this warp's own mailbox segment at a register counter:
-                    // the epilogue issues no atomics and never waits on a store.
-                    uint32_t pass = 0u, ties = 0u;
+                    // the epilogue issues no atomics and never waits on a store. Most chunks
+                    // hold none: a max over the lane's 32 scores (one operation each) decides
+                    // whether the per-score masks are built at all.
+                    bool maybe;
+                    if constexpr (MODE == kModeBin) {
+                        int dmax = dv[0];
 #pragma unroll
-                    for (int j = 0; j < 32; ++j) {
-                        if constexpr (MODE == kModeBin) {
-                            pass |= (dv[j] >= d_gt ? 1u : 0u) << j;
-                            ties |= (dv[j] == d_eq ? 1u : 0u) << j;
-                        } else {
-                            pass |= (sc[j] > thr ? 1u : 0u) << j;
-                            ties |= (sc[j] == thr ? 1u : 0u) << j;
-                        }
+                        for (int j = 1; j < 32; ++j) dmax = max(dmax, dv[j]);
+                        maybe = live && (dmax >= d_gt || dmax >= d_eq);
+                    } else {
+                        float fmax = sc[0];
+#pragma unroll
+                        for (int j = 1; j < 32; ++j) fmax = fmaxf(fmax, sc[j]);  // NaN (invalid) ignored
+                        maybe = live && fmax >= thr;
                     }
-                    pass = live ? (pass & valid) : 0u;
-                    ties = live ? (ties & valid) : 0u;
+                    if (__ballot_sync(0xffffffffu, maybe) == 0u) continue;
+                    uint32_t pass = 0u, ties = 0u;
+                    if (maybe) {
+#pragma unroll
+                        for (int j = 0; j < 32; ++j) {
+                            if constexpr (MODE == kModeBin) {
+                                pass |= (dv[j] >= d_gt ? 1u : 0u) << j;
+                                ties |= (dv[j] == d_eq ? 1u : 0u) << j;
+                            } else {
+                                pass |= (sc[j] > thr ? 1u : 0u) << j;
+                                ties |= (sc[j] == thr ? 1u : 0u) << j;
+                            }
+                        }
+                        pass &= valid;
+                        ties &= valid;
+                    }
                     // A score equal to the threshold's passes only if its key (ties by id) does.
                     while (ties != 0u) {
                         const int j = __ffs(ties) - 1;
@@ -844,13 +764,7 @@ __global__ void __launch_bounds__(threads_of<MODE>(), 1)
             }
             tc_fence_before();
             __syncwarp();
-            if (lane == 0) {
-                if constexpr (PAIR) {
-                    mbar_arrive_cluster(cluster_addr(&acc_empty[a], 0));  // the MMAs run from rank 0
-                } else {
-                    mbar_arrive_cta(&acc_empty[a]);
-                }
-            }
+            if (lane == 0) mbar_arrive_cta(&acc_empty[a]);
             ++local;
             w = w_next;
         }
@@ -863,22 +777,13 @@ __global__ void __launch_bounds__(threads_of<MODE>(), 1)
     }
 
     tc_fence_before();
-    if constexpr (PAIR) {
-        cluster_sync_all();  // the leader's MMAs (which write both CTAs' tensor memory) are drained
-    } else {
-        __syncthreads();
-    }
+    __syncthreads();
     tc_fence_after();
 
     if (warp == kMmaWarp) {
         __syncwarp();
-        if constexpr (PAIR) {
-            asm volatile("tcgen05.dealloc.cta_group::2.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
-                         : "memory");
-        } else {
-            asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
-                         : "memory");
-        }
+        asm volatile("tcgen05.dealloc.cta_group::1.sync.aligned.b32 %0, %1;" ::"r"(tmem_base), "r"(kTmemCols)
+                     : "memory");
     }
 }
 
