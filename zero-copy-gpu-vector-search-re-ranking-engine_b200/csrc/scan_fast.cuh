@@ -60,6 +60,7 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
     __shared__ int s_done;
     __shared__ int s_last;
     __shared__ int s_merge_count;
+    __shared__ int s_sel_count;
     __shared__ int s_sel_complete;
     __shared__ int s_wcount[kFastConsumers];
 
@@ -216,11 +217,9 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
             __nanosleep(128);
             if ((spin & 63u) == 0u && global_timer_ns() - start > kWaitBudgetNs) break;
         }
-        // Keep the selector's state for the end of the kernel: sort it once more so sbuf holds
-        // the exact top of every key it saw.
-        __syncwarp();
-        warp_sort_buffer(sbuf, scount, lane);
-        if (lane == 0) s_merge_count = min(scount, k);
+        // sbuf[0, scount) holds the best keys the selector saw (its top k among them, unsorted):
+        // the whole CTA ranks them once the scan is over.
+        if (lane == 0) s_sel_count = scount;
     } else {
         // ---------------- consumer warps ----------------
         const int grp = lane / LPR;
@@ -343,9 +342,15 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
     bool spilled = false;
     for (int w = 0; w < kFastConsumers; ++w) spilled |= s_wcount[w] > kRegionCap;
     if (!spilled && s_sel_complete) {
+        // Its keys are distinct: each one's rank among them is its place in the sorted list.
         unsigned long long* dst = p.lists + (static_cast<size_t>(pass) * G + cta) * k;
-        const int n = s_merge_count;
-        for (int j = tid; j < k; j += kFastThreads) dst[j] = j < n ? sbuf[j] : 0ull;
+        const int n = s_sel_count;
+        for (int i = tid; i < n; i += kFastThreads) {
+            const u64 key = sbuf[i];
+            const int r = key_rank(sbuf, n, key);
+            if (r < k) dst[r] = key;
+        }
+        for (int j = min(n, k) + tid; j < k; j += kFastThreads) dst[j] = 0ull;
     } else {
     // Otherwise select this CTA's top-k from every candidate at or above the selector's
     // threshold: the shared regions first, then any spill.

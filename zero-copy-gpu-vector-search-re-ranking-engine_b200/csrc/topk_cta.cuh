@@ -293,9 +293,91 @@ __device__ inline bool topk_merge_lists_small(const TopkSmem& t, int q_local, co
     return true;
 }
 
+// How many of the n distinct keys in keys[] are larger than key (its rank, 0 = largest). All
+// lanes of a warp read the same entry at once (a broadcast).
+__device__ __forceinline__ int key_rank(const u64* keys, int n, u64 key) {
+    int r = 0;
+#pragma unroll 4
+    for (int j = 0; j < n; ++j) r += keys[j] > key ? 1 : 0;
+    return r;
+}
+
+// Lists at least as many as k: the floor F is the k-th largest list head (found by counting
+// ranks, one head per thread), so exactly k lists hold keys >= F and only their prefixes >= F
+// are read (a warp per list, 32 keys per step); the kept keys are placed by counting ranks
+// instead of sorting. A CTA-wide bitonic network costs a barrier per stage, and its input would
+// be every key of the lists. Falls back (returns false) when the candidates outgrow kMergeCand.
+constexpr int kMergeCand = 2048;
+
+__device__ inline bool topk_merge_lists_rank(const TopkSmem& t, int q_local, const u64* src, int lists,
+                                             int nthreads, u64* s_scratch) {
+    const int k = t.k;
+    const int lists_pad = (lists + 31) & ~31;
+    if (lists < k || lists > nthreads || kMergeCand + lists_pad + k > t.cap) return false;
+    const int tid = threadIdx.x;
+    const int lane = tid & 31;
+    const int warp = tid >> 5;
+    const int nwarps = nthreads >> 5;
+    u64* cand = t.buf + q_local * t.cap;  // [kMergeCand] keys >= F
+    u64* heads = cand + kMergeCand;       // [lists]
+    u64* kept = heads + lists_pad;        // [k] the result, before it moves to the front
+    if (tid < lists) heads[tid] = __ldcg(src + static_cast<size_t>(tid) * k);
+    if (tid == 0) {
+        s_scratch[0] = 1ull;  // F when fewer than k lists are non-empty: every non-empty key
+        t.count[q_local] = 0;
+    }
+    __syncthreads();
+    if (tid < lists) {
+        const u64 h = heads[tid];
+        if (h != 0ull && key_rank(heads, lists, h) == k - 1) s_scratch[0] = h;
+    }
+    __syncthreads();
+    const u64 floor_key = s_scratch[0];
+    // Keys >= F: a prefix of each list whose head is >= F.
+    bool overflow = false;
+    for (int l = warp; l < lists; l += nwarps) {
+        if (heads[l] < floor_key) continue;
+        for (int off = 0; off < k; off += 32) {
+            const u64 key = off + lane < k ? __ldcg(src + static_cast<size_t>(l) * k + off + lane) : 0ull;
+            const bool take = key >= floor_key;
+            const uint32_t ballot = __ballot_sync(0xffffffffu, take);
+            int slot = 0;
+            if (lane == 0) slot = atomicAdd(&t.count[q_local], __popc(ballot));
+            slot = __shfl_sync(0xffffffffu, slot, 0) + __popc(ballot & ((1u << lane) - 1u));
+            if (take) {
+                if (slot < kMergeCand) {
+                    cand[slot] = key;
+                } else {
+                    overflow = true;
+                }
+            }
+            if (ballot != 0xffffffffu) break;  // the prefix ended
+        }
+    }
+    if (__syncthreads_or(overflow ? 1 : 0)) return false;
+    const int n = t.count[q_local];
+    // Exact top k by rank (keys are distinct), then to the front of the buffer.
+    for (int i = tid; i < n; i += nthreads) {
+        const u64 key = cand[i];
+        const int r = key_rank(cand, n, key);
+        if (r < k) kept[r] = key;
+    }
+    __syncthreads();
+    const int got = min(n, k);
+    for (int j = tid; j < got; j += nthreads) t.buf[q_local * t.cap + j] = kept[j];
+    __syncthreads();
+    if (tid == 0) {
+        t.count[q_local] = got;
+        t.thr[q_local] = n >= k ? t.buf[q_local * t.cap + k - 1] : 0ull;
+    }
+    __syncthreads();
+    return true;
+}
+
 __device__ inline void topk_merge_lists(const TopkSmem& t, int q_local, const u64* src, int lists,
                                         int nthreads, u64* s_scratch /* >= 32 entries */) {
     if (topk_merge_lists_small(t, q_local, src, lists, nthreads, s_scratch)) return;
+    if (topk_merge_lists_rank(t, q_local, src, lists, nthreads, s_scratch)) return;
     const int tid = threadIdx.x;
     const int k = t.k;
     const int j = (k + lists - 1) / lists - 1;
