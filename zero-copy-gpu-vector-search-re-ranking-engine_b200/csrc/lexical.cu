@@ -36,7 +36,7 @@ namespace zc {
 
 namespace {
 
-constexpr int kLexThreads = 256;
+constexpr int kLexThreads = 512;
 constexpr int kLexWarps = kLexThreads / 32;
 constexpr int kLexSlots = 128;          // term slots searched per round
 constexpr int kLexMaxDocsPerCta = 32768;  // 128 KB accumulator
@@ -146,69 +146,115 @@ __global__ void __launch_bounds__(kLexThreads) lexical_kernel(const LexParams p)
             __syncthreads();
             continue;
         }
-        for (int t = 0; t < slots; ++t) {
-            const long long lo = s_lo[t];
-            const long long hi = s_hi[t];
-            if (p.vec) {
-                // Thread tid of a round owns the 4 postings of 16-byte group g = g0 + tid (two
-                // groups per round, loaded before either is used); a posting is the head of its
-                // run unless the posting before it (the same thread's, the previous lane's last
-                // one, or for lane 0 a load) holds the same document.
-                const long long g_lo = lo >> 2;
-                const long long g_hi = (hi + 3) >> 2;
-                for (long long g0 = g_lo; g0 < g_hi; g0 += 2 * kLexThreads) {
-                    int4 dv[2];
-                    float4 wv[2];
-                    int before[2];
+        if (p.vec) {
+            // 16-byte posting groups, software-pipelined across slots. A step is two groups per
+            // thread of one slot (thread tid owns groups g0 + tid and g0 + kLexThreads + tid);
+            // the next step's loads are issued before this step's additions and before the
+            // barrier that closes a slot (loads never touch the accumulator), so a slot's memory
+            // latency overlaps the previous slot's work. Slots without postings here are skipped.
+            // A posting is the head of its run unless the posting before it (the same thread's,
+            // the previous lane's last one, or for lane 0 a load) holds the same document.
+            struct Step {
+                int t;
+                long long g0;
+            };
+            auto g_lo = [&](int t) { return s_lo[t] >> 2; };
+            auto g_hi = [&](int t) { return (s_hi[t] + 3) >> 2; };
+            auto first_from = [&](int t) {
+                while (t < slots && g_lo(t) >= g_hi(t)) ++t;
+                return Step{t, t < slots ? g_lo(t) : 0};
+            };
+            auto advance = [&](Step c) {
+                const long long g0 = c.g0 + 2 * kLexThreads;
+                return g0 < g_hi(c.t) ? Step{c.t, g0} : first_from(c.t + 1);
+            };
+            auto load = [&](Step c, int4 (&dv)[2], float4 (&wv)[2], int (&before)[2]) {
 #pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        const long long g = g0 + u * kLexThreads + tid;
-                        if (g < g_hi && 4 * g + 3 < total) {
-                            dv[u] = __ldg(reinterpret_cast<const int4*>(p.docs) + g);
-                            wv[u] = __ldg(reinterpret_cast<const float4*>(p.weights) + g);
-                        } else {
-                            // Past the slice, or the index's last partial group: element loads.
-                            int dd[4] = {-1, -1, -1, -1};
-                            float ww[4] = {0.f, 0.f, 0.f, 0.f};
-                            if (g < g_hi) {
+                for (int u = 0; u < 2; ++u) {
+                    dv[u] = make_int4(-1, -1, -1, -1);
+                    wv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
+                    before[u] = -1;
+                }
+                if (c.t >= slots) return;
+                const long long lo = s_lo[c.t];
+                const long long ghi = g_hi(c.t);
 #pragma unroll
-                                for (int e = 0; e < 4; ++e) {
-                                    if (4 * g + e < total) {
-                                        dd[e] = __ldg(p.docs + 4 * g + e);
-                                        ww[e] = __ldg(p.weights + 4 * g + e);
-                                    }
-                                }
-                            }
-                            dv[u] = make_int4(dd[0], dd[1], dd[2], dd[3]);
-                            wv[u] = make_float4(ww[0], ww[1], ww[2], ww[3]);
-                        }
-                        before[u] = (lane == 0 && g < g_hi && 4 * g > lo) ? __ldg(p.docs + 4 * g - 1) : -1;
-                    }
-#pragma unroll
-                    for (int u = 0; u < 2; ++u) {
-                        const long long g = g0 + u * kLexThreads + tid;
-                        const int up = __shfl_up_sync(0xffffffffu, dv[u].w, 1);
-                        if (g >= g_hi) continue;
-                        const int d[4] = {dv[u].x, dv[u].y, dv[u].z, dv[u].w};
-                        const float w[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
-                        int prev = lane == 0 ? before[u] : up;
+                for (int u = 0; u < 2; ++u) {
+                    const long long g = c.g0 + u * kLexThreads + tid;
+                    if (g >= ghi) continue;
+                    if (4 * g + 3 < total) {
+                        dv[u] = __ldg(reinterpret_cast<const int4*>(p.docs) + g);
+                        wv[u] = __ldg(reinterpret_cast<const float4*>(p.weights) + g);
+                    } else {
+                        // The index's last partial group: element loads.
+                        int dd[4] = {-1, -1, -1, -1};
+                        float ww[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
-                            const long long i = 4 * g + e;
-                            const int doc = d[e];
-                            const bool head = i >= lo && i < hi && (i == lo || prev != doc);
-                            prev = doc;
-                            if (!head) continue;
-                            float a = __fadd_rn(acc[doc - d0], w[e]);
-                            // The rest of a run of equal documents, in posting order (rare).
-                            for (long long j = i + 1; j < hi && __ldg(p.docs + j) == doc; ++j) {
-                                a = __fadd_rn(a, __ldg(p.weights + j));
+                            if (4 * g + e < total) {
+                                dd[e] = __ldg(p.docs + 4 * g + e);
+                                ww[e] = __ldg(p.weights + 4 * g + e);
                             }
-                            acc[doc - d0] = a;
                         }
+                        dv[u] = make_int4(dd[0], dd[1], dd[2], dd[3]);
+                        wv[u] = make_float4(ww[0], ww[1], ww[2], ww[3]);
+                    }
+                    if (lane == 0 && 4 * g > lo) before[u] = __ldg(p.docs + 4 * g - 1);
+                }
+            };
+            auto process = [&](Step c, const int4 (&dv)[2], const float4 (&wv)[2], const int (&before)[2]) {
+                const long long lo = s_lo[c.t];
+                const long long hi = s_hi[c.t];
+                const long long ghi = g_hi(c.t);
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    const long long g = c.g0 + u * kLexThreads + tid;
+                    const int up = __shfl_up_sync(0xffffffffu, dv[u].w, 1);
+                    if (g >= ghi) continue;
+                    const int d[4] = {dv[u].x, dv[u].y, dv[u].z, dv[u].w};
+                    const float w[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
+                    int prev = lane == 0 ? before[u] : up;
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const long long i = 4 * g + e;
+                        const int doc = d[e];
+                        const bool head = i >= lo && i < hi && (i == lo || prev != doc);
+                        prev = doc;
+                        if (!head) continue;
+                        float a = __fadd_rn(acc[doc - d0], w[e]);
+                        // The rest of a run of equal documents, in posting order (rare).
+                        for (long long j = i + 1; j < hi && __ldg(p.docs + j) == doc; ++j) {
+                            a = __fadd_rn(a, __ldg(p.weights + j));
+                        }
+                        acc[doc - d0] = a;
                     }
                 }
-            } else {
+            };
+            Step cur = first_from(0);
+            int4 dv[2];
+            float4 wv[2];
+            int before[2];
+            load(cur, dv, wv, before);
+            while (cur.t < slots) {
+                const Step nxt = advance(cur);
+                int4 ndv[2];
+                float4 nwv[2];
+                int nbefore[2];
+                load(nxt, ndv, nwv, nbefore);
+                process(cur, dv, wv, before);
+                if (nxt.t != cur.t) __syncthreads();  // slot cur.t's additions land before the next slot's
+                cur = nxt;
+#pragma unroll
+                for (int u = 0; u < 2; ++u) {
+                    dv[u] = ndv[u];
+                    wv[u] = nwv[u];
+                    before[u] = nbefore[u];
+                }
+            }
+        } else {
+            for (int t = 0; t < slots; ++t) {
+                const long long lo = s_lo[t];
+                const long long hi = s_hi[t];
                 for (long long i = lo + tid; i < hi; i += kLexThreads) {
                     const int doc = __ldg(p.docs + i);
                     if (i > lo && __ldg(p.docs + i - 1) == doc) continue;  // not the head of its run
@@ -219,8 +265,8 @@ __global__ void __launch_bounds__(kLexThreads) lexical_kernel(const LexParams p)
                     }
                     acc[doc - d0] = a;
                 }
+                __syncthreads();  // slot t's additions land before slot t + 1's
             }
-            __syncthreads();  // slot t's additions land before slot t + 1's
         }
     }
 
