@@ -95,7 +95,8 @@ __device__ __forceinline__ void score_rows(const RescoreParams& p, const uint8_t
     }
     if (p.vec) {
         constexpr int kEpc = ModeTraits<MODE>::kEpc;
-#pragma unroll 2
+        // Four steps (16 row loads per lane) in flight: a 2 KB row is four steps of a warp.
+#pragma unroll 4
         for (int c = lane; c < p.nch; c += 32) {
             uint4 raw[kRescoreRows];
 #pragma unroll
@@ -317,7 +318,7 @@ int plan_rescore(const void* store, int dtype, float scale, const float* row_sca
     int cluster = 1;
     if (!emit) {
         const int sms = device_sm_count();
-        cluster = std::max(1, std::min(kRescoreMaxCluster, (2 * sms + batch - 1) / std::max(batch, 1)));
+        cluster = std::max(1, std::min(kRescoreMaxCluster, (4 * sms + batch - 1) / std::max(batch, 1)));
         cluster = std::min(cluster, std::max(1, m / 32));
         while (cluster > 1 && static_cast<long long>(cluster) * k > kRescoreMaxKeys) --cluster;
     } else {
