@@ -313,6 +313,20 @@ class Workload:
         else:
             self.search_staged_direct(stream)
 
+    # End-to-end step of a batch-1 workload: the pinned host -> device copy of the query, the
+    # search and the device -> pinned host copy of the result, replayed as one graph per query of
+    # the pool when the copies can be captured (else the search alone is a graph).
+    def e2e_step(self, i, stream):
+        g = getattr(self, "g_e2e_full", None)
+        if g:
+            g[i % len(g)].replay()
+        else:
+            self.stage_in(i)
+            self.search_staged(stream)
+            self.stage_out()
+        stream.synchronize()
+        return self.e2e_bytes()
+
     def capture(self, torch):
         if not self.graphs:
             return
@@ -333,6 +347,19 @@ class Workload:
         with torch.cuda.graph(g, stream=s):
             self.search_staged_direct(s)
         self.g_e2e = g
+        torch.cuda.synchronize()
+        try:
+            full = []
+            for i in range(self.pool):
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=s):
+                    self.stage_in(i)
+                    self.search_staged_direct(s)
+                    self.stage_out()
+                full.append(g)
+            self.g_e2e_full = full
+        except RuntimeError:
+            self.g_e2e_full = None
         torch.cuda.synchronize()
 
     @staticmethod
@@ -393,12 +420,14 @@ class Cfg2(Workload):
         self.zc.scan_topk(self.codes, self.zc.DTYPE_I8_ROW, self.D, self.d_q, self.K, row_scales=self.scales,
                           workspace=self.ws, out=self.out, stream=stream)
 
-    def e2e_step(self, i, stream):
+    def stage_in(self, i):
         self.d_q.copy_(self._q(i, self.h_queries), non_blocking=True)
-        self.search_staged(stream)
+
+    def stage_out(self):
         self.h_out[0].copy_(self.out[0], non_blocking=True)
         self.h_out[1].copy_(self.out[1], non_blocking=True)
-        stream.synchronize()
+
+    def e2e_bytes(self):
         return self.B * self.D * 4, self.B * self.K * 8
 
     def config(self, world):
@@ -463,13 +492,15 @@ class Cfg1(Workload):
         self.zc.scan_topk(self.corpus, self.zc.DTYPE_F32, self.D, self.d_q, self.K, metric=self.zc.METRIC_COSINE,
                           workspace=self.ws, out=self.out, stream=stream)
 
-    def e2e_step(self, i, stream):
+    def stage_in(self, i):
         j = i % self.NQ
         self.d_q.copy_(self.h_queries[j:j + 1], non_blocking=True)
-        self.search_staged(stream)
+
+    def stage_out(self):
         self.h_out[0].copy_(self.out[0], non_blocking=True)
         self.h_out[1].copy_(self.out[1], non_blocking=True)
-        stream.synchronize()
+
+    def e2e_bytes(self):
         return self.D * 4, self.K * 8
 
     def config(self, world):
@@ -699,14 +730,16 @@ class Cfg5(Workload):
     def search_staged_direct(self, stream):
         self._run(self.d_q, self.d_t, stream)
 
-    def e2e_step(self, i, stream):
+    def stage_in(self, i):
         j = i % self.NQ
         self.d_q.copy_(self.h_queries[j:j + 1], non_blocking=True)
         self.d_t.copy_(self.h_terms[j:j + 1], non_blocking=True)
-        self.search_staged(stream)
+
+    def stage_out(self):
         self.h_out[0].copy_(self.out[0], non_blocking=True)
         self.h_out[1].copy_(self.out[1], non_blocking=True)
-        stream.synchronize()
+
+    def e2e_bytes(self):
         return self.D * 4 + self.terms_h.shape[1] * 4, self.K * 8
 
     def config(self, world):
