@@ -174,17 +174,32 @@ __global__ void __launch_bounds__(kBucketThreads) bucket_kernel(
     const unsigned int n = mb_count[c];
     const size_t base = static_cast<size_t>(c) * mb_cap;
     const unsigned int lane = threadIdx.x & 31u;
-    for (unsigned int i0 = 0; i0 < n; i0 += 32u) {
-        const unsigned int i = i0 + lane;
-        const unsigned long long key = i < n ? mb_key[base + i] : 0ull;  // 0: empty, or a tie rejected by its key
-        const unsigned int q = key != 0ull ? mb_query[base + i] : 0xFFFFFFFFu;
-        const unsigned int peers = __match_any_sync(0xffffffffu, q);
-        if (q == 0xFFFFFFFFu) continue;
-        const int leader = __ffs(peers) - 1;
-        unsigned int slot = 0u;
-        if (static_cast<int>(lane) == leader) slot = atomicAdd(cand_count + q, static_cast<unsigned int>(__popc(peers)));
-        slot = __shfl_sync(peers, slot, leader) + static_cast<unsigned int>(__popc(peers & ((1u << lane) - 1u)));
-        if (slot < static_cast<unsigned int>(cap)) cand[static_cast<size_t>(q) * cap + slot] = key;
+    // Four 32-entry chunks per step: their loads, then their atomics, are in flight together.
+    constexpr int kU = 4;
+    for (unsigned int i0 = 0; i0 < n; i0 += 32u * kU) {
+        unsigned long long key[kU];
+        unsigned int q[kU], peers[kU], slot[kU];
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            const unsigned int i = i0 + 32u * u + lane;
+            key[u] = i < n ? mb_key[base + i] : 0ull;  // 0: empty, or a tie rejected by its key
+            q[u] = i < n ? mb_query[base + i] : 0xFFFFFFFFu;
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            if (key[u] == 0ull) q[u] = 0xFFFFFFFFu;
+            peers[u] = __match_any_sync(0xffffffffu, q[u]);
+            slot[u] = 0u;
+            if (q[u] != 0xFFFFFFFFu && static_cast<int>(lane) == __ffs(peers[u]) - 1) {
+                slot[u] = atomicAdd(cand_count + q[u], static_cast<unsigned int>(__popc(peers[u])));
+            }
+        }
+#pragma unroll
+        for (int u = 0; u < kU; ++u) {
+            const unsigned int at = __shfl_sync(0xffffffffu, slot[u], __ffs(peers[u]) - 1) +
+                                    static_cast<unsigned int>(__popc(peers[u] & ((1u << lane) - 1u)));
+            if (q[u] != 0xFFFFFFFFu && at < static_cast<unsigned int>(cap)) cand[static_cast<size_t>(q[u]) * cap + at] = key[u];
+        }
     }
 }
 
