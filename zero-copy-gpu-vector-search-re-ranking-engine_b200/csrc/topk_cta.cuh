@@ -333,25 +333,42 @@ __device__ inline bool topk_merge_lists_rank(const TopkSmem& t, int q_local, con
     }
     __syncthreads();
     const u64 floor_key = s_scratch[0];
-    // Keys >= F: a prefix of each list whose head is >= F.
+    // Keys >= F: a prefix of each list whose head is >= F. A warp takes lists warp,
+    // warp + nwarps, ...; the first 32 keys of up to kPre of them are read at once.
     bool overflow = false;
-    for (int l = warp; l < lists; l += nwarps) {
-        if (heads[l] < floor_key) continue;
-        for (int off = 0; off < k; off += 32) {
-            const u64 key = off + lane < k ? __ldcg(src + static_cast<size_t>(l) * k + off + lane) : 0ull;
-            const bool take = key >= floor_key;
-            const uint32_t ballot = __ballot_sync(0xffffffffu, take);
-            int slot = 0;
-            if (lane == 0) slot = atomicAdd(&t.count[q_local], __popc(ballot));
-            slot = __shfl_sync(0xffffffffu, slot, 0) + __popc(ballot & ((1u << lane) - 1u));
-            if (take) {
-                if (slot < kMergeCand) {
-                    cand[slot] = key;
-                } else {
-                    overflow = true;
-                }
+    auto append = [&](u64 key) {  // warp-wide; returns whether all 32 lanes took a key
+        const bool take = key >= floor_key;
+        const uint32_t ballot = __ballot_sync(0xffffffffu, take);
+        int slot = 0;
+        if (lane == 0 && ballot != 0u) slot = atomicAdd(&t.count[q_local], __popc(ballot));
+        slot = __shfl_sync(0xffffffffu, slot, 0) + __popc(ballot & ((1u << lane) - 1u));
+        if (take) {
+            if (slot < kMergeCand) {
+                cand[slot] = key;
+            } else {
+                overflow = true;
             }
-            if (ballot != 0xffffffffu) break;  // the prefix ended
+        }
+        return ballot == 0xffffffffu;
+    };
+    constexpr int kPre = 8;
+    for (int l0 = warp; l0 < lists; l0 += nwarps * kPre) {
+        u64 first[kPre];
+#pragma unroll
+        for (int u = 0; u < kPre; ++u) {
+            const int l = l0 + u * nwarps;
+            first[u] = (l < lists && heads[l] >= floor_key && lane < k) ? __ldcg(src + static_cast<size_t>(l) * k + lane)
+                                                                        : 0ull;
+        }
+#pragma unroll
+        for (int u = 0; u < kPre; ++u) {
+            const int l = l0 + u * nwarps;
+            if (l >= lists || heads[l] < floor_key) continue;  // uniform in the warp
+            if (!append(first[u])) continue;                   // the prefix ended in the first 32
+            for (int off = 32; off < k; off += 32) {
+                const u64 key = off + lane < k ? __ldcg(src + static_cast<size_t>(l) * k + off + lane) : 0ull;
+                if (!append(key)) break;
+            }
         }
     }
     if (__syncthreads_or(overflow ? 1 : 0)) return false;
