@@ -526,24 +526,41 @@ class Cfg1(Workload):
 
 class Cfg3(Workload):
     """1-bit codes (128 B/row) of 10M x 1024 fp16 rows, Hamming top-1,000,
-    fp16 rescore to top-10, batch 64."""
+    fp16 rescore to top-10, batch 64. With N ranks the rows are split into N shards, each rank
+    holding its rows' codes and fp16 rows: per-shard top-1,000 (global ids), an NCCL exchange
+    and merge to the global top-1,000, each rank rescoring the candidates it owns, a second
+    exchange and merge of the top-10 (sharded.ShardedRescoreSearch, the reference's
+    semantics)."""
 
     N, D, M, K, B, NQ = 10_000_000, 1024, 1000, 10, 64, 4096
     name = "cfg3_bin1024_10M_top1000_f16rescore_top10_b64"
     dtype = "u32 (xor+popc) / f16"
     units = 64
-    launches = 13  # prep, sample, threshold, 3 x (filter, bucket, select), rescore
     steps, warmup = 10, 3
     dominant = ("gemm_filter",)
+    scaling = "strong"
+    # prep, sample, threshold, 3 x (filter, bucket, select), rescore; sharded: two merges more
+    launches = property(lambda self: 13 if self.world == 1 else 15)
 
     def setup(self, torch, zc, device, rank, world):
-        self.torch, self.zc = torch, zc
-        self.store = normal_rows(torch, device, self.N, self.D, 3001, torch.float16)
-        self.codes = torch.empty((self.N, self.D // 32), dtype=torch.int32, device=device)
-        step = 1 << 20
-        for s in range(0, self.N, step):
-            self.codes[s:s + step] = pack_signs(torch, self.store[s:s + step])
-        self.queries = normal_rows(torch, device, self.NQ, self.D, 3002 + rank, torch.float32)
+        import sharded
+
+        self.torch, self.zc, self.world = torch, zc, world
+        self.begin, self.end = sharded.shard_bounds(self.N, world, rank)
+        rows = self.end - self.begin
+        # Each 1M-row block of the global corpus has its own seed, so a shard holds the same rows
+        # whatever the number of ranks.
+        self.store = torch.empty((rows, self.D), dtype=torch.float16, device=device)
+        blk = 1 << 20
+        for b0 in range(self.begin // blk * blk, self.end, blk):
+            block = normal_rows(torch, device, min(blk, self.N - b0), self.D, 3001 + b0 // blk, torch.float16)
+            lo, hi = max(b0, self.begin), min(b0 + block.shape[0], self.end)
+            self.store[lo - self.begin:hi - self.begin] = block[lo - b0:hi - b0]
+            del block
+        self.codes = torch.empty((rows, self.D // 32), dtype=torch.int32, device=device)
+        for s in range(0, rows, blk):
+            self.codes[s:s + blk] = pack_signs(torch, self.store[s:s + blk])
+        self.queries = normal_rows(torch, device, self.NQ, self.D, 3002, torch.float32)
         self.ws = zc.Workspace(device)
         self.cand = (torch.empty((self.B, self.M), dtype=torch.int32, device=device),
                      torch.empty((self.B, self.M), dtype=torch.float32, device=device))
@@ -554,8 +571,22 @@ class Cfg3(Workload):
                       torch.empty((self.B, self.K), dtype=torch.float32).pin_memory())
         self.d_q = torch.empty((self.B, self.D), dtype=torch.float32, device=device)
         self.store_i16 = self.store.view(torch.int16)
+        self.search = None
+        if world > 1:
+            def coarse(q, m, id_base):
+                return zc.scan_topk(self.codes, zc.DTYPE_BINARY, self.D, q, m, id_base=id_base, workspace=self.ws)
+
+            def rescore(q, local, k):
+                return zc.rescore_topk(self.store_i16, zc.DTYPE_F16, self.D, q, local, k, metric=zc.METRIC_COSINE)
+
+            self.search = sharded.ShardedRescoreSearch(self.begin, self.end, coarse, rescore)
 
     def _run(self, q, stream):
+        if self.search is not None:
+            ids, scores = self.search.search(q, self.M, self.K)
+            self.out[0].copy_(ids)
+            self.out[1].copy_(scores)
+            return
         self.zc.scan_topk(self.codes, self.zc.DTYPE_BINARY, self.D, q, self.M, workspace=self.ws, out=self.cand,
                           stream=stream)
         self.zc.rescore_topk(self.store_i16, self.zc.DTYPE_F16, self.D, q, self.cand[0], self.K,
@@ -576,14 +607,16 @@ class Cfg3(Workload):
 
     def config(self, world):
         return {"workload": self.name, "docs": self.N, "dim": self.D, "candidates": self.M, "k": self.K,
-                "batch": self.B, "storage": "1-bit codes + fp16 rescore store", "parallelism": f"replicas{world}",
+                "batch": self.B, "storage": "1-bit codes + fp16 rescore store",
+                "parallelism": f"rowshard{world}" if world > 1 else "single",
                 "l2": "inputs larger than L2 (1.28 GB codes, 20.5 GB rescore store)"}
 
     def roofline(self, kernel_ms, peaks, peak_kind):
         # Dominant: the filtered tensor-core Hamming scan (1-bit rows expanded to int8 on chip).
         # Its tensor work bounds it before its HBM reads do: 2 B N D int8 ops (0.41 ms at the
-        # int8 peak) against N D / 8 bytes of codes (0.20 ms at the HBM peak).
-        ops = 2.0 * self.B * self.N * self.D
+        # int8 peak) against N D / 8 bytes of codes (0.20 ms at the HBM peak). Sharded, each
+        # rank scans its own rows.
+        ops = 2.0 * self.B * (self.end - self.begin) * self.D
         achieved = ops / (kernel_ms * 1e-3) / 1e12
         peak, src = self.tensor_peak(peaks, "i8")
         return {"bound": "tensor", "achieved": achieved, "peak": peak, "unit": "TOP/s", "frac": achieved / peak,

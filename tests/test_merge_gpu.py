@@ -138,3 +138,79 @@ def test_sharded_search_over_nccl(tmp_path, orc):
         got = np.load(f"{path}.{rank}.npz")
         np.testing.assert_array_equal(got["ids"], ref_i)
         np.testing.assert_array_equal(got["scores"], ref_s)
+
+
+def _dev(a):
+    import torch
+
+    a = np.ascontiguousarray(a)
+    if a.dtype == np.uint16:
+        a = a.view(np.int16)
+    elif a.dtype == np.uint32:
+        a = a.view(np.int32)
+    return torch.from_numpy(a).cuda()
+
+
+def _nccl_rescore_worker(rank, world, port, result_path):
+    import sys
+
+    root = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
+    for p in (root, os.path.join(root, "zero-copy-gpu-vector-search-re-ranking-engine_b200"), os.path.join(root, "oracle")):
+        sys.path.insert(0, p)
+    from datetime import timedelta
+
+    import torch
+    import torch.distributed as dist
+
+    import oracle
+    import sharded
+    import zcgvs_sm100 as zc
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    torch.cuda.set_device(rank)
+    dist.init_process_group("nccl", rank=rank, world_size=world, timeout=timedelta(seconds=60),
+                            device_id=torch.device("cuda", rank))
+    try:
+        n, dim, batch, m, k = 30011, 256, 5, 500, 10
+        corpus = oracle.normal_rows(n, dim, 501)
+        queries = _dev(oracle.normal_rows(batch, dim, 502))
+        b, e = sharded.shard_bounds(n, world, rank)
+        codes = _dev(oracle.pack_binary(corpus[b:e]))
+        store = _dev(oracle.to_f16_bits(corpus[b:e]))
+        ws = zc.Workspace(torch.device("cuda", rank))
+
+        def coarse(q, mm, id_base):
+            return zc.scan_topk(codes, zc.DTYPE_BINARY, dim, q, mm, id_base=id_base, workspace=ws)
+
+        def rescore(q, local, kk):
+            return zc.rescore_topk(store, zc.DTYPE_F16, dim, q, local, kk, metric=zc.METRIC_COSINE)
+
+        ids, scores = sharded.ShardedRescoreSearch(b, e, coarse, rescore).search(queries, m, k)
+        torch.cuda.synchronize()
+        np.savez(f"{result_path}.{rank}.npz", ids=ids.cpu().numpy(), scores=scores.cpu().numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+def test_sharded_coarse_rescore_over_nccl(tmp_path, orc):
+    """The row-sharded 1-bit coarse search with fp16 rescoring (two exchanges) over NCCL ranks
+    equals the one-corpus pipeline of the oracle on every rank."""
+    import torch
+    import torch.multiprocessing as mp
+
+    world = min(torch.cuda.device_count(), 8)
+    if world < 2:
+        pytest.skip("needs two or more GPUs")
+    path = str(tmp_path / "nccl_rescore")
+    mp.start_processes(_nccl_rescore_worker, args=(world, _free_port(), path), nprocs=world, start_method="spawn")
+    n, dim, batch, m, k = 30011, 256, 5, 500, 10
+    corpus = orc.normal_rows(n, dim, 501)
+    queries = orc.normal_rows(batch, dim, 502)
+    c_ids, _ = orc.scan_topk(orc.pack_binary(corpus), orc.DTYPE_BINARY, dim, queries, m)
+    ref_i, ref_s = orc.rescore_topk(orc.to_f16_bits(corpus), orc.DTYPE_F16, dim, queries, c_ids, k,
+                                    metric=orc.METRIC_COSINE)
+    for rank in range(world):
+        got = np.load(f"{path}.{rank}.npz")
+        np.testing.assert_array_equal(got["ids"], ref_i)
+        np.testing.assert_allclose(got["scores"], ref_s, rtol=0, atol=1e-4)

@@ -106,3 +106,58 @@ def test_shard_bounds_cover_rows_once():
             assert spans[0][0] == 0 and spans[-1][1] == n
             assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
             assert max(e - b for b, e in spans) - min(e - b for b, e in spans) <= 1
+
+
+def rescore_worker(rank, world, port, n, dim, batch, m, k, result_path):
+    import torch
+    import torch.distributed as dist
+
+    import oracle
+    import sharded
+
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world)
+    try:
+        corpus = oracle.normal_rows(n, dim, 777)
+        queries = oracle.normal_rows(batch, dim, 778)
+        codes = oracle.pack_binary(corpus)
+        store = oracle.to_f16_bits(corpus)
+        begin, end = sharded.shard_bounds(n, world, rank)
+
+        def coarse(qs, mm, id_base):
+            i, s = oracle.scan_topk(codes[begin:end], oracle.DTYPE_BINARY, dim, qs, mm, id_base=id_base)
+            return torch.from_numpy(i), torch.from_numpy(s)
+
+        def rescore(qs, local, kk):
+            i, s = oracle.rescore_topk(store[begin:end], oracle.DTYPE_F16, dim, qs, local.numpy(), kk)
+            return torch.from_numpy(i), torch.from_numpy(s)
+
+        search = sharded.ShardedRescoreSearch(begin, end, coarse, rescore, merge=oracle_merge)
+        ids, scores = search.search(queries, m, k)
+        np.savez(f"{result_path}.{rank}.npz", ids=ids.numpy(), scores=scores.numpy())
+    finally:
+        dist.destroy_process_group()
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_sharded_coarse_rescore_equals_single_corpus(tmp_path, world):
+    """BASELINE config 3 split over ranks: per-shard 1-bit top-m, exchange and merge, each rank
+    rescores the global candidates it owns against its fp16 rows, exchange and merge. Every rank
+    must hold the one-corpus pipeline's result bit for bit."""
+    import torch.multiprocessing as mp
+
+    import oracle
+
+    n, dim, batch, m, k = 4001, 128, 3, 64, 10
+    path = str(tmp_path / "rescore")
+    mp.start_processes(rescore_worker, args=(world, free_port(), n, dim, batch, m, k, path), nprocs=world,
+                       start_method="spawn")
+    corpus = oracle.normal_rows(n, dim, 777)
+    queries = oracle.normal_rows(batch, dim, 778)
+    cand, _ = oracle.scan_topk(oracle.pack_binary(corpus), oracle.DTYPE_BINARY, dim, queries, m)
+    ref_i, ref_s = oracle.rescore_topk(oracle.to_f16_bits(corpus), oracle.DTYPE_F16, dim, queries, cand, k)
+    for rank in range(world):
+        got = np.load(f"{path}.{rank}.npz")
+        np.testing.assert_array_equal(got["ids"], ref_i)
+        np.testing.assert_array_equal(got["scores"], ref_s)

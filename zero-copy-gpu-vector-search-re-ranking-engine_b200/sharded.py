@@ -9,7 +9,8 @@ top-k lists contains the global top-k and the order is total, so the result is i
 single-GPU search over the whole corpus.
 
 The exchange is [P, B, k] ids and score bits (B x k x 8 bytes per rank): latency-bound, so one
-all-gather of a packed int32 tensor is used, capturable in a CUDA graph.
+all-gather of a packed int32 tensor is used, capturable in a CUDA graph. A coarse search with
+rescoring (ShardedRescoreSearch) exchanges twice: the coarse top-M, then the rescored top-k.
 """
 
 from __future__ import annotations
@@ -42,20 +43,65 @@ class ShardedSearch:
         self.group = group
 
     def search(self, queries, k: int):
-        import torch
-        import torch.distributed as dist
-
         ids, scores = self.local_search(queries, k, self.shard_begin)
-        world = dist.get_world_size(self.group)
-        # One packed exchange: ids and the scores' bit patterns side by side.
-        packed = torch.stack([ids, scores.view(torch.int32)])            # [2, B, k]
-        # Concatenated along dim 0 (the layout every backend accepts), then viewed per rank.
-        gathered = torch.empty((world * 2,) + tuple(packed.shape[1:]), dtype=packed.dtype, device=packed.device)
-        dist.all_gather_into_tensor(gathered, packed, group=self.group)
-        gathered = gathered.view((world, 2) + tuple(packed.shape[1:]))
-        all_ids = gathered[:, 0].contiguous()                              # [P, B, k]
-        all_scores = gathered[:, 1].contiguous().view(torch.float32)
-        return self.merge(all_ids, all_scores, k)
+        return gather_merge(ids, scores, k, self.merge, self.group)
+
+
+def gather_merge(ids, scores, k: int, merge, group=None):
+    """Every rank's [B, k_in] (global ids, scores) -> the global top-k on every rank: one
+    all-gather of ids and score bits packed side by side, then `merge` over [P, B, k_in]."""
+    import torch
+    import torch.distributed as dist
+
+    world = dist.get_world_size(group)
+    packed = torch.stack([ids, scores.view(torch.int32)])            # [2, B, k_in]
+    # Concatenated along dim 0 (the layout every backend accepts), then viewed per rank.
+    gathered = torch.empty((world * 2,) + tuple(packed.shape[1:]), dtype=packed.dtype, device=packed.device)
+    dist.all_gather_into_tensor(gathered, packed, group=group)
+    gathered = gathered.view((world, 2) + tuple(packed.shape[1:]))
+    all_ids = gathered[:, 0].contiguous()                              # [P, B, k_in]
+    all_scores = gathered[:, 1].contiguous().view(torch.float32)
+    return merge(all_ids, all_scores, k)
+
+
+class ShardedRescoreSearch:
+    """One rank's part of a row-sharded coarse search with exact rescoring (
+    1-bit top-M, fp16 rescore to top-k), with the reference's semantics: the rescore sees the
+    global top-M.
+
+    1. coarse_search(queries, m, id_base) -> [B, m] (global ids, scores) over this rank's codes;
+    2. all-gather and merge: every rank holds the same global top-m;
+    3. rescore(queries, local_candidates [B, m], k) -> [B, k] (local ids, scores) over this
+       rank's rows of the rescore store, for the candidates it owns (the others are -1, which
+       the rescore drops);
+    4. all-gather and merge of the per-rank top-k.
+
+    Each step's result is the single-GPU one (unions of per-shard top lists contain the global
+    ones, the order is total), so the search equals the one-GPU pipeline bit for bit.
+    """
+
+    def __init__(self, shard_begin: int, shard_end: int, coarse_search, rescore, merge=None, group=None):
+        self.shard_begin = shard_begin
+        self.shard_end = shard_end
+        self.coarse_search = coarse_search
+        self.rescore = rescore
+        if merge is None:
+            import zcgvs_sm100 as zc
+
+            merge = zc.merge_topk
+        self.merge = merge
+        self.group = group
+
+    def search(self, queries, m: int, k: int):
+        import torch
+
+        ids, scores = self.coarse_search(queries, m, self.shard_begin)
+        cand, _ = gather_merge(ids, scores, m, self.merge, self.group)
+        mine = (cand >= self.shard_begin) & (cand < self.shard_end)
+        local = torch.where(mine, cand - self.shard_begin, torch.full_like(cand, -1))
+        r_ids, r_scores = self.rescore(queries, local, k)
+        r_ids = torch.where(r_ids >= 0, r_ids + self.shard_begin, r_ids)
+        return gather_merge(r_ids, r_scores, k, self.merge, self.group)
 
 
 def scan_shard_search(corpus_shard, dtype: int, dim: int, *, scale: float = 1.0, row_scales=None, mask=None,
