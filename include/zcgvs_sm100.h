@@ -291,6 +291,10 @@ int zcgvs_fuse_scores(float* dense, const float* lexical, const float* lexical_m
  *   zcgvs_convert_f16   : launchConvertF32ToF16 (include/zcgvs/cuda/convert.cuh:10-20).
  *   zcgvs_convert_i8    : launchConvertF32ToI8: clamp(rint(x * (1 / scale)), +-127) with the
  *                         reciprocal taken on the host (0 when scale <= 0).
+ *   zcgvs_convert_i8_rows : the per-row extension of launchConvertF32ToI8 that builds
+ *                         ZCGVS_DTYPE_I8_ROW stores: per row, scale = max|x| / 127 (1 for an
+ *                         all-zero row) into row_scales[rows], then clamp(rint(x * (1 / scale)),
+ *                         +-127) into dst_int8 [rows, dim].
  *   zcgvs_pack_binary   : launchPackBinary: bit b of word w = dim 32w+b, set when x >= 0.
  *   zcgvs_remap_indices : launchRemapIndices (include/zcgvs/cuda/rescore.cuh:34-45).
  * --------------------------------------------------------------------------------------- */
@@ -298,6 +302,8 @@ int zcgvs_topk(const float* scores, int64_t doc_count, int k, int batch, int* ou
                float* out_scores, void* stream);
 int zcgvs_convert_f16(const float* src, void* dst_half, size_t count, void* stream);
 int zcgvs_convert_i8(const float* src, void* dst_int8, size_t count, float scale, void* stream);
+int zcgvs_convert_i8_rows(const float* src, void* dst_int8, float* row_scales, int64_t rows, int dim,
+                          void* stream);
 int zcgvs_pack_binary(const float* src, void* dst_words, int64_t rows, int dim, void* stream);
 int zcgvs_remap_indices(const int* candidates, const int* local_indices, int candidate_count,
                         int k, int batch, int* out_indices, void* stream);

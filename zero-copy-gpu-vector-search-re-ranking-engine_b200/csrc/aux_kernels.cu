@@ -98,6 +98,58 @@ __global__ void convert_i8_kernel(const float* __restrict__ src, int8_t* __restr
     }
 }
 
+// Per-row symmetric int8 (the per-row extension of src/cuda/convert.cu:17-32): one warp per row,
+// scale = max|x| / 127 (1 for an all-zero row), then clamp(rint(x * (1 / scale)), +-127), both
+// rounded as the host oracle rounds them. The max is order-independent, so any lane split gives
+// the same scale. The row is read twice; the second pass hits L1 / L2 (rows of a few KB).
+__global__ void __launch_bounds__(kConvertThreads) convert_i8_rows_kernel(const float* __restrict__ src,
+                                                                          int8_t* __restrict__ dst,
+                                                                          float* __restrict__ row_scales,
+                                                                          long long rows, int dim, int vec) {
+    const int lane = threadIdx.x & 31;
+    const long long warps = static_cast<long long>(gridDim.x) * (kConvertThreads / 32);
+    for (long long r = blockIdx.x * static_cast<long long>(kConvertThreads / 32) + (threadIdx.x >> 5); r < rows;
+         r += warps) {
+        const float* x = src + r * dim;
+        int8_t* y = dst + r * dim;
+        float peak = 0.0f;
+        if (vec) {
+            const float4* x4 = reinterpret_cast<const float4*>(x);
+            for (int c = lane; c < dim / 4; c += 32) {
+                const float4 v = __ldg(x4 + c);
+                peak = fmaxf(peak, fmaxf(fmaxf(fabsf(v.x), fabsf(v.y)), fmaxf(fabsf(v.z), fabsf(v.w))));
+            }
+        } else {
+            for (int j = lane; j < dim; j += 32) peak = fmaxf(peak, fabsf(__ldg(x + j)));
+        }
+#pragma unroll
+        for (int o = 16; o > 0; o >>= 1) peak = fmaxf(peak, __shfl_xor_sync(0xffffffffu, peak, o));
+        const float scale = peak > 0.0f ? __fdiv_rn(peak, 127.0f) : 1.0f;
+        const float inv = __fdiv_rn(1.0f, scale);
+        if (lane == 0) row_scales[r] = scale;
+        if (vec) {
+            const float4* x4 = reinterpret_cast<const float4*>(x);
+            uint32_t* y4 = reinterpret_cast<uint32_t*>(y);
+            for (int c = lane; c < dim / 4; c += 32) {
+                const float4 v = __ldg(x4 + c);
+                const float f[4] = {v.x, v.y, v.z, v.w};
+                uint32_t packed = 0u;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const float q = fminf(fmaxf(rintf(__fmul_rn(f[e], inv)), -127.0f), 127.0f);
+                    packed |= (static_cast<uint32_t>(static_cast<int>(q)) & 0xffu) << (8 * e);
+                }
+                y4[c] = packed;
+            }
+        } else {
+            for (int j = lane; j < dim; j += 32) {
+                const float q = fminf(fmaxf(rintf(__fmul_rn(__ldg(x + j), inv)), -127.0f), 127.0f);
+                y[j] = static_cast<int8_t>(q);
+            }
+        }
+    }
+}
+
 // Bit b of word w = dimension 32 w + b, set when the value is >= 0 (src/cuda/convert.cu:34-53).
 __global__ void pack_binary_kernel(const float* __restrict__ src, uint32_t* __restrict__ dst, long long rows, int dim,
                                    int words) {
@@ -206,6 +258,21 @@ int zcgvs_convert_i8(const float* src, void* dst_int8, size_t count, float scale
     convert_i8_kernel<<<grid_for(count), kConvertThreads, 0, static_cast<cudaStream_t>(stream)>>>(
         src, static_cast<int8_t*>(dst_int8), count, inv);
     return launched("convert_i8_kernel launch");
+}
+
+int zcgvs_convert_i8_rows(const float* src, void* dst_int8, float* row_scales, int64_t rows, int dim, void* stream) {
+    using namespace zc;
+    if (rows <= 0 || dim <= 0) return ok();
+    if (src == nullptr || dst_int8 == nullptr || row_scales == nullptr) {
+        return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs_convert_i8_rows: null pointer");
+    }
+    const int vec = (dim % 4 == 0 && reinterpret_cast<uintptr_t>(src) % 16 == 0 &&
+                     reinterpret_cast<uintptr_t>(dst_int8) % 4 == 0) ? 1 : 0;
+    const long long blocks = (rows + kConvertThreads / 32 - 1) / (kConvertThreads / 32);
+    const int grid = static_cast<int>(std::max<long long>(1, std::min<long long>(blocks, 16LL * device_sm_count())));
+    convert_i8_rows_kernel<<<grid, kConvertThreads, 0, static_cast<cudaStream_t>(stream)>>>(
+        src, static_cast<int8_t*>(dst_int8), row_scales, rows, dim, vec);
+    return launched("convert_i8_rows_kernel launch");
 }
 
 int zcgvs_pack_binary(const float* src, void* dst_words, int64_t rows, int dim, void* stream) {

@@ -66,8 +66,52 @@ public:
         bytes(got, 4);
         if (std::memcmp(got, expected, 4) != 0) throw std::runtime_error("zcgvs: '" + path_ + "' has the wrong magic");
     }
+    // Streams `count` bytes of the file into device memory through two pinned chunks: the read
+    // of one chunk overlaps the host-to-device copy of the other, and no host copy of the whole
+    // payload is made.
+    void toDevice(void* device_dst, std::size_t count) {
+        if (count == 0) return;
+        constexpr std::size_t kChunk = std::size_t(32) << 20;
+        const std::size_t chunk = std::min(count, kChunk);
+        PinnedBuffer<std::uint8_t> stage[2] = {PinnedBuffer<std::uint8_t>(chunk),
+                                               PinnedBuffer<std::uint8_t>(count > chunk ? chunk : 0)};
+        StreamGuard copies;
+        auto* dst = static_cast<std::uint8_t*>(device_dst);
+        for (std::size_t done = 0, i = 0; done < count; done += chunk, ++i) {
+            const std::size_t n = std::min(chunk, count - done);
+            const int b = static_cast<int>(i & 1);
+            ZCGVS_CUDA_CHECK(cudaEventSynchronize(copies.ready[b]));  // its previous copy has finished
+            bytes(stage[b].data(), n);
+            ZCGVS_CUDA_CHECK(cudaMemcpyAsync(dst + done, stage[b].data(), n, cudaMemcpyHostToDevice, copies.stream));
+            ZCGVS_CUDA_CHECK(cudaEventRecord(copies.ready[b], copies.stream));
+        }
+        ZCGVS_CUDA_CHECK(cudaStreamSynchronize(copies.stream));
+    }
 
 private:
+    // A copy stream and one event per staging chunk, synchronised and released on every exit
+    // (a short file throws from bytes() with copies in flight).
+    struct StreamGuard {
+        cudaStream_t stream = nullptr;
+        cudaEvent_t ready[2] = {nullptr, nullptr};
+        StreamGuard() {
+            ZCGVS_CUDA_CHECK(cudaStreamCreateWithFlags(&stream, cudaStreamNonBlocking));
+            for (auto& e : ready) {
+                ZCGVS_CUDA_CHECK(cudaEventCreateWithFlags(&e, cudaEventDisableTiming));
+                ZCGVS_CUDA_CHECK(cudaEventRecord(e, stream));
+            }
+        }
+        ~StreamGuard() {
+            if (stream != nullptr) cudaStreamSynchronize(stream);
+            for (auto e : ready) {
+                if (e != nullptr) cudaEventDestroy(e);
+            }
+            if (stream != nullptr) cudaStreamDestroy(stream);
+        }
+        StreamGuard(const StreamGuard&) = delete;
+        StreamGuard& operator=(const StreamGuard&) = delete;
+    };
+
     std::ifstream in_;
     std::string path_;
 };
@@ -150,6 +194,11 @@ void launchPackBinary(const float* src, void* dst_words, int rows, int dim, cuda
     check(zcgvs_pack_binary(src, dst_words, rows, dim, stream), "zcgvs_pack_binary");
 }
 
+void launchConvertF32ToI8Rows(const float* src, void* dst_int8, float* row_scales, std::int64_t rows, int dim,
+                              cudaStream_t stream) {
+    check(zcgvs_convert_i8_rows(src, dst_int8, row_scales, rows, dim, stream), "zcgvs_convert_i8_rows");
+}
+
 void launchBm25(const std::int64_t* d_offsets, const int* d_docs, const float* d_weights, const int* d_query_terms,
                 int term_count, int doc_count, float* d_scores, cudaStream_t stream) {
     check(zcgvs_bm25(d_offsets, d_docs, d_weights, d_query_terms, term_count, doc_count, d_scores, stream),
@@ -186,12 +235,15 @@ std::size_t rescoreSharedBytes(int dim) { return static_cast<std::size_t>(dim) *
 // ------------------------------------------------------------------------------------------
 // EmbeddingStore
 // ------------------------------------------------------------------------------------------
-void EmbeddingStore::convertInto(std::uint8_t* destination, const float* device_float32, std::int64_t rows,
-                                 cudaStream_t stream) {
+void EmbeddingStore::convertInto(std::uint8_t* destination, float* row_scales, const float* device_float32,
+                                 std::int64_t rows, cudaStream_t stream) {
     const std::size_t elements = static_cast<std::size_t>(rows) * static_cast<std::size_t>(dim_);
     switch (dtype_) {
         case ScalarType::Float16: cuda::launchConvertF32ToF16(device_float32, destination, elements, stream); break;
         case ScalarType::Int8: cuda::launchConvertF32ToI8(device_float32, destination, elements, scale_, stream); break;
+        case ScalarType::Int8PerRow:
+            cuda::launchConvertF32ToI8Rows(device_float32, destination, row_scales, rows, dim_, stream);
+            break;
         case ScalarType::Binary: cuda::launchPackBinary(device_float32, destination, static_cast<int>(rows), dim_, stream); break;
         default: throw std::invalid_argument("zcgvs: unsupported storage dtype");
     }
@@ -210,6 +262,7 @@ EmbeddingStore EmbeddingStore::fromHostMatrix(const float* host_float32, std::in
     store.doc_count_ = doc_count;
     store.capacity_ = doc_count;
     store.device_.allocate(static_cast<std::size_t>(doc_count) * store.rowStride());
+    if (dtype == ScalarType::Int8PerRow) store.row_scales_.allocate(static_cast<std::size_t>(doc_count));
     const std::size_t elements = static_cast<std::size_t>(doc_count) * static_cast<std::size_t>(dim);
     if (dtype == ScalarType::Float32) {
         ZCGVS_CUDA_CHECK(cudaMemcpy(store.device_.data(), host_float32, elements * sizeof(float), cudaMemcpyHostToDevice));
@@ -217,7 +270,7 @@ EmbeddingStore EmbeddingStore::fromHostMatrix(const float* host_float32, std::in
     }
     DeviceBuffer<float> staging(elements);
     ZCGVS_CUDA_CHECK(cudaMemcpy(staging.data(), host_float32, elements * sizeof(float), cudaMemcpyHostToDevice));
-    store.convertInto(store.device_.data(), staging.data(), doc_count, nullptr);
+    store.convertInto(store.device_.data(), store.row_scales_.data(), staging.data(), doc_count, nullptr);
     ZCGVS_CUDA_CHECK(cudaDeviceSynchronize());
     return store;
 }
@@ -226,13 +279,16 @@ EmbeddingStore EmbeddingStore::loadFromFile(const std::string& path) {
     Reader in(path);
     in.magic("ZCVE");
     const auto version = in.scalar<std::uint32_t>();
-    if (version == 0 || version > 2) throw std::runtime_error("zcgvs: unsupported embedding file version " + std::to_string(version));
+    if (version == 0 || version > 3) throw std::runtime_error("zcgvs: unsupported embedding file version " + std::to_string(version));
     const auto flags = in.scalar<std::uint32_t>();
     const auto doc_count = in.scalar<std::int64_t>();
     const auto dim = in.scalar<std::int32_t>();
     const auto code = in.scalar<std::int32_t>();
     if (doc_count <= 0 || dim <= 0) throw std::runtime_error("zcgvs: embedding file reports an empty matrix");
-    if (code < 0 || code > 3) throw std::runtime_error("zcgvs: unsupported embedding dtype code " + std::to_string(code));
+    if (code < 0 || code > 4) throw std::runtime_error("zcgvs: unsupported embedding dtype code " + std::to_string(code));
+    if (code == static_cast<std::int32_t>(ScalarType::Int8PerRow) && version < 3) {
+        throw std::runtime_error("zcgvs: per-row int8 embeddings require file version 3");
+    }
     EmbeddingStore store;
     store.dim_ = dim;
     store.dtype_ = static_cast<ScalarType>(code);
@@ -248,10 +304,12 @@ EmbeddingStore EmbeddingStore::loadFromFile(const std::string& path) {
         throw std::runtime_error("zcgvs: quantized embeddings require file version 2");
     }
     const std::size_t total = static_cast<std::size_t>(doc_count) * stride;
-    std::vector<std::uint8_t> host(total);
-    in.bytes(host.data(), total);
     store.device_.allocate(total);
-    ZCGVS_CUDA_CHECK(cudaMemcpy(store.device_.data(), host.data(), total, cudaMemcpyHostToDevice));
+    in.toDevice(store.device_.data(), total);
+    if (store.dtype_ == ScalarType::Int8PerRow) {
+        store.row_scales_.allocate(static_cast<std::size_t>(doc_count));
+        in.toDevice(store.row_scales_.data(), static_cast<std::size_t>(doc_count) * sizeof(float));
+    }
     store.doc_count_ = doc_count;
     store.capacity_ = doc_count;
     return store;
@@ -261,12 +319,19 @@ void EmbeddingStore::ensureCapacity(std::int64_t required_docs, cudaStream_t str
     if (capacity_ >= required_docs) return;
     const std::int64_t grown = std::max(required_docs, capacity_ * 2);
     DeviceBuffer<std::uint8_t> resized(static_cast<std::size_t>(grown) * rowStride());
+    DeviceBuffer<float> resized_scales(dtype_ == ScalarType::Int8PerRow ? static_cast<std::size_t>(grown) : 0);
     if (doc_count_ > 0) {
         ZCGVS_CUDA_CHECK(cudaMemcpyAsync(resized.data(), device_.data(), static_cast<std::size_t>(doc_count_) * rowStride(),
                                          cudaMemcpyDeviceToDevice, stream));
+        if (resized_scales.size() > 0) {
+            ZCGVS_CUDA_CHECK(cudaMemcpyAsync(resized_scales.data(), row_scales_.data(),
+                                             static_cast<std::size_t>(doc_count_) * sizeof(float),
+                                             cudaMemcpyDeviceToDevice, stream));
+        }
     }
     ZCGVS_CUDA_CHECK(cudaStreamSynchronize(stream));
     device_ = std::move(resized);
+    row_scales_ = std::move(resized_scales);
     capacity_ = grown;
 }
 
@@ -281,7 +346,8 @@ void EmbeddingStore::append(const float* host_float32, std::int64_t add_count, c
     } else {
         DeviceBuffer<float> staging(elements);
         ZCGVS_CUDA_CHECK(cudaMemcpyAsync(staging.data(), host_float32, elements * sizeof(float), cudaMemcpyHostToDevice, stream));
-        convertInto(destination, staging.data(), add_count, stream);
+        float* scales = row_scales_.size() > 0 ? row_scales_.data() + doc_count_ : nullptr;
+        convertInto(destination, scales, staging.data(), add_count, stream);
         ZCGVS_CUDA_CHECK(cudaStreamSynchronize(stream));
     }
     ZCGVS_CUDA_CHECK(cudaStreamSynchronize(stream));
@@ -476,21 +542,22 @@ void Searcher::recordPipeline(std::int64_t doc_count, int batch, const SearchPar
     const int dtype = static_cast<int>(store_.dtype());
     const int metric = static_cast<int>(params.metric);
     if (lexicalEnabled(params)) {
-        check(zcgvs_hybrid_topk(store_.deviceData(), dtype, store_.scale(), nullptr, doc_count, dim_, d_queries_.data(),
+        check(zcgvs_hybrid_topk(store_.deviceData(), dtype, store_.scale(), store_.rowScales(), doc_count, dim_, d_queries_.data(),
                                 batch, params.d_mask, metric, lexical_index_->deviceOffsets(),
                                 lexical_index_->devicePostingDocs(), lexical_index_->devicePostingWeights(),
                                 lexical_index_->vocabSize(), d_query_terms_.data(), params.lexical_stride,
                                 params.dense_weight, width, ids, scores, d_workspace_.data(), d_workspace_.bytes(), stream),
               "zcgvs_hybrid_topk");
     } else {
-        check(zcgvs_scan_topk(store_.deviceData(), dtype, store_.scale(), nullptr, doc_count, dim_, d_queries_.data(),
+        check(zcgvs_scan_topk(store_.deviceData(), dtype, store_.scale(), store_.rowScales(), doc_count, dim_, d_queries_.data(),
                               batch, params.d_mask, metric, width, 0, ids, scores, d_workspace_.data(),
                               d_workspace_.bytes(), stream),
               "zcgvs_scan_topk");
     }
     if (rescore) {
         check(zcgvs_rescore_topk(rescore_store_->deviceData(), static_cast<int>(rescore_store_->dtype()),
-                                 rescore_store_->scale(), nullptr, rescore_store_->docCount(), dim_, d_queries_.data(),
+                                 rescore_store_->scale(), rescore_store_->rowScales(), rescore_store_->docCount(), dim_,
+                                 d_queries_.data(),
                                  batch, d_coarse_indices_.data(), width, metric, params.k, d_out_indices_.data(),
                                  d_out_values_.data(), stream),
               "zcgvs_rescore_topk");

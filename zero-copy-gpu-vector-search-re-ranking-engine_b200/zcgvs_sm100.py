@@ -50,6 +50,7 @@ SIGNATURES = {
     "zcgvs_topk": (_i32, [_P, _i64, _i32, _i32, _P, _P, _P]),
     "zcgvs_convert_f16": (_i32, [_P, _P, _sz, _P]),
     "zcgvs_convert_i8": (_i32, [_P, _P, _sz, _f32, _P]),
+    "zcgvs_convert_i8_rows": (_i32, [_P, _P, _P, _i64, _i32, _P]),
     "zcgvs_pack_binary": (_i32, [_P, _P, _i64, _i32, _P]),
     "zcgvs_remap_indices": (_i32, [_P, _P, _i32, _i32, _i32, _P, _P]),
     "zcgvs_merge_topk": (_i32, [_P, _P, _i32, _i32, _i32, _i32, _P, _P, _P]),
@@ -360,4 +361,50 @@ def topk(scores, k: int, out=None, stream=None):
         out = (torch.empty((batch, k), dtype=torch.int32, device=scores.device),
                torch.empty((batch, k), dtype=torch.float32, device=scores.device))
     check(lib().zcgvs_topk(_ptr(scores), n, k, batch, _ptr(out[0]), _ptr(out[1]), _stream(stream)))
+    return out
+
+
+# ------------------------------------------------------------------------------------------
+# Store converters: fp32 rows on the device -> the stored precisions.
+# ------------------------------------------------------------------------------------------
+def convert_f16(src, out=None, stream=None):
+    """fp32 -> fp16 bits (round to nearest even), any shape. Returns int16 bits of src's shape."""
+    import torch
+
+    out = torch.empty(src.shape, dtype=torch.int16, device=src.device) if out is None else out
+    check(lib().zcgvs_convert_f16(_ptr(src), _ptr(out), src.numel(), _stream(stream)))
+    return out
+
+
+def convert_i8(src, scale: float, out=None, stream=None):
+    """Per-matrix int8: clamp(rint(x * (1 / scale)), +-127), any shape."""
+    import torch
+
+    out = torch.empty(src.shape, dtype=torch.int8, device=src.device) if out is None else out
+    check(lib().zcgvs_convert_i8(_ptr(src), _ptr(out), src.numel(), scale, _stream(stream)))
+    return out
+
+
+def convert_i8_rows(src, out=None, stream=None):
+    """Per-row int8 of fp32 rows [rows, dim] -> (int8 [rows, dim], fp32 scales [rows]), the
+    DTYPE_I8_ROW store layout."""
+    import torch
+
+    rows, dim = src.shape
+    if out is None:
+        out = (torch.empty((rows, dim), dtype=torch.int8, device=src.device),
+               torch.empty((rows,), dtype=torch.float32, device=src.device))
+    check(lib().zcgvs_convert_i8_rows(_ptr(src), _ptr(out[0]), _ptr(out[1]), rows, dim, _stream(stream)))
+    return out
+
+
+def pack_binary(src, out=None, stream=None):
+    """Sign bits of fp32 rows [rows, dim] -> int32 words [rows, ceil(dim / 32)] (bit b of word w
+    is dimension 32 w + b, set when x >= 0)."""
+    import torch
+
+    rows, dim = src.shape
+    if out is None:
+        out = torch.empty((rows, (dim + 31) // 32), dtype=torch.int32, device=src.device)
+    check(lib().zcgvs_pack_binary(_ptr(src), _ptr(out), rows, dim, _stream(stream)))
     return out
