@@ -212,29 +212,34 @@ __global__ void __launch_bounds__(kBucketThreads) bucket_kernel(
 //
 // Selection by radix: passes over 8-bit digits from the top (the query's candidates re-read
 // each pass, from L1 after the first) find the prefix of the k-th largest key, stopping once
-// the keys sharing the prefix are exactly the ones still needed. Each warp counts digits in its
+// the keys sharing the prefix are exactly the ones still needed. Once the keys sharing the
+// prefix fit the sort buffer (typically after the score's leading digits: the rest are the
+// boundary score's ties, told apart by id digits), they are copied there and the remaining
+// passes read only them. Each warp counts digits in its
 // own histogram (one leader lane per group of equal digits adds the group's size: no shared
 // atomics, which serialise when every candidate shares the top digits). The selected keys, k
 // in all (keys are distinct), land at per-warp offsets and are sorted in shared memory. A
 // network over all candidates would cost a compare-exchange per key and stage of a sort k to
 // 16 times wider.
 constexpr int kSelectSort = 1024;  // >= ZCGVS_MAX_K, a power of two
-constexpr int kSelectWarps = kSelectThreads / 32;
-
-__global__ void __launch_bounds__(kSelectThreads) select_kernel(const unsigned long long* __restrict__ cand,
+// One query per block: 1,024 threads when the batch leaves SMs idle (latency of the passes),
+// 512 (more blocks per SM) otherwise.
+template <int kPickThreads>
+__global__ void __launch_bounds__(kPickThreads) select_kernel(const unsigned long long* __restrict__ cand,
                                                                 unsigned int* cand_count, int cap, int k,
                                                                 unsigned long long* thr_key,
                                                                 const unsigned long long* thr_safe, int* done,
                                                                 unsigned int* flags, unsigned int* mneed, int mtiles,
                                                                 unsigned int* status, int pass, int* out_idx,
                                                                 float* out_scores) {
+    constexpr int kSelectWarps = kPickThreads / 32;
     __shared__ u64 keys[kSelectSort];
     __shared__ unsigned int whist[kSelectWarps][256];
     __shared__ unsigned int hist[256];
     __shared__ int s_wbase[kSelectWarps];
     __shared__ int s_count;
     __shared__ u64 s_thr;
-    __shared__ int s_digit, s_above, s_group;
+    __shared__ int s_digit, s_above, s_group, s_fill;
     const int q = blockIdx.x;
     if (pass > 0 && (*reinterpret_cast<const volatile unsigned int*>(flags + pass) == 0u || done[q])) return;
     const bool final = pass == kPasses - 1;
@@ -247,19 +252,22 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(const unsigned l
     const int warp = tid >> 5;
     const unsigned long long* mine = cand + static_cast<size_t>(q) * cap;  // non-zero keys
     // Candidate i of a round: every warp runs the same number of rounds (warp-wide shuffles).
-    const int rounds = (n + kSelectThreads - 1) / kSelectThreads;
+    const int rounds = (n + kPickThreads - 1) / kPickThreads;
     // Prefix (under mask) of the k-th largest key; with n <= k every candidate is kept.
     u64 prefix = 0ull, mask = 0ull;
     if (n > k) {
         int rem = k;
+        int src_n = n;         // keys in the pass's source
+        bool compact = false;  // the source is keys[]: the keys sharing the prefix
         for (int shift = 56; shift >= 0; shift -= 8) {
 #pragma unroll
             for (int j = 0; j < 8; ++j) whist[warp][lane + 32 * j] = 0u;
             __syncwarp();
+            const int src_rounds = (src_n + kPickThreads - 1) / kPickThreads;
 #pragma unroll 4
-            for (int r = 0; r < rounds; ++r) {
-                const int i = r * kSelectThreads + tid;
-                const u64 key = i < n ? __ldg(mine + i) : 0ull;
+            for (int r = 0; r < src_rounds; ++r) {
+                const int i = r * kPickThreads + tid;
+                const u64 key = i < src_n ? (compact ? keys[i] : __ldg(mine + i)) : 0ull;
                 const bool in = key != 0ull && (key & mask) == prefix;
                 const unsigned int digit = in ? static_cast<unsigned int>(key >> shift) & 0xFFu : 0x100u + lane;
                 const unsigned int peers = __match_any_sync(0xffffffffu, digit);
@@ -314,13 +322,33 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(const unsigned l
             mask |= 0xFFull << shift;
             rem -= s_above;
             if (s_group == rem) break;  // every key with this prefix is in
+            if (!compact && s_group <= kSelectSort && shift > 0) {
+                // keys[] is free until the final gather: copy the keys sharing the prefix.
+                if (tid == 0) s_fill = 0;
+                __syncthreads();
+#pragma unroll 4
+                for (int r = 0; r < rounds; ++r) {
+                    const int i = r * kPickThreads + tid;
+                    const u64 key = i < n ? __ldg(mine + i) : 0ull;
+                    const bool take = key != 0ull && (key & mask) == prefix;
+                    const unsigned int ballot = __ballot_sync(0xffffffffu, take);
+                    int base = 0;
+                    if (lane == 0 && ballot != 0u) base = atomicAdd(&s_fill, __popc(ballot));
+                    base = __shfl_sync(0xffffffffu, base, 0);
+                    if (take) keys[base + __popc(ballot & ((1u << lane) - 1u))] = key;
+                }
+                __syncthreads();
+                src_n = s_group;
+                compact = true;
+            }
         }
+        __syncthreads();  // keys[] is rewritten by the gather below
     }
     // Gather the selected keys (k of them, or all n) at per-warp offsets and sort them.
     int wsel = 0;  // this warp's selected keys (the same in every lane)
 #pragma unroll 4
     for (int r = 0; r < rounds; ++r) {
-        const int i = r * kSelectThreads + tid;
+        const int i = r * kPickThreads + tid;
         const u64 key = i < n ? __ldg(mine + i) : 0ull;
         wsel += __popc(__ballot_sync(0xffffffffu, key != 0ull && (key & mask) >= prefix));
     }
@@ -340,7 +368,7 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(const unsigned l
     int slot = s_wbase[warp];
 #pragma unroll 4
     for (int r = 0; r < rounds; ++r) {
-        const int i = r * kSelectThreads + tid;
+        const int i = r * kPickThreads + tid;
         const u64 key = i < n ? __ldg(mine + i) : 0ull;
         const bool take = key != 0ull && (key & mask) >= prefix;
         const unsigned int ballot = __ballot_sync(0xffffffffu, take);
@@ -355,7 +383,7 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(const unsigned l
     t.thr = &s_thr;
     t.cap = kSelectSort;
     t.k = k;
-    topk_flush_mask(t, 1u, kSelectThreads);  // sorts the selected keys; keeps min(count, k)
+    topk_flush_mask(t, 1u, kPickThreads);  // sorts the selected keys; keeps min(count, k)
     const bool short_list = !overflow && n < k && thr_key[q] != thr_safe[q];
     if ((overflow || short_list) && !final) {
         if (tid == 0) {
@@ -371,7 +399,7 @@ __global__ void __launch_bounds__(kSelectThreads) select_kernel(const unsigned l
         return;
     }
     if ((overflow || short_list) && tid == 0) atomicOr(status, kStatusOverflow);
-    topk_write(t, 0, out_idx + static_cast<size_t>(q) * k, out_scores + static_cast<size_t>(q) * k, kSelectThreads);
+    topk_write(t, 0, out_idx + static_cast<size_t>(q) * k, out_scores + static_cast<size_t>(q) * k, kPickThreads);
     if (tid == 0) done[q] = 1;
 }
 
@@ -687,7 +715,8 @@ int zcgvs_gemm_topk(const void* corpus, int dtype, const float* row_scales, int6
     }
     e = cudaGetLastError();
     if (e != cudaSuccess) return fail_cuda(e, "threshold_kernel launch");
-    e = ensure_smem_optin(reinterpret_cast<const void*>(select_kernel));
+    e = ensure_smem_optin(reinterpret_cast<const void*>(select_kernel<512>));
+    if (e == cudaSuccess) e = ensure_smem_optin(reinterpret_cast<const void*>(select_kernel<1024>));
     if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(select_kernel)");
 
     // Filter pass over the whole corpus and its selection, then the (usually empty) retry.
@@ -712,9 +741,15 @@ int zcgvs_gemm_topk(const void* corpus, int dtype, const float* row_scales, int6
         if (e != cudaSuccess) return fail_cuda(e, "bucket_kernel launch");
         {
             KernelTimer timer("gemm_select", st);
-            select_kernel<<<batch, kSelectThreads, 0, st>>>(
-                cand, cand_count, kCandCap, k, thr_key, thr_safe, done, retry, mneed, g.mtiles, p.status, pass,
-                out_indices, out_scores);
+            if (batch < device_sm_count()) {
+                select_kernel<1024><<<batch, 1024, 0, st>>>(cand, cand_count, kCandCap, k, thr_key, thr_safe, done,
+                                                            retry, mneed, g.mtiles, p.status, pass, out_indices,
+                                                            out_scores);
+            } else {
+                select_kernel<512><<<batch, 512, 0, st>>>(cand, cand_count, kCandCap, k, thr_key, thr_safe, done,
+                                                          retry, mneed, g.mtiles, p.status, pass, out_indices,
+                                                          out_scores);
+            }
         }
         e = cudaGetLastError();
         if (e != cudaSuccess) return fail_cuda(e, "select_kernel launch");

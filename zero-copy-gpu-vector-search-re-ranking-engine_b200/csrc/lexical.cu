@@ -76,6 +76,24 @@ __device__ long long lower_bound_warp(const int* __restrict__ docs, long long lo
     return lo + __popc(__ballot_sync(0xffffffffu, less));
 }
 
+// lower_bound_warp with a first round of 32 probes `step` apart around `guess` (where the target
+// would sit if the list's documents were spread evenly over [0, n)); the answer's side of that
+// window is then searched as usual. Exact for any sorted list; for evenly spread lists the
+// window holds the answer and about two dependent loads are saved per search.
+__device__ long long lower_bound_hint(const int* __restrict__ docs, long long lo, long long hi, int target,
+                                      long long guess, long long step, int lane) {
+    if (hi - lo > 64) {
+        const long long pos = min(max(guess + static_cast<long long>(lane - 16) * step, lo), hi - 1);
+        const bool less = __ldg(docs + pos) < target;  // a prefix of the lanes (positions ascend)
+        const int c = __popc(__ballot_sync(0xffffffffu, less));
+        const long long below = __shfl_sync(0xffffffffu, pos, max(c - 1, 0));
+        const long long at = __shfl_sync(0xffffffffu, pos, min(c, 31));
+        if (c > 0) lo = below + 1;   // docs[below] < target
+        if (c < 32) hi = at + 1;     // docs[at] >= target
+    }
+    return lower_bound_warp(docs, lo, hi, target, lane);
+}
+
 __global__ void __launch_bounds__(kLexThreads) lexical_kernel(const LexParams p) {
     extern __shared__ __align__(16) float acc[];
     __shared__ long long s_lo[kLexSlots];
@@ -105,8 +123,16 @@ __global__ void __launch_bounds__(kLexThreads) lexical_kernel(const LexParams p)
                 const long long begin = __ldg(p.offsets + term);
                 const long long end = __ldg(p.offsets + term + 1);
                 if (p.sorted) {
-                    lo = lower_bound_warp(p.docs, begin, end, static_cast<int>(d0), lane);
-                    hi = lower_bound_warp(p.docs, lo, end, static_cast<int>(d0 + count), lane);
+                    // Interpolated first probes: a window of +-16 steps covers about three standard
+                    // deviations of a randomly spread list's position (sqrt(df) / 2 at most).
+                    const long long df = end - begin;
+                    const double per_doc = static_cast<double>(df) / static_cast<double>(p.n);
+                    const long long step = 1 + static_cast<long long>(0.1 * sqrt(static_cast<double>(df)));
+                    lo = lower_bound_hint(p.docs, begin, end, static_cast<int>(d0),
+                                          begin + static_cast<long long>(per_doc * static_cast<double>(d0)), step, lane);
+                    hi = lower_bound_hint(p.docs, lo, end, static_cast<int>(d0 + count),
+                                          begin + static_cast<long long>(per_doc * static_cast<double>(d0 + count)), step,
+                                          lane);
                 } else {
                     lo = begin;
                     hi = end;
@@ -147,16 +173,21 @@ __global__ void __launch_bounds__(kLexThreads) lexical_kernel(const LexParams p)
             continue;
         }
         if (p.vec) {
-            // 16-byte posting groups, software-pipelined across slots. A step is two groups per
-            // thread of one slot (thread tid owns groups g0 + tid and g0 + kLexThreads + tid);
-            // the next step's loads are issued before this step's additions and before the
-            // barrier that closes a slot (loads never touch the accumulator), so a slot's memory
-            // latency overlaps the previous slot's work. Slots without postings here are skipped.
-            // A posting is the head of its run unless the posting before it (the same thread's,
-            // the previous lane's last one, or for lane 0 a load) holds the same document.
+            // 16-byte posting groups, software-pipelined across slots. A step is one group per
+            // thread of one slot (thread tid owns group g0 + tid); the loads of the next two steps
+            // are in flight while a step's additions run, across the barrier that closes a slot
+            // (loads never touch the accumulator), so a slot's memory latency overlaps the work
+            // of the slots before it. Slots without postings here are skipped. A posting is the
+            // head of its run unless the posting before it (the same thread's, the previous
+            // lane's last one, or for lane 0 a load) holds the same document.
             struct Step {
                 int t;
                 long long g0;
+            };
+            struct Group {
+                int4 dv;
+                float4 wv;
+                int before;
             };
             auto g_lo = [&](int t) { return s_lo[t] >> 2; };
             auto g_hi = [&](int t) { return (s_hi[t] + 3) >> 2; };
@@ -165,91 +196,74 @@ __global__ void __launch_bounds__(kLexThreads) lexical_kernel(const LexParams p)
                 return Step{t, t < slots ? g_lo(t) : 0};
             };
             auto advance = [&](Step c) {
-                const long long g0 = c.g0 + 2 * kLexThreads;
+                if (c.t >= slots) return c;
+                const long long g0 = c.g0 + kLexThreads;
                 return g0 < g_hi(c.t) ? Step{c.t, g0} : first_from(c.t + 1);
             };
-            auto load = [&](Step c, int4 (&dv)[2], float4 (&wv)[2], int (&before)[2]) {
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    dv[u] = make_int4(-1, -1, -1, -1);
-                    wv[u] = make_float4(0.f, 0.f, 0.f, 0.f);
-                    before[u] = -1;
-                }
+            auto load = [&](Step c, Group& b) {
+                b.dv = make_int4(-1, -1, -1, -1);
+                b.wv = make_float4(0.f, 0.f, 0.f, 0.f);
+                b.before = -1;
                 if (c.t >= slots) return;
-                const long long lo = s_lo[c.t];
-                const long long ghi = g_hi(c.t);
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    const long long g = c.g0 + u * kLexThreads + tid;
-                    if (g >= ghi) continue;
-                    if (4 * g + 3 < total) {
-                        dv[u] = __ldg(reinterpret_cast<const int4*>(p.docs) + g);
-                        wv[u] = __ldg(reinterpret_cast<const float4*>(p.weights) + g);
-                    } else {
-                        // The index's last partial group: element loads.
-                        int dd[4] = {-1, -1, -1, -1};
-                        float ww[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            if (4 * g + e < total) {
-                                dd[e] = __ldg(p.docs + 4 * g + e);
-                                ww[e] = __ldg(p.weights + 4 * g + e);
-                            }
-                        }
-                        dv[u] = make_int4(dd[0], dd[1], dd[2], dd[3]);
-                        wv[u] = make_float4(ww[0], ww[1], ww[2], ww[3]);
-                    }
-                    if (lane == 0 && 4 * g > lo) before[u] = __ldg(p.docs + 4 * g - 1);
-                }
-            };
-            auto process = [&](Step c, const int4 (&dv)[2], const float4 (&wv)[2], const int (&before)[2]) {
-                const long long lo = s_lo[c.t];
-                const long long hi = s_hi[c.t];
-                const long long ghi = g_hi(c.t);
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    const long long g = c.g0 + u * kLexThreads + tid;
-                    const int up = __shfl_up_sync(0xffffffffu, dv[u].w, 1);
-                    if (g >= ghi) continue;
-                    const int d[4] = {dv[u].x, dv[u].y, dv[u].z, dv[u].w};
-                    const float w[4] = {wv[u].x, wv[u].y, wv[u].z, wv[u].w};
-                    int prev = lane == 0 ? before[u] : up;
+                const long long g = c.g0 + tid;
+                if (g >= g_hi(c.t)) return;
+                if (4 * g + 3 < total) {
+                    b.dv = __ldg(reinterpret_cast<const int4*>(p.docs) + g);
+                    b.wv = __ldg(reinterpret_cast<const float4*>(p.weights) + g);
+                } else {
+                    // The index's last partial group: element loads.
+                    int dd[4] = {-1, -1, -1, -1};
+                    float ww[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
-                        const long long i = 4 * g + e;
-                        const int doc = d[e];
-                        const bool head = i >= lo && i < hi && (i == lo || prev != doc);
-                        prev = doc;
-                        if (!head) continue;
-                        float a = __fadd_rn(acc[doc - d0], w[e]);
-                        // The rest of a run of equal documents, in posting order (rare).
-                        for (long long j = i + 1; j < hi && __ldg(p.docs + j) == doc; ++j) {
-                            a = __fadd_rn(a, __ldg(p.weights + j));
+                        if (4 * g + e < total) {
+                            dd[e] = __ldg(p.docs + 4 * g + e);
+                            ww[e] = __ldg(p.weights + 4 * g + e);
                         }
-                        acc[doc - d0] = a;
                     }
+                    b.dv = make_int4(dd[0], dd[1], dd[2], dd[3]);
+                    b.wv = make_float4(ww[0], ww[1], ww[2], ww[3]);
+                }
+                if (lane == 0 && 4 * g > s_lo[c.t]) b.before = __ldg(p.docs + 4 * g - 1);
+            };
+            auto process = [&](Step c, const Group& b) {
+                const long long lo = s_lo[c.t];
+                const long long hi = s_hi[c.t];
+                const long long g = c.g0 + tid;
+                const int up = __shfl_up_sync(0xffffffffu, b.dv.w, 1);
+                if (g >= g_hi(c.t)) return;
+                const int d[4] = {b.dv.x, b.dv.y, b.dv.z, b.dv.w};
+                const float w[4] = {b.wv.x, b.wv.y, b.wv.z, b.wv.w};
+                int prev = lane == 0 ? b.before : up;
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                    const long long i = 4 * g + e;
+                    const int doc = d[e];
+                    const bool head = i >= lo && i < hi && (i == lo || prev != doc);
+                    prev = doc;
+                    if (!head) continue;
+                    float a = __fadd_rn(acc[doc - d0], w[e]);
+                    // The rest of a run of equal documents, in posting order (rare).
+                    for (long long j = i + 1; j < hi && __ldg(p.docs + j) == doc; ++j) {
+                        a = __fadd_rn(a, __ldg(p.weights + j));
+                    }
+                    acc[doc - d0] = a;
                 }
             };
-            Step cur = first_from(0);
-            int4 dv[2];
-            float4 wv[2];
-            int before[2];
-            load(cur, dv, wv, before);
-            while (cur.t < slots) {
-                const Step nxt = advance(cur);
-                int4 ndv[2];
-                float4 nwv[2];
-                int nbefore[2];
-                load(nxt, ndv, nwv, nbefore);
-                process(cur, dv, wv, before);
-                if (nxt.t != cur.t) __syncthreads();  // slot cur.t's additions land before the next slot's
-                cur = nxt;
-#pragma unroll
-                for (int u = 0; u < 2; ++u) {
-                    dv[u] = ndv[u];
-                    wv[u] = nwv[u];
-                    before[u] = nbefore[u];
-                }
+            Step s0 = first_from(0);
+            Step s1 = advance(s0);
+            Group b0, b1, b2;
+            load(s0, b0);
+            load(s1, b1);
+            while (s0.t < slots) {
+                const Step s2 = advance(s1);
+                load(s2, b2);
+                process(s0, b0);
+                if (s1.t != s0.t) __syncthreads();  // slot s0.t's additions land before the next slot's
+                s0 = s1;
+                s1 = s2;
+                b0 = b1;
+                b1 = b2;
             }
         } else {
             for (int t = 0; t < slots; ++t) {
