@@ -111,6 +111,34 @@ __device__ __forceinline__ bool mbar_try_wait(uint32_t bar_addr, uint32_t parity
     return done != 0u;
 }
 
+// try_wait with a suspend-time hint: a thread whose phase is not complete sleeps until it
+// completes or `hint_ns` passes, instead of re-issuing the test (the issue slots go to the
+// other warps of its scheduler).
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint32_t bar_addr, uint32_t parity, uint32_t hint_ns) {
+    uint32_t done;
+    asm volatile(
+        "{\n\t.reg .pred p;\n\t"
+        "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+        "selp.u32 %0, 1, 0, p;\n\t}"
+        : "=r"(done)
+        : "r"(bar_addr), "r"(parity), "r"(hint_ns)
+        : "memory");
+    return done != 0u;
+}
+
+// mbar_wait_bounded with sleeping tests (mbar_try_wait_sleep), the same budget.
+__device__ __forceinline__ bool mbar_wait_sleep_bounded(u64* bar, uint32_t parity, uint32_t* status, uint32_t flag) {
+    const uint32_t addr = smem_u32(bar);
+    if (mbar_try_wait(addr, parity)) return true;
+    const u64 start = global_timer_ns();
+    for (uint32_t spin = 0; spin < (1u << 28); ++spin) {
+        if (mbar_try_wait_sleep(addr, parity, 20000u)) return true;
+        if ((spin & 15u) == 0u && global_timer_ns() - start > kWaitBudgetNs) break;
+    }
+    if (status != nullptr) atomicOr(status, flag);
+    return false;
+}
+
 // Waits for phase `parity` of an mbarrier, giving up after kWaitBudgetNs. Returns false (and
 // sets `flag` in the device status word) when the wait ran out.
 __device__ __forceinline__ bool mbar_wait_bounded(u64* bar, uint32_t parity,

@@ -333,7 +333,7 @@ __global__ void __launch_bounds__(threads_of<MODE>(), 1)
                 const int n = static_cast<int>(w / p.mtiles);
                 for (int kb = 0; kb < p.kblocks; ++kb) {
                     if (issued >= S) {
-                        ok = !*abort_flag && mbar_wait_bounded(&empty[s], phase ^ 1u, p.status, kStatusTileWaitTimeout);
+                        ok = !*abort_flag && mbar_wait_sleep_bounded(&empty[s], phase ^ 1u, p.status, kStatusTileWaitTimeout);
                         if (!ok) {
                             *abort_flag = 1;
                             break;
@@ -375,7 +375,7 @@ __global__ void __launch_bounds__(threads_of<MODE>(), 1)
                 const int a = static_cast<int>(local & 1);
                 if (local >= 2) {
                     ok = !*abort_flag &&
-                         mbar_wait_bounded(&acc_empty[a], static_cast<uint32_t>(((local >> 1) - 1) & 1), p.status,
+                         mbar_wait_sleep_bounded(&acc_empty[a], static_cast<uint32_t>(((local >> 1) - 1) & 1), p.status,
                                            kStatusTmemWait);
                     if (!ok) {
                         *abort_flag = 1;
@@ -385,7 +385,7 @@ __global__ void __launch_bounds__(threads_of<MODE>(), 1)
                 tc_fence_after();
                 const uint32_t tmem_d = tmem_base + static_cast<uint32_t>(a * kBN);
                 for (int kb = 0; kb < p.kblocks; ++kb) {
-                    ok = !*abort_flag && mbar_wait_bounded(&full[s], phase, p.status, kStatusTileWaitTimeout);
+                    ok = !*abort_flag && mbar_wait_sleep_bounded(&full[s], phase, p.status, kStatusTileWaitTimeout);
                     if (!ok) {
                         *abort_flag = 1;
                         break;
@@ -591,7 +591,7 @@ __global__ void __launch_bounds__(threads_of<MODE>(), 1)
 
             bool ok = true;
             if (lane == 0) {
-                ok = !*abort_flag && mbar_wait_bounded(&acc_full[a], static_cast<uint32_t>((local >> 1) & 1), p.status,
+                ok = !*abort_flag && mbar_wait_sleep_bounded(&acc_full[a], static_cast<uint32_t>((local >> 1) & 1), p.status,
                                                        kStatusTmemWait);
                 if (!ok) *abort_flag = 1;
             }
