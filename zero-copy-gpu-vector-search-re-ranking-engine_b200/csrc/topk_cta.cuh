@@ -393,8 +393,8 @@ __device__ inline bool topk_merge_lists_rank(const TopkSmem& t, int q_local, con
 
 __device__ inline void topk_merge_lists(const TopkSmem& t, int q_local, const u64* src, int lists,
                                         int nthreads, u64* s_scratch /* >= 32 entries */) {
-    if (topk_merge_lists_small(t, q_local, src, lists, nthreads, s_scratch)) return;
     if (topk_merge_lists_rank(t, q_local, src, lists, nthreads, s_scratch)) return;
+    if (topk_merge_lists_small(t, q_local, src, lists, nthreads, s_scratch)) return;
     const int tid = threadIdx.x;
     const int k = t.k;
     const int j = (k + lists - 1) / lists - 1;
