@@ -797,15 +797,25 @@ class Cfg5(Workload):
         docs = self.index.docs.cpu().numpy()
         weights = self.index.weights.cpu().numpy()
         queries = self.queries.cpu().numpy()
+        from concurrent.futures import ThreadPoolExecutor
+
+        # One query per host thread at a time (the oracle's C loops run outside the GIL).
+        threads = os.cpu_count() or 1
+        oracle.lib()  # loaded once, before the threads
+
+        def one(i):
+            oracle.hybrid_topk(dense_bits, oracle.DTYPE_F16, self.D, queries[i:i + 1], self.K, self.offsets_h,
+                               docs, weights, self.V, self.terms_h[i:i + 1], 0.5, metric=oracle.METRIC_COSINE)
+
         done, t0 = 0, time.perf_counter()
-        while done < 64 and (done == 0 or time.perf_counter() - t0 < budget_s):
-            oracle.hybrid_topk(dense_bits, oracle.DTYPE_F16, self.D, queries[done:done + 1], self.K, self.offsets_h,
-                               docs, weights, self.V, self.terms_h[done:done + 1], 0.5,
-                               metric=oracle.METRIC_COSINE)
-            done += 1
+        with ThreadPoolExecutor(max_workers=threads) as pool:
+            while done + threads <= len(queries) and (done == 0 or time.perf_counter() - t0 < budget_s):
+                list(pool.map(one, range(done, done + threads)))
+                done += threads
         elapsed = time.perf_counter() - t0
-        return {"value": done / elapsed, "unit": UNIT, "cores": 1, "kind": "port",
-                "sample": f"{done} queries over the full corpus, oracle hybrid (reference loops restated), 1 thread",
+        return {"value": done / elapsed, "unit": UNIT, "cores": threads, "kind": "port",
+                "sample": f"{done} queries over the full corpus, oracle hybrid (reference loops restated), "
+                          f"{threads} threads, one query each",
                 "seconds": elapsed}
 
 
