@@ -157,6 +157,63 @@ __global__ void __launch_bounds__(kSelectThreads) threshold_kernel(const float* 
     }
 }
 
+// threshold_kernel for samples of at most kThrRegs * 32 chunks: one warp per query holds the
+// query's chunk maxima in registers (as orderable bits) and builds the r-th largest bit by bit
+// from the top, keeping a bit when at least r maxima are at or above the candidate; the same
+// bounds without a sort. Padding slots hold 0, below every float's orderable bits.
+constexpr int kThrRegs = 64;
+constexpr int kThrWarps = 2;  // small blocks: a 64-query batch spreads over 32 SMs
+
+__global__ void __launch_bounds__(kThrWarps * 32) threshold_regs_kernel(const float* __restrict__ chunk_max,
+                                                                        int chunks, int k, int batch,
+                                                                        unsigned long long* thr_key,
+                                                                        unsigned long long* thr_safe,
+                                                                        unsigned int* cand_count, int* done,
+                                                                        unsigned int* retry, unsigned int* mneed,
+                                                                        int mtiles) {
+    const int lane = threadIdx.x & 31;
+    const int q = blockIdx.x * kThrWarps + (threadIdx.x >> 5);
+    if (q >= batch) return;
+    const float* row = chunk_max + static_cast<size_t>(q) * chunks;
+    uint32_t v[kThrRegs];
+#pragma unroll
+    for (int j = 0; j < kThrRegs; ++j) {
+        const int i = j * 32 + lane;
+        v[j] = i < chunks ? orderable_bits(__ldg(row + i)) : 0u;
+    }
+    auto rth = [&](int r) -> uint32_t {
+        uint32_t t = 0u;
+        for (int bit = 31; bit >= 0; --bit) {
+            const uint32_t cand = t | (1u << bit);
+            int c = 0;
+#pragma unroll
+            for (int j = 0; j < kThrRegs; ++j) c += v[j] >= cand ? 1 : 0;
+            if (__reduce_add_sync(0xffffffffu, c) >= r) t = cand;
+        }
+        return t;
+    };
+    const uint32_t neg_inf = orderable_bits(-INFINITY);
+    auto bound = [&](int r) -> u64 {
+        if (chunks < r) return 0ull;
+        const uint32_t t = rth(r);
+        return t > neg_inf ? (static_cast<u64>(t) << 32) : 0ull;
+    };
+    const u64 safe = bound(k);
+    const u64 key = kStatRank < k ? max(bound(kStatRank), safe) : safe;
+    if (lane == 0) {
+        thr_safe[q] = safe;
+        thr_key[q] = key;
+        if (q < mtiles) {
+            for (int i = 0; i < kPasses; ++i) mneed[i * mtiles + q] = 0u;
+        }
+        cand_count[q] = 0u;
+        done[q] = 0;
+        if (q == 0) {
+            for (int i = 0; i < 2 * kPasses; ++i) retry[i] = 0u;  // retry requests, mailbox overflows
+        }
+    }
+}
+
 // Moves the mailbox entries of every filter epilogue warp (one mailbox segment per warp of
 // this kernel) into per-query candidate buffers. The lanes of a warp holding entries of the
 // same query take their slots with one atomic (few queries with many candidates each would
@@ -710,8 +767,13 @@ int zcgvs_gemm_topk(const void* corpus, int dtype, const float* row_scales, int6
     unsigned int* mneed = reinterpret_cast<unsigned int*>(ws + g.off_mneed);
     {
         KernelTimer timer("gemm_threshold", st);
-        threshold_kernel<<<batch, kSelectThreads, static_cast<size_t>(tcap) * 8, st>>>(
-            p.chunk_max, chunks, k, tcap, thr_key, thr_safe, cand_count, done, retry, mneed, g.mtiles);
+        if (chunks <= kThrRegs * 32) {
+            threshold_regs_kernel<<<(batch + kThrWarps - 1) / kThrWarps, kThrWarps * 32, 0, st>>>(
+                p.chunk_max, chunks, k, batch, thr_key, thr_safe, cand_count, done, retry, mneed, g.mtiles);
+        } else {
+            threshold_kernel<<<batch, kSelectThreads, static_cast<size_t>(tcap) * 8, st>>>(
+                p.chunk_max, chunks, k, tcap, thr_key, thr_safe, cand_count, done, retry, mneed, g.mtiles);
+        }
     }
     e = cudaGetLastError();
     if (e != cudaSuccess) return fail_cuda(e, "threshold_kernel launch");
