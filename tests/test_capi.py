@@ -77,3 +77,17 @@ def test_rescore_rejects_bad_arguments(zc, dtype, m, k, expect):
 def test_rescore_zero_sized_is_a_noop(zc):
     assert zc.lib().zcgvs_rescore_topk(None, 0, 1.0, None, 10, 8, None, 1, None, 0, 0, 5, None, None, None) == zc.OK
     assert zc.lib().zcgvs_gather_rescore(None, 0, 1.0, None, 10, 8, None, 0, None, 4, 0, None, None) == zc.OK
+
+
+def test_converters_check_arguments_before_touching_the_device(zc):
+    """Zero-sized conversions are no-ops; null pointers are INVALID_ARG (no device call either
+    way, so this runs without a GPU)."""
+    lib = zc.lib()
+    assert lib.zcgvs_convert_i8_rows(None, None, None, 0, 8, None) == zc.OK
+    assert lib.zcgvs_convert_i8_rows(None, None, None, 4, 0, None) == zc.OK
+    assert lib.zcgvs_convert_i8_rows(None, None, None, 4, 8, None) == zc.ERR_INVALID_ARG
+    assert "zcgvs_convert_i8_rows" in lib.zcgvs_last_error_message().decode()
+    assert lib.zcgvs_convert_i8(None, None, 0, 1.0, None) == zc.OK
+    assert lib.zcgvs_convert_i8(None, None, 16, 1.0, None) == zc.ERR_INVALID_ARG
+    assert lib.zcgvs_pack_binary(None, None, 0, 8, None) == zc.OK
+    assert lib.zcgvs_pack_binary(None, None, 3, 8, None) == zc.ERR_INVALID_ARG

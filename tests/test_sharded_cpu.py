@@ -161,3 +161,14 @@ def test_sharded_coarse_rescore_equals_single_corpus(tmp_path, world):
         got = np.load(f"{path}.{rank}.npz")
         np.testing.assert_array_equal(got["ids"], ref_i)
         np.testing.assert_array_equal(got["scores"], ref_s)
+
+
+def test_sharded_rescore_rejects_candidates_beyond_a_shard():
+    """m above a shard's rows (or k above m) is rejected before any exchange, as the reference
+    rejects k above the corpus (src/cuda/topk.cu:146-153)."""
+    import sharded
+
+    search = sharded.ShardedRescoreSearch(0, 100, lambda *a: None, lambda *a: None, merge=lambda *a: None)
+    for m, k in [(101, 10), (50, 51), (50, 0)]:
+        with pytest.raises(ValueError):
+            search.search(None, m, k)

@@ -95,6 +95,11 @@ class ShardedRescoreSearch:
     def search(self, queries, m: int, k: int):
         import torch
 
+        # Every shard returns m coarse candidates (the per-shard search, like the reference's
+        # top-k, rejects m above its row count), and the rescore keeps k of the m.
+        if not 0 < k <= m <= self.shard_end - self.shard_begin:
+            raise ValueError(f"sharded rescore search needs 0 < k <= m <= rows per shard; got k={k}, m={m}, "
+                             f"shard rows {self.shard_end - self.shard_begin}")
         ids, scores = self.coarse_search(queries, m, self.shard_begin)
         cand, _ = gather_merge(ids, scores, m, self.merge, self.group)
         mine = (cand >= self.shard_begin) & (cand < self.shard_end)
