@@ -851,7 +851,7 @@ def run_reference(args):
         return
     ref = ref_cpu()
     if ref is None:
-        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libzcgvs_refcpu.so was not built"}))
+        emit(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libzcgvs_refcpu.so was not built"}))
         return
     device = "cuda" if torch.cuda.is_available() else "cpu"
     import zcgvs_sm100 as zc
@@ -878,7 +878,7 @@ def run_reference(args):
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": min(threads, sample), "kind": "reference",
                              "sample": f"{sample} queries per step over the full corpus"},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line))
+    emit(json.dumps(line))
 
 
 def run_reference_sampled(args, wl, steps, warmup):
@@ -892,7 +892,7 @@ def run_reference_sampled(args, wl, steps, warmup):
     import zcgvs_sm100 as zc
 
     if ref_cpu() is None and not isinstance(wl, Cfg5):
-        print(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libzcgvs_refcpu.so was not built"}))
+        emit(json.dumps({"impl": "reference", "unavailable": "oracle/_ref/libzcgvs_refcpu.so was not built"}))
         return
     device = "cuda" if torch.cuda.is_available() else "cpu"
     wl.setup(torch, zc, device, 0, 1)  # the seeded inputs are generated on the device
@@ -912,7 +912,7 @@ def run_reference_sampled(args, wl, steps, warmup):
             "cpu_baseline": {"value": value, "unit": UNIT, "cores": last["cores"], "kind": last["kind"],
                              "sample": last["sample"]},
             "e2e": {"value": value, "unit": UNIT, "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
-    print(json.dumps(line))
+    emit(json.dumps(line))
 
 
 def run_ours(args):
@@ -1016,18 +1016,48 @@ def run_ours(args):
             "device_status": status,
             "cpu_baseline": cpu,
         }
-        print(json.dumps(line))
+        emit(json.dumps(line))
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
 
 
+_RESULT_FD = None
+
+
+def emit(text: str) -> None:
+    """Writes the run's one result line to the real standard output."""
+    sys.stdout.flush()
+    os.write(_RESULT_FD if _RESULT_FD is not None else 1, (text + "\n").encode())
+
+
+class StdoutToStderr:
+    """Sends everything else written to file descriptor 1 (Python prints and the libraries' own,
+    such as NCCL's version banner on rank 0) to stderr, so that standard output carries only the
+    result line that emit() writes."""
+
+    def __enter__(self):
+        global _RESULT_FD
+        sys.stdout.flush()
+        _RESULT_FD = os.dup(1)
+        os.dup2(2, 1)
+        return self
+
+    def __exit__(self, *exc):
+        global _RESULT_FD
+        sys.stdout.flush()
+        os.dup2(_RESULT_FD, 1)
+        os.close(_RESULT_FD)
+        _RESULT_FD = None
+
+
 def main():
     args = parse_args()
-    if args.impl == "reference":
-        run_reference(args)
-    else:
-        run_ours(args)
+    with StdoutToStderr():
+        if args.impl == "reference":
+            run_reference(args)
+        else:
+            run_ours(args)
 
 
 if __name__ == "__main__":
