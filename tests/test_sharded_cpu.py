@@ -76,8 +76,7 @@ def worker(rank, world, port, n, dim, batch, k, dtype, result_path):
         dist.destroy_process_group()
 
 
-@pytest.mark.parametrize("world", [2, 3])
-@pytest.mark.parametrize("dtype", [4, 0])
+@pytest.mark.parametrize("world,dtype", [(2, 4), (3, 4), (2, 0), (3, 0), (4, 3)])
 def test_sharded_search_equals_single_corpus(tmp_path, world, dtype):
     import torch.multiprocessing as mp
 
