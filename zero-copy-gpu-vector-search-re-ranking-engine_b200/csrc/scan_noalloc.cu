@@ -11,12 +11,20 @@
 //
 // Set-up: the first call on a device looks up that device's address of the array with
 // cudaGetSymbolAddress (with that device current) and caches it; that first call should
-// therefore come before any stream capture.
+// therefore come before any stream capture. The library's modules load lazily (CUDA's default
+// lazy loading), so the array is reserved on a device when that first lookup loads its module,
+// not when the library is loaded: a host that wants the reservation made at start-up, before
+// it takes the rest of the GPU's memory, calls zcgvs_scan_topk_noalloc_status (or this entry
+// point with a zero-sized problem) once per device then.
 //
 // Sharing: every call on a device uses the same array, which keeps the last call's contents.
 // Each call clears the part that must start at zero (status word and merge counters) on its
 // own stream before launching. Calls whose kernels overlap on the GPU (other streams, other
 // threads) race on the array; callers must serialise them.
+//
+// Status: the array's first 4 bytes are the status word every kernel of a call writes (a
+// bounded wait that ran out, a candidate buffer that overflowed; the ZCGVS_DEVICE_* bits).
+// zcgvs_scan_topk_noalloc_status copies it to the host after a call; the next call clears it.
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -64,7 +72,12 @@ int zcgvs_scan_topk_noalloc(const void* corpus, int dtype, float scale, const fl
                             int64_t doc_count, int dim, const float* queries, int batch,
                             const uint8_t* mask, int metric, int k, int id_base, int* out_indices,
                             float* out_scores, void* stream) {
-    if (doc_count <= 0 || batch <= 0 || dim <= 0) return zc::ok();
+    if (doc_count <= 0 || batch <= 0 || dim <= 0) {
+        // Nothing to search; the scratch address is still resolved, so a zero-sized call at
+        // start-up reserves the array on this device (see the set-up note above).
+        void* scratch = nullptr;
+        return scratch_address(&scratch);
+    }
     const size_t need = zcgvs_scan_topk_workspace_bytes(dtype, doc_count, dim, batch, k);
     if (need > kNoAllocScratchBytes) {
         return zc::fail(ZCGVS_ERR_INVALID_ARG,
@@ -82,6 +95,14 @@ int zcgvs_scan_topk_noalloc(const void* corpus, int dtype, float scale, const fl
     if (e != cudaSuccess) return zc::fail_cuda(e, "zcgvs_scan_topk_noalloc: clearing the scratch header");
     return zcgvs_scan_topk(corpus, dtype, scale, row_scales, doc_count, dim, queries, batch, mask, metric,
                            k, id_base, out_indices, out_scores, scratch, kNoAllocScratchBytes, stream);
+}
+
+int zcgvs_scan_topk_noalloc_status(uint32_t* status, void* stream) {
+    if (status == nullptr) return zc::fail(ZCGVS_ERR_INVALID_ARG, "zcgvs_scan_topk_noalloc_status: null status pointer");
+    void* scratch = nullptr;
+    const int rc = scratch_address(&scratch);
+    if (rc != ZCGVS_OK) return rc;
+    return zcgvs_workspace_status(scratch, kNoAllocScratchBytes, status, stream);
 }
 
 }  // extern "C"
