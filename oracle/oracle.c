@@ -14,6 +14,7 @@
 
 #include <float.h>
 #include <math.h>
+#include <pthread.h>
 #include <stdlib.h>
 #include <string.h>
 
@@ -151,16 +152,17 @@ int orc_hamming(const uint32_t* a, const uint32_t* b, int words) {
  *   I8_ROW: float(int32 dot of per-row-quantised query and row) * s_query * s_row.
  *   mask[i] == 0 -> -FLT_MAX (src/cuda/similarity.cu:109-113).
  * --------------------------------------------------------------------------------------- */
-static void scores_one(int dtype, const void* corpus, float scale, const float* row_scales,
-                       int64_t n, int dim, const float* query, const uint8_t* mask, int metric,
-                       float* out) {
+/* Scores of rows [i0, i1) of the corpus (out indexed by row). */
+static void scores_rows(int dtype, const void* corpus, float scale, const float* row_scales,
+                        int64_t i0, int64_t n, int dim, const float* query, const uint8_t* mask, int metric,
+                        float* out) {
     const int l2 = (metric == ORC_METRIC_L2);
     if (dtype == ORC_DTYPE_BINARY) {
         const int words = (dim + 31) / 32;
         uint32_t* qbits = (uint32_t*)calloc((size_t)words, sizeof(uint32_t));
         orc_pack_binary(query, 1, dim, qbits);
         const uint32_t* codes = (const uint32_t*)corpus;
-        for (int64_t i = 0; i < n; ++i) {
+        for (int64_t i = i0; i < n; ++i) {
             const int h = orc_hamming(codes + (size_t)i * (size_t)words, qbits, words);
             out[i] = (float)(dim - 2 * h) / (float)dim;
         }
@@ -170,7 +172,7 @@ static void scores_one(int dtype, const void* corpus, float scale, const float* 
         float qs = 0.0f;
         orc_quantize_rows_i8(query, 1, dim, qq, &qs);
         const int8_t* rows = (const int8_t*)corpus;
-        for (int64_t i = 0; i < n; ++i) {
+        for (int64_t i = i0; i < n; ++i) {
             const int8_t* x = rows + (size_t)i * (size_t)dim;
             int32_t dot = 0;
             for (int j = 0; j < dim; ++j) dot += (int32_t)x[j] * (int32_t)qq[j];
@@ -179,7 +181,7 @@ static void scores_one(int dtype, const void* corpus, float scale, const float* 
         }
         free(qq);
     } else {
-        for (int64_t i = 0; i < n; ++i) {
+        for (int64_t i = i0; i < n; ++i) {
             float acc = 0.0f;
             for (int j = 0; j < dim; ++j) {
                 float x;
@@ -202,9 +204,59 @@ static void scores_one(int dtype, const void* corpus, float scale, const float* 
         }
     }
     if (mask != NULL) {
-        for (int64_t i = 0; i < n; ++i) {
+        for (int64_t i = i0; i < n; ++i) {
             if (mask[i] == 0) out[i] = -FLT_MAX;
         }
+    }
+}
+
+/* Host threads scores_one may use (orc_set_threads; 1 by default). Rows are scored
+ * independently, so the thread count changes no arithmetic: every score is the same sequential
+ * sum whatever the split. */
+static int g_threads = 1;
+
+void orc_set_threads(int threads) { g_threads = threads > 1 ? (threads < 256 ? threads : 256) : 1; }
+
+struct rows_job {
+    int dtype, dim, metric;
+    const void* corpus;
+    float scale;
+    const float* row_scales;
+    int64_t i0, i1;
+    const float* query;
+    const uint8_t* mask;
+    float* out;
+};
+
+static void* rows_job_run(void* arg) {
+    const struct rows_job* j = (const struct rows_job*)arg;
+    scores_rows(j->dtype, j->corpus, j->scale, j->row_scales, j->i0, j->i1, j->dim, j->query, j->mask, j->metric,
+                j->out);
+    return NULL;
+}
+
+static void scores_one(int dtype, const void* corpus, float scale, const float* row_scales,
+                       int64_t n, int dim, const float* query, const uint8_t* mask, int metric,
+                       float* out) {
+    const int threads = (g_threads > 1 && n >= 65536) ? g_threads : 1;
+    if (threads == 1) {
+        scores_rows(dtype, corpus, scale, row_scales, 0, n, dim, query, mask, metric, out);
+        return;
+    }
+    pthread_t tid[256];
+    int spawned[256];
+    struct rows_job jobs[256];
+    for (int t = 0; t < threads; ++t) {
+        const struct rows_job j = {dtype, dim, metric, corpus, scale, row_scales, n * t / threads,
+                                   n * (t + 1) / threads, query, mask, out};
+        jobs[t] = j;
+        spawned[t] = t > 0 && pthread_create(&tid[t], NULL, rows_job_run, &jobs[t]) == 0;
+    }
+    for (int t = 0; t < threads; ++t) {
+        if (!spawned[t]) rows_job_run(&jobs[t]);  /* the calling thread, or a thread that failed to start */
+    }
+    for (int t = 1; t < threads; ++t) {
+        if (spawned[t]) pthread_join(tid[t], NULL);
     }
 }
 

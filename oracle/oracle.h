@@ -16,6 +16,7 @@ extern "C" {
 enum { ORC_DTYPE_F32 = 0, ORC_DTYPE_F16 = 1, ORC_DTYPE_I8 = 2, ORC_DTYPE_BINARY = 3, ORC_DTYPE_I8_ROW = 4 };
 enum { ORC_METRIC_COSINE = 0, ORC_METRIC_DOT = 1, ORC_METRIC_L2 = 2 };
 
+void orc_set_threads(int threads);
 uint16_t orc_f32_to_f16(float value);
 float orc_f16_to_f32(uint16_t h);
 void orc_convert_f16(const float* src, size_t count, uint16_t* dst);

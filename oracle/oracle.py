@@ -27,15 +27,28 @@ _lib = None
 _ref = None
 
 
+def reference_root() -> Path | None:
+    """The reference checkout: $ZCGVS_REFERENCE, else a `reference` directory beside this
+    repository; None when neither holds the reference's tests/cpp (e.g. on a GPU box, which
+    uses the prebuilt oracle/_ref)."""
+    env = os.environ.get("ZCGVS_REFERENCE")
+    candidates = [Path(env)] if env else [HERE.parents[1] / "reference"]
+    for path in candidates:
+        if (path / "tests" / "cpp").is_dir():
+            return path.resolve()
+    return None
+
+
 def build() -> None:
-    """Compiles liboracle.so (gcc) and, when the reference tree is present, the reference CPU
-    library and (once the CUDA library is built) the reference's C++ test programs linked
-    against it."""
+    """Compiles liboracle.so and, when the reference checkout is found (reference_root), the
+    reference CPU library and (once the CUDA library is built) the reference's C++ programs
+    linked against it."""
     subprocess.run(["make", "-s", "-C", str(HERE), "liboracle.so"], check=True)
-    if Path(os.environ.get("ZCGVS_REFERENCE", "/root/reference"), "tests", "cpp").is_dir():
-        subprocess.run(["make", "-s", "-C", str(HERE), "ref"], check=True)
+    ref = reference_root()
+    if ref is not None:
+        subprocess.run(["make", "-s", "-C", str(HERE), "ref", f"REF={ref}"], check=True)
         if (HERE.parent / "zero-copy-gpu-vector-search-re-ranking-engine_b200" / "libzcgvs_sm100.so").exists():
-            subprocess.run(["make", "-s", "-j8", "-C", str(HERE), "reftests"], check=True)
+            subprocess.run(["make", "-s", "-j8", "-C", str(HERE), "reftests", f"REF={ref}"], check=True)
 
 
 def lib():
@@ -45,6 +58,7 @@ def lib():
             build()
         _lib = ctypes.CDLL(str(LIB_PATH))
         i64, i32, f32, u32 = ctypes.c_int64, ctypes.c_int, ctypes.c_float, ctypes.c_uint32
+        _lib.orc_set_threads.argtypes = [i32]
         _lib.orc_f32_to_f16.restype = ctypes.c_uint16
         _lib.orc_f32_to_f16.argtypes = [f32]
         _lib.orc_convert_f16.argtypes = [_P, ctypes.c_size_t, _P]
@@ -88,6 +102,12 @@ def ref_lib():
         _ref.refcpu_search.restype = ctypes.c_double
         _ref.refcpu_search.argtypes = [_P, i32, i32, _P, i32, i32, i32, _P]
     return _ref
+
+
+def set_threads(threads: int) -> None:
+    """Host threads for the oracle's row loops (1 = sequential, the default). Rows are scored
+    independently, so the results do not depend on it."""
+    lib().orc_set_threads(int(threads))
 
 
 def _ptr(a: np.ndarray | None):
