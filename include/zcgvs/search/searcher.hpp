@@ -33,6 +33,10 @@ public:
     void setLexicalIndex(const LexicalIndex* index);
 
     void search(const float* host_queries, int dim, int batch, const SearchParams& params, const CudaStream& stream);
+    // Copies the last search's result to the host (synchronising `stream`). Throws
+    // std::runtime_error when the search's kernels left a non-zero device status word (a bounded
+    // wait ran out, or a query of the tensor-core path kept more candidates than its buffer
+    // holds): the result may be incomplete. The word is cleared first, so the next search runs.
     HostTopK copyResultToHost(const CudaStream& stream);
 
     int resultK() const { return current_k_; }
@@ -86,6 +90,7 @@ private:
     PinnedBuffer<int> h_query_terms_;
     PinnedBuffer<int> h_out_indices_;
     PinnedBuffer<float> h_out_values_;
+    PinnedBuffer<std::uint32_t> h_status_;  // the workspace's device status word, read with each result
 
     cudaEvent_t ev_start_ = nullptr;
     cudaEvent_t ev_end_ = nullptr;

@@ -83,9 +83,33 @@ int zcgvs_last_cuda_error(void);
 /* Zero-fills `bytes` of a workspace on `stream` (a cudaMemsetAsync). */
 int zcgvs_workspace_init(void* workspace, size_t bytes, void* stream);
 
+/* Bits of the device status word that kernels set in the first 4 bytes of a workspace
+ * (sticky: they stay set until the caller clears them, e.g. with zcgvs_workspace_init).
+ * A non-zero word means the results of the calls since it was last cleared may be incomplete. */
+#define ZCGVS_DEVICE_TILE_WAIT_TIMEOUT 0x1u  /* a bounded wait for a corpus tile ran out */
+#define ZCGVS_DEVICE_DRAIN_TIMEOUT 0x2u      /* a bounded wait for in-flight copies ran out */
+#define ZCGVS_DEVICE_TMEM_WAIT_TIMEOUT 0x4u  /* a tensor-memory accumulator hand-off ran out */
+#define ZCGVS_DEVICE_CANDIDATE_OVERFLOW 0x8u /* a query of the tensor-core path kept more
+                                                candidates than its buffer holds after every
+                                                retry; its top-k is incomplete */
+
 /* Copies the device status word of a workspace to *status and synchronises `stream`.
- * 0 means every bounded wait of every call that used the workspace completed. */
+ * 0 means every bounded wait of every call that used the workspace completed and no
+ * candidate buffer overflowed (ZCGVS_DEVICE_* bits above otherwise). */
 int zcgvs_workspace_status(const void* workspace, size_t bytes, uint32_t* status, void* stream);
+
+/* Test hook (no reference counterpart): caps the per-query candidate buffer of the tensor-core
+ * path (zcgvs_gemm_topk, and zcgvs_scan_topk where it dispatches there) at `cap` entries instead
+ * of 16384, so tests can drive a query past its buffer and check that the overflow reaches the
+ * caller. 0 restores the default; 1..16384 are accepted. Process-wide; not for production use. */
+int zcgvs_test_set_candidate_cap(int cap);
+
+/* Diagnostic (no reference counterpart): launches one warp that waits on a shared-memory
+ * barrier nothing ever completes, through the same bounded wait every kernel of this library
+ * uses. The wait gives up after its 2 s budget, sets ZCGVS_DEVICE_TILE_WAIT_TIMEOUT in the
+ * workspace status word and the kernel returns normally: the failure path a caller sees when a
+ * real wait runs out, exercised without faulting or hanging the GPU. */
+int zcgvs_check_bounded_wait(void* workspace, size_t bytes, void* stream);
 
 /* Diagnostics (no reference counterpart): CUDA-event timing of the library's main kernel
  * launches, off by default. zcgvs_kernel_timing(1) clears earlier records and starts recording
@@ -200,9 +224,12 @@ int zcgvs_gather_rescore(const void* store, int dtype, float scale, const float*
  * zcgvs_gemm_topk: a threshold pre-pass over a sample of document tiles (per query, the k-th
  * largest tile maximum, a lower bound of the k-th best score), a filtered pass over the whole
  * corpus that keeps only documents at or above it, and an exact selection of those candidates.
- * Arguments and result as zcgvs_scan_topk. A query with more than 16384 candidates at its
- * threshold sets bit 8 of the workspace status word (zcgvs_workspace_status); its result is
- * then incomplete. The workspace must be 256-byte aligned; it needs no zero-fill.
+ * Arguments and result as zcgvs_scan_topk. A query still holding more than 16384 candidates
+ * at its threshold after both retries sets ZCGVS_DEVICE_CANDIDATE_OVERFLOW (value 8, bit 3) in
+ * the workspace status word (zcgvs_workspace_status); its result is then incomplete. The
+ * workspace must be 256-byte aligned; apart from its status word (the first 4 bytes: zero
+ * them once, and again after reading a non-zero value, since the bits are sticky) it needs no
+ * zero-fill.
  *
  * zcgvs_gemm_similarity: the [batch, doc_count] score matrix (masked documents -FLT_MAX).
  * --------------------------------------------------------------------------------------- */

@@ -10,6 +10,10 @@
 //     queries=<raw f32 [batch, dim]> batch=<B> dim=<d> k=<k> metric=<0|1|2>
 //     [rescore=<zcve> m=<candidates>] [index=<zcvl> terms=<raw i32 [batch, stride]> stride=<s>
 //     weight=<dense weight>] [graph=1]  out=<prefix>  -> <prefix>.ids, <prefix>.scores
+//     [cap=<n>]                  lower the tensor-core path's candidate buffer to n entries
+//                                (zcgvs_test_set_candidate_cap) for the search; on the
+//                                exception it raises, restore the default and search again,
+//                                printing "recovered" when the Searcher's next result is clean
 // Exit status 0 on success; a thrown exception prints its message and exits 1.
 #include <cstdint>
 #include <cstdio>
@@ -25,6 +29,7 @@
 #include "zcgvs/data/embedding_store.hpp"
 #include "zcgvs/data/lexical_index.hpp"
 #include "zcgvs/search/searcher.hpp"
+#include "zcgvs_sm100.h"
 
 namespace {
 
@@ -97,6 +102,25 @@ int main(int argc, char** argv) {
         const auto queries = read_raw<float>(a["queries"], static_cast<std::size_t>(batch) * dim);
         zcgvs::CudaStream stream;
         zcgvs::HostTopK result;
+        if (a.count("cap")) {
+            if (zcgvs_test_set_candidate_cap(static_cast<int>(num("cap", 0))) != ZCGVS_OK) {
+                throw std::runtime_error(zcgvs_last_error_message());
+            }
+            try {
+                searcher.search(queries.data(), dim, batch, params, stream);
+                result = searcher.copyResultToHost(stream);
+            } catch (const std::runtime_error& e) {
+                zcgvs_test_set_candidate_cap(0);
+                std::cerr << "store_search: " << e.what() << "\n";
+                searcher.search(queries.data(), dim, batch, params, stream);
+                result = searcher.copyResultToHost(stream);
+                std::printf("recovered\n");
+                write_raw(a["out"] + ".ids", result.indices);
+                write_raw(a["out"] + ".scores", result.scores);
+                return 1;
+            }
+            zcgvs_test_set_candidate_cap(0);
+        }
         for (int pass = 0; pass < (params.use_graph ? 3 : 1); ++pass) {  // capture, then replays
             searcher.search(queries.data(), dim, batch, params, stream);
             result = searcher.copyResultToHost(stream);

@@ -91,3 +91,22 @@ def test_converters_check_arguments_before_touching_the_device(zc):
     assert lib.zcgvs_convert_i8(None, None, 16, 1.0, None) == zc.ERR_INVALID_ARG
     assert lib.zcgvs_pack_binary(None, None, 0, 8, None) == zc.OK
     assert lib.zcgvs_pack_binary(None, None, 3, 8, None) == zc.ERR_INVALID_ARG
+
+
+def test_status_readers_and_test_hooks_check_arguments(zc):
+    """The no-alloc status reader, the candidate-cap test hook and the bounded-wait diagnostic
+    reject bad arguments before touching a device."""
+    lib = zc.lib()
+    assert lib.zcgvs_scan_topk_noalloc_status(None, None) == zc.ERR_INVALID_ARG
+    assert "null status pointer" in lib.zcgvs_last_error_message().decode()
+    for cap in (-1, 16385):
+        assert lib.zcgvs_test_set_candidate_cap(cap) == zc.ERR_INVALID_ARG
+    assert lib.zcgvs_test_set_candidate_cap(0) == zc.OK
+    assert lib.zcgvs_check_bounded_wait(None, 256, None) == zc.ERR_INVALID_ARG
+    assert lib.zcgvs_workspace_status(None, 0, None, None) == zc.ERR_INVALID_ARG
+
+
+def test_device_status_text_names_every_bit(zc):
+    text = zc.describe_device_status(zc.DEVICE_CANDIDATE_OVERFLOW | zc.DEVICE_TILE_WAIT_TIMEOUT)
+    assert "0x9" in text and "corpus tile" in text and "more candidates" in text
+    assert "unknown bits 0x20" in zc.describe_device_status(0x20)

@@ -69,10 +69,10 @@ def test_reference_written_files_search_like_the_oracle(driver, orc, tmp_path, d
         np.testing.assert_allclose(scores, ref_s, rtol=0, atol=1e-5)
 
 
-@pytest.mark.parametrize("n,dim,batch", [(3000, 384, 3), (200_000, 256, 2), (20_000, 768, 64)])
+@pytest.mark.parametrize("n,dim,batch", [(3000, 384, 3), (200_000, 256, 2), (70_000, 768, 64)])
 def test_version3_per_row_file_searches_like_the_oracle(driver, orc, tmp_path, n, dim, batch):
-    """Per-row int8 from a version-3 file; 200K x 256 streams in two pinned chunks; batch 64 takes
-    the tensor-core path. Integer dots: bit-exact."""
+    """Per-row int8 from a version-3 file; 200K x 256 streams in two pinned chunks; batch 64 over
+    70K rows takes the tensor-core path. Integer dots: bit-exact."""
     corpus = orc.normal_rows(n, dim, 300 + dim)
     path = tmp_path / "c.zcve"
     formats.write_embeddings(path, corpus, normalized=True, dtype="int8_row")
@@ -132,3 +132,31 @@ def test_loader_rejects_per_row_dtype_in_version2_and_short_files(driver, orc, t
     short.write_bytes(path.read_bytes()[:-3])
     err = run(driver, tmp_path, orc.normal_rows(1, 32, 6), 5, corpus=short, expect_ok=False)
     assert "ends early" in err
+
+
+def test_searcher_throws_when_candidates_overflow_and_recovers(driver, orc, tmp_path):
+    """A query of the tensor-core path whose candidates overflow its buffer after every retry gets
+    an incomplete top-k; the Searcher reads the device status word with the result and throws
+    std::runtime_error instead of returning it. The test hook caps the buffer at 5 entries for
+    k = 10 (a host-side setting: no device fault is involved). The driver then restores the
+    default cap and searches again with the same Searcher: the word was cleared, the result is
+    the oracle's."""
+    n, dim, batch, k = 70_000, 256, 64, 10
+    corpus = orc.normal_rows(n, dim, 4242)
+    path = tmp_path / "c.zcve"
+    formats.write_embeddings(path, corpus, normalized=True, dtype="int8_row")
+    queries = orc.normal_rows(batch, dim, 4243)
+    qpath = tmp_path / "q.f32"
+    queries.tofile(qpath)
+    res = subprocess.run([str(driver), f"queries={qpath}", f"batch={batch}", f"dim={dim}", f"k={k}", "metric=1",
+                          f"out={tmp_path / 'r'}", f"corpus={path}", "cap=5"], capture_output=True, text=True,
+                         timeout=300)
+    assert res.returncode == 1, res.stdout + res.stderr
+    assert "search incomplete" in res.stderr and "more candidates than its buffer holds" in res.stderr, res.stderr
+    assert "recovered" in res.stdout
+    ids = np.fromfile(tmp_path / "r.ids", dtype=np.int32).reshape(batch, k)
+    scores = np.fromfile(tmp_path / "r.scores", dtype=np.float32).reshape(batch, k)
+    q, s = orc.quantize_rows_i8(corpus)
+    ref_i, ref_s = orc.scan_topk(q, orc.DTYPE_I8_ROW, dim, queries, k, row_scales=s)
+    np.testing.assert_array_equal(ids, ref_i)
+    np.testing.assert_array_equal(scores, ref_s)

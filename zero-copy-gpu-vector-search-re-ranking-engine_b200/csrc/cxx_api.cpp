@@ -6,19 +6,24 @@
 
 #include <algorithm>
 #include <cstdint>
+#include <cstdio>
 #include <cstring>
 #include <fstream>
 #include <numeric>
 #include <stdexcept>
 #include <string>
+#include <utility>
 #include <vector>
 
 #include "zcgvs/core/cuda_check.hpp"
+#include "zcgvs/core/cuda_context.hpp"
 #include "zcgvs/cuda/convert.cuh"
 #include "zcgvs/cuda/lexical.cuh"
 #include "zcgvs/cuda/rescore.cuh"
 #include "zcgvs/cuda/similarity.cuh"
 #include "zcgvs/cuda/topk.cuh"
+#include "zcgvs/data/binary_format.hpp"
+#include "zcgvs/data/corpus.hpp"
 #include "zcgvs/data/embedding_store.hpp"
 #include "zcgvs/data/lexical_index.hpp"
 #include "zcgvs/search/searcher.hpp"
@@ -37,6 +42,27 @@ void check(int status, const char* call) {
         throw CudaError(code != 0 ? static_cast<cudaError_t>(code) : cudaErrorUnknown, call, __FILE__, __LINE__);
     }
     throw std::runtime_error(message);
+}
+
+// Text of the device status word's bits (ZCGVS_DEVICE_* in zcgvs_sm100.h).
+std::string describeDeviceStatus(std::uint32_t word) {
+    static const std::pair<std::uint32_t, const char*> kBits[] = {
+        {ZCGVS_DEVICE_TILE_WAIT_TIMEOUT, "a bounded wait for a corpus tile ran out"},
+        {ZCGVS_DEVICE_DRAIN_TIMEOUT, "a bounded wait for in-flight copies ran out"},
+        {ZCGVS_DEVICE_TMEM_WAIT_TIMEOUT, "a tensor-memory accumulator hand-off ran out"},
+        {ZCGVS_DEVICE_CANDIDATE_OVERFLOW, "a query kept more candidates than its buffer holds (its top-k is incomplete)"},
+    };
+    char hex[16];
+    std::snprintf(hex, sizeof(hex), "0x%x", word);
+    std::string text = std::string("device status ") + hex + ":";
+    std::uint32_t known = 0u;
+    for (const auto& bit : kBits) {
+        known |= bit.first;
+        if ((word & bit.first) != 0u) text += std::string(" ") + bit.second + ";";
+    }
+    if ((word & ~known) != 0u) text += " unknown bits;";
+    text.pop_back();
+    return text;
 }
 
 // Per-query staging limit of the reference's similarity launcher (src/cuda/similarity.cu:23):
@@ -61,10 +87,15 @@ public:
         in_.read(static_cast<char*>(dst), static_cast<std::streamsize>(count));
         if (!in_) throw std::runtime_error("zcgvs: '" + path_ + "' ends early");
     }
-    void magic(const char (&expected)[5]) {
+    void magic(const char (&expected)[4]) {
         char got[4];
         bytes(got, 4);
         if (std::memcmp(got, expected, 4) != 0) throw std::runtime_error("zcgvs: '" + path_ + "' has the wrong magic");
+    }
+    std::string text(std::size_t length) {
+        std::string value(length, '\0');
+        if (length > 0) bytes(value.data(), length);
+        return value;
     }
     // Streams `count` bytes of the file into device memory through two pinned chunks: the read
     // of one chunk overlaps the host-to-device copy of the other, and no host copy of the whole
@@ -277,22 +308,24 @@ EmbeddingStore EmbeddingStore::fromHostMatrix(const float* host_float32, std::in
 
 EmbeddingStore EmbeddingStore::loadFromFile(const std::string& path) {
     Reader in(path);
-    in.magic("ZCVE");
+    in.magic(kEmbeddingMagic);
     const auto version = in.scalar<std::uint32_t>();
-    if (version == 0 || version > 3) throw std::runtime_error("zcgvs: unsupported embedding file version " + std::to_string(version));
+    if (version == 0 || version > kEmbeddingVersionRowScales) {
+        throw std::runtime_error("zcgvs: unsupported embedding file version " + std::to_string(version));
+    }
     const auto flags = in.scalar<std::uint32_t>();
     const auto doc_count = in.scalar<std::int64_t>();
     const auto dim = in.scalar<std::int32_t>();
     const auto code = in.scalar<std::int32_t>();
     if (doc_count <= 0 || dim <= 0) throw std::runtime_error("zcgvs: embedding file reports an empty matrix");
     if (code < 0 || code > 4) throw std::runtime_error("zcgvs: unsupported embedding dtype code " + std::to_string(code));
-    if (code == static_cast<std::int32_t>(ScalarType::Int8PerRow) && version < 3) {
+    if (code == kDtypeInt8PerRow && version < kEmbeddingVersionRowScales) {
         throw std::runtime_error("zcgvs: per-row int8 embeddings require file version 3");
     }
     EmbeddingStore store;
     store.dim_ = dim;
     store.dtype_ = static_cast<ScalarType>(code);
-    store.normalized_ = (flags & 1u) != 0;
+    store.normalized_ = (flags & kFlagNormalized) != 0;
     std::size_t stride = store.rowStride();
     if (version >= 2) {
         store.scale_ = in.scalar<float>();
@@ -389,9 +422,9 @@ LexicalIndex LexicalIndex::fromHostCsr(const std::int64_t* offsets, int vocab_si
 
 LexicalIndex LexicalIndex::loadFromFile(const std::string& path) {
     Reader in(path);
-    in.magic("ZCVL");
+    in.magic(kLexicalMagic);
     const auto version = in.scalar<std::uint32_t>();
-    if (version != 1) throw std::runtime_error("zcgvs: unsupported lexical index version " + std::to_string(version));
+    if (version != kLexicalVersion) throw std::runtime_error("zcgvs: unsupported lexical index version " + std::to_string(version));
     const auto doc_count = in.scalar<std::int64_t>();
     const auto vocab = in.scalar<std::int32_t>();
     const auto nnz = in.scalar<std::int64_t>();
@@ -409,6 +442,75 @@ LexicalIndex LexicalIndex::loadFromFile(const std::string& path) {
         in.bytes(weights.data(), weights.size() * sizeof(float));
     }
     return fromHostCsr(offsets.data(), vocab, docs.data(), weights.data(), doc_count, k1, b, avgdl);
+}
+
+// ------------------------------------------------------------------------------------------
+// Corpus: embeddings + ZCVM metadata
+// ------------------------------------------------------------------------------------------
+Corpus Corpus::load(const std::string& embeddings_path, const std::string& metadata_path) {
+    Corpus corpus;
+    corpus.embeddings_ = EmbeddingStore::loadFromFile(embeddings_path);
+    Reader in(metadata_path);
+    in.magic(kMetadataMagic);
+    const auto version = in.scalar<std::uint32_t>();
+    if (version != kMetadataVersion) throw std::runtime_error("zcgvs: unsupported metadata version " + std::to_string(version));
+    const auto count = in.scalar<std::int64_t>();
+    if (count != corpus.embeddings_.docCount()) {
+        throw std::runtime_error("zcgvs: metadata lists " + std::to_string(count) + " documents, the embeddings " +
+                                 std::to_string(corpus.embeddings_.docCount()));
+    }
+    corpus.doc_ids_.reserve(static_cast<std::size_t>(count));
+    corpus.texts_.reserve(static_cast<std::size_t>(count));
+    for (std::int64_t i = 0; i < count; ++i) {
+        corpus.doc_ids_.push_back(in.text(in.scalar<std::uint32_t>()));
+        corpus.texts_.push_back(in.text(in.scalar<std::uint32_t>()));
+    }
+    return corpus;
+}
+
+void Corpus::addDocuments(const std::vector<std::string>& ids, const std::vector<std::string>& texts,
+                          const float* host_float32, std::int64_t add_count, cudaStream_t stream) {
+    if (static_cast<std::int64_t>(ids.size()) != add_count || static_cast<std::int64_t>(texts.size()) != add_count) {
+        throw std::runtime_error("zcgvs: addDocuments needs one id and one text per added row");
+    }
+    if (add_count <= 0) return;
+    embeddings_.append(host_float32, add_count, stream);
+    doc_ids_.insert(doc_ids_.end(), ids.begin(), ids.end());
+    texts_.insert(texts_.end(), texts.begin(), texts.end());
+}
+
+// ------------------------------------------------------------------------------------------
+// Device context
+// ------------------------------------------------------------------------------------------
+void setDevice(int device_id) { ZCGVS_CUDA_CHECK(cudaSetDevice(device_id)); }
+
+int currentDevice() {
+    int device = 0;
+    ZCGVS_CUDA_CHECK(cudaGetDevice(&device));
+    return device;
+}
+
+int deviceCount() {
+    int count = 0;
+    ZCGVS_CUDA_CHECK(cudaGetDeviceCount(&count));
+    return count;
+}
+
+DeviceInfo queryDevice(int device_id) {
+    cudaDeviceProp prop{};
+    ZCGVS_CUDA_CHECK(cudaGetDeviceProperties(&prop, device_id));
+    int memory_khz = 0;  // an attribute: the property field is gone from newer runtimes
+    ZCGVS_CUDA_CHECK(cudaDeviceGetAttribute(&memory_khz, cudaDevAttrMemoryClockRate, device_id));
+    DeviceInfo info;
+    info.device_id = device_id;
+    info.name = prop.name;
+    info.total_memory = prop.totalGlobalMem;
+    info.compute_major = prop.major;
+    info.compute_minor = prop.minor;
+    info.multiprocessor_count = prop.multiProcessorCount;
+    info.memory_clock_khz = memory_khz;
+    info.memory_bus_width_bits = prop.memoryBusWidth;
+    return info;
 }
 
 // ------------------------------------------------------------------------------------------
@@ -528,6 +630,7 @@ void Searcher::ensureCapacity(std::int64_t doc_count, int batch, const SearchPar
     grow(h_queries_, queries * static_cast<std::size_t>(dim_));
     grow(h_out_indices_, queries * static_cast<std::size_t>(params.k));
     grow(h_out_values_, queries * static_cast<std::size_t>(params.k));
+    grow(h_status_, 1);
     if (reallocated) {
         ++generation_;
         destroyGraph();
@@ -641,7 +744,15 @@ HostTopK Searcher::copyResultToHost(const CudaStream& stream) {
     const std::size_t elements = static_cast<std::size_t>(current_batch_) * static_cast<std::size_t>(current_k_);
     d_out_indices_.copyToHost(h_out_indices_.data(), elements, stream.get());
     d_out_values_.copyToHost(h_out_values_.data(), elements, stream.get());
+    // The device status word (first 4 bytes of the workspace) travels with the result.
+    ZCGVS_CUDA_CHECK(cudaMemcpyAsync(h_status_.data(), d_workspace_.data(), sizeof(std::uint32_t),
+                                     cudaMemcpyDeviceToHost, stream.get()));
     stream.synchronize();
+    if (const std::uint32_t word = h_status_.data()[0]; word != 0u) {
+        ZCGVS_CUDA_CHECK(cudaMemsetAsync(d_workspace_.data(), 0, sizeof(std::uint32_t), stream.get()));
+        stream.synchronize();
+        throw std::runtime_error("zcgvs: search incomplete, " + describeDeviceStatus(word));
+    }
     HostTopK result;
     result.batch = current_batch_;
     result.k = current_k_;

@@ -28,6 +28,7 @@
 #include <cuda_runtime.h>
 
 #include <algorithm>
+#include <atomic>
 #include <cfloat>
 #include <climits>
 #include <string>
@@ -43,6 +44,16 @@ namespace gemm {
 namespace {
 
 constexpr int kCandCap = 16384;
+static_assert(kStatusOverflow == ZCGVS_DEVICE_CANDIDATE_OVERFLOW && kStatusTmemWait == ZCGVS_DEVICE_TMEM_WAIT_TIMEOUT,
+              "device status bits must match the header");
+
+// Per-query candidate buffer entries a search uses: kCandCap, or a smaller test cap
+// (zcgvs_test_set_candidate_cap). The workspace layout always reserves kCandCap per query.
+std::atomic<int> g_test_cand_cap{0};
+int cand_cap() {
+    const int cap = g_test_cand_cap.load(std::memory_order_relaxed);
+    return cap > 0 ? cap : kCandCap;
+}
 constexpr int kStatRank = 16;  // rank of the statistical threshold among the sample's chunk maxima
 constexpr int kPasses = 3;     // the filter pass and up to two retries
 constexpr int kSelectThreads = 512;
@@ -786,6 +797,7 @@ int zcgvs_gemm_topk(const void* corpus, int dtype, const float* row_scales, int6
     p.done = done;
     const long long items = static_cast<long long>(p.mtiles) * p.ntiles;
     const int filter_ctas = static_cast<int>(std::min<long long>(items, g.mb_ctas));
+    const int cap = cand_cap();
     for (int pass = 0; pass < kPasses; ++pass) {
         p.retry = pass == 0 ? nullptr : retry + pass;
         p.mneed = pass == 0 ? nullptr : mneed + static_cast<size_t>(pass) * g.mtiles;
@@ -797,18 +809,18 @@ int zcgvs_gemm_topk(const void* corpus, int dtype, const float* row_scales, int6
             const int segments = filter_ctas * kEpiWarps;
             const int blocks = (segments + kBucketThreads / 32 - 1) / (kBucketThreads / 32);
             bucket_kernel<<<blocks, kBucketThreads, 0, st>>>(p.mb_key, p.mb_query, p.mb_count, segments, g.mb_cap,
-                                                             cand_count, cand, kCandCap, p.retry);
+                                                             cand_count, cand, cap, p.retry);
         }
         e = cudaGetLastError();
         if (e != cudaSuccess) return fail_cuda(e, "bucket_kernel launch");
         {
             KernelTimer timer("gemm_select", st);
             if (batch < device_sm_count()) {
-                select_kernel<1024><<<batch, 1024, 0, st>>>(cand, cand_count, kCandCap, k, thr_key, thr_safe, done,
+                select_kernel<1024><<<batch, 1024, 0, st>>>(cand, cand_count, cap, k, thr_key, thr_safe, done,
                                                             retry, mneed, g.mtiles, p.status, pass, out_indices,
                                                             out_scores);
             } else {
-                select_kernel<512><<<batch, 512, 0, st>>>(cand, cand_count, kCandCap, k, thr_key, thr_safe, done,
+                select_kernel<512><<<batch, 512, 0, st>>>(cand, cand_count, cap, k, thr_key, thr_safe, done,
                                                           retry, mneed, g.mtiles, p.status, pass, out_indices,
                                                           out_scores);
             }
@@ -817,6 +829,15 @@ int zcgvs_gemm_topk(const void* corpus, int dtype, const float* row_scales, int6
         if (e != cudaSuccess) return fail_cuda(e, "select_kernel launch");
     }
     return ok();
+}
+
+int zcgvs_test_set_candidate_cap(int cap) {
+    if (cap < 0 || cap > zc::gemm::kCandCap) {
+        return zc::fail(ZCGVS_ERR_INVALID_ARG,
+                        "zcgvs_test_set_candidate_cap: cap must be 0 (default) or 1.." + std::to_string(zc::gemm::kCandCap));
+    }
+    zc::gemm::g_test_cand_cap.store(cap, std::memory_order_relaxed);
+    return zc::ok();
 }
 
 size_t zcgvs_gemm_similarity_workspace_bytes(int dtype, int64_t doc_count, int dim, int batch) {

@@ -1,4 +1,4 @@
-"""ZCVE embedding and ZCVL lexical-index files: writers and readers.
+"""ZCVE embedding, ZCVM metadata and ZCVL lexical-index files: writers and readers.
 
 The byte layouts are the reference's (include/zcgvs/data/binary_format.hpp:12-47; its Python
 counterpart python/zcgvs_tools/formats.py), all scalars little-endian, so files move between
@@ -9,6 +9,8 @@ the reference and this library in both directions:
         Version 3 (this library's extension, dtype 4 = int8 with one scale per row) appends the
         [doc_count] f32 row scales after the matrix. Writers emit version 2 for the reference's
         dtypes (0-3) and version 3 only for dtype 4.
+  ZCVM  magic 'ZCVM', u32 version 1, i64 doc_count, then per document u32 length + UTF-8 id
+        and u32 length + UTF-8 passage text.
   ZCVL  magic 'ZCVL', u32 version 1, i64 doc_count, i32 vocab, i64 nnz, f32 k1, f32 b,
         f32 average_doc_length, i64 offsets[vocab + 1], i32 docs[nnz], f32 weights[nnz].
 
@@ -18,7 +20,7 @@ as the reference's writer does, clamp(rint(x / scale), +-127) (formats.py:85-91)
 are byte-identical to the reference's; per-row int8 rounds as zcgvs_convert_i8_rows and the
 reference's CUDA converter do, clamp(rint(x * (1 / scale)), +-127), so a host-written int8_row
 file equals a store converted on the device. The C++ loaders are EmbeddingStore::loadFromFile /
-LexicalIndex::loadFromFile (include/zcgvs/data/).
+LexicalIndex::loadFromFile and Corpus::load (include/zcgvs/data/).
 """
 
 from __future__ import annotations
@@ -30,6 +32,8 @@ import numpy as np
 
 EMBEDDING_MAGIC = b"ZCVE"
 LEXICAL_MAGIC = b"ZCVL"
+METADATA_MAGIC = b"ZCVM"
+METADATA_VERSION = 1
 EMBEDDING_VERSION = 2          # what the reference writes and reads
 EMBEDDING_VERSION_ROW_SCALES = 3
 LEXICAL_VERSION = 1
@@ -243,3 +247,47 @@ def read_lexical_index(path: str | Path) -> dict:
             parts.append(np.frombuffer(data, dtype=dtype))
     return {"doc_count": doc_count, "vocab_size": vocab, "nnz": nnz, "k1": k1, "b": b, "average_doc_length": avgdl,
             "offsets": parts[0], "posting_docs": parts[1], "posting_weights": parts[2]}
+
+
+_META_HEAD = struct.Struct("<4sIq")        # magic, version, doc_count
+_U32 = struct.Struct("<I")
+
+
+def write_metadata(path: str | Path, doc_ids: list[str], texts: list[str]) -> None:
+    """The corpus metadata file: one (id, passage text) pair per document, in corpus order."""
+    if len(doc_ids) != len(texts):
+        raise ValueError(f"{len(doc_ids)} document ids but {len(texts)} texts")
+    parts = [_META_HEAD.pack(METADATA_MAGIC, METADATA_VERSION, len(doc_ids))]
+    for doc_id, text in zip(doc_ids, texts):
+        for field in (doc_id.encode("utf-8"), text.encode("utf-8")):
+            parts.append(_U32.pack(len(field)))
+            parts.append(field)
+    Path(path).write_bytes(b"".join(parts))
+
+
+def read_metadata(path: str | Path) -> tuple[list[str], list[str]]:
+    raw = Path(path).read_bytes()
+    if len(raw) < _META_HEAD.size:
+        raise ValueError(f"{path}: shorter than a metadata header")
+    magic, version, count = _META_HEAD.unpack_from(raw, 0)
+    if magic != METADATA_MAGIC:
+        raise ValueError(f"{path}: not a metadata file (magic {magic!r})")
+    if version != METADATA_VERSION:
+        raise ValueError(f"{path}: unsupported metadata version {version}")
+    at = _META_HEAD.size
+    ids: list[str] = []
+    texts: list[str] = []
+    for _ in range(count):
+        fields = []
+        for _ in range(2):
+            if at + 4 > len(raw):
+                raise ValueError(f"{path}: ends inside document {len(ids)}")
+            (length,) = _U32.unpack_from(raw, at)
+            at += 4
+            if at + length > len(raw):
+                raise ValueError(f"{path}: ends inside document {len(ids)}")
+            fields.append(raw[at:at + length].decode("utf-8"))
+            at += length
+        ids.append(fields[0])
+        texts.append(fields[1])
+    return ids, texts

@@ -17,6 +17,14 @@ LIB_PATH = HERE / "libzcgvs_sm100.so"
 HEADER_PATH = HERE.parent / "include" / "zcgvs_sm100.h"
 
 OK, ERR_INVALID_ARG, ERR_CUDA, ERR_UNSUPPORTED, ERR_DEVICE_STATUS = 0, 1, 2, 3, 4
+# Bits of the device status word (the first 4 bytes of a workspace; ZCGVS_DEVICE_* in the header).
+DEVICE_TILE_WAIT_TIMEOUT, DEVICE_DRAIN_TIMEOUT, DEVICE_TMEM_WAIT_TIMEOUT, DEVICE_CANDIDATE_OVERFLOW = 1, 2, 4, 8
+_DEVICE_STATUS_TEXT = {
+    DEVICE_TILE_WAIT_TIMEOUT: "a bounded wait for a corpus tile ran out",
+    DEVICE_DRAIN_TIMEOUT: "a bounded wait for in-flight copies ran out",
+    DEVICE_TMEM_WAIT_TIMEOUT: "a tensor-memory accumulator hand-off ran out",
+    DEVICE_CANDIDATE_OVERFLOW: "a query kept more candidates than its buffer holds (its top-k is incomplete)",
+}
 DTYPE_F32, DTYPE_F16, DTYPE_I8, DTYPE_BINARY, DTYPE_I8_ROW = 0, 1, 2, 3, 4
 METRIC_COSINE, METRIC_DOT, METRIC_L2 = 0, 1, 2
 MAX_K = 1024
@@ -31,6 +39,8 @@ SIGNATURES = {
     "zcgvs_last_cuda_error": (_i32, []),
     "zcgvs_workspace_init": (_i32, [_P, _sz, _P]),
     "zcgvs_workspace_status": (_i32, [_P, _sz, _P, _P]),
+    "zcgvs_test_set_candidate_cap": (_i32, [_i32]),
+    "zcgvs_check_bounded_wait": (_i32, [_P, _sz, _P]),
     "zcgvs_kernel_timing": (_i32, [_i32]),
     "zcgvs_kernel_timing_read": (_i32, [ctypes.c_char_p, _P, _P]),
     "zcgvs_scan_topk_workspace_bytes": (_sz, [_i32, _i64, _i32, _i32, _i32]),
@@ -38,6 +48,7 @@ SIGNATURES = {
                                _P, _P, _P, _sz, _P]),
     "zcgvs_scan_topk_noalloc": (_i32, [_P, _i32, _f32, _P, _i64, _i32, _P, _i32, _P, _i32, _i32,
                                        _i32, _P, _P, _P]),
+    "zcgvs_scan_topk_noalloc_status": (_i32, [_P, _P]),
     "zcgvs_similarity": (_i32, [_P, _i32, _f32, _P, _i64, _i32, _P, _i32, _P, _i32, _P, _P]),
     "zcgvs_rescore_topk": (_i32, [_P, _i32, _f32, _P, _i64, _i32, _P, _i32, _P, _i32, _i32, _i32,
                                   _P, _P, _P]),
@@ -71,6 +82,22 @@ class ZcgvsError(RuntimeError):
 
 class InvalidArgument(ZcgvsError, ValueError):
     pass
+
+
+class DeviceStatusError(ZcgvsError):
+    """A search finished with a non-zero device status word: its results may be incomplete."""
+
+    def __init__(self, word: int):
+        super().__init__(ERR_DEVICE_STATUS, describe_device_status(word))
+        self.word = word
+
+
+def describe_device_status(word: int) -> str:
+    parts = [text for bit, text in _DEVICE_STATUS_TEXT.items() if word & bit]
+    unknown = word & ~sum(_DEVICE_STATUS_TEXT)
+    if unknown:
+        parts.append(f"unknown bits 0x{unknown:x}")
+    return f"device status 0x{word:x}: " + "; ".join(parts)
 
 
 _lib = None
@@ -133,12 +160,48 @@ class Workspace:
         return self.buffer
 
     def status(self, stream=None) -> int:
+        """The device status word (synchronises `stream`); 0 when every call completed."""
         if self.buffer is None:
             return 0
         value = ctypes.c_uint32(0)
         check(lib().zcgvs_workspace_status(_ptr(self.buffer), self.buffer.numel(), ctypes.byref(value),
                                            _stream(stream)))
         return int(value.value)
+
+    def clear_status(self, stream=None) -> None:
+        if self.buffer is not None:
+            check(lib().zcgvs_workspace_init(_ptr(self.buffer), 4, _stream(stream)))
+
+    def raise_on_status(self, stream=None) -> None:
+        """Raises DeviceStatusError (after clearing the word) when a call left it non-zero."""
+        word = self.status(stream)
+        if word:
+            self.clear_status(stream)
+            raise DeviceStatusError(word)
+
+
+def _own_workspace(workspace, device):
+    """(workspace, owned): a helper that creates its own workspace also checks its status."""
+    return (workspace, False) if workspace is not None else (Workspace(device), True)
+
+
+def set_test_candidate_cap(cap: int) -> None:
+    """Test hook: caps the tensor-core path's per-query candidate buffer (0 restores 16384)."""
+    check(lib().zcgvs_test_set_candidate_cap(int(cap)))
+
+
+def check_bounded_wait(workspace: Workspace, stream=None) -> None:
+    """Runs the diagnostic whose bounded wait runs out (2 s), setting the timeout bit in the
+    workspace's status word."""
+    buf = workspace.get(256, stream)
+    check(lib().zcgvs_check_bounded_wait(_ptr(buf), buf.numel(), _stream(stream)))
+
+
+def noalloc_status(stream=None) -> int:
+    """Status word of the last zcgvs_scan_topk_noalloc call on the current device."""
+    value = ctypes.c_uint32(0)
+    check(lib().zcgvs_scan_topk_noalloc_status(ctypes.byref(value), _stream(stream)))
+    return int(value.value)
 
 
 def kernel_timing(enable: bool) -> None:
@@ -170,20 +233,23 @@ def scan_topk(corpus, dtype: int, dim: int, queries, k: int, *, scale: float = 1
     if out is None:
         out = (torch.empty((batch, k), dtype=torch.int32, device=queries.device),
                torch.empty((batch, k), dtype=torch.float32, device=queries.device))
-    ws = workspace or Workspace(queries.device)
+    ws, owned = _own_workspace(workspace, queries.device)
     nbytes = scan_topk_workspace_bytes(dtype, doc_count, dim, batch, k)
     buf = ws.get(nbytes, stream)
     check(lib().zcgvs_scan_topk(_ptr(corpus), dtype, scale, _ptr(row_scales), doc_count, dim,
                                 _ptr(queries), batch, _ptr(mask), metric, k, id_base,
                                 _ptr(out[0]), _ptr(out[1]), _ptr(buf), buf.numel(), _stream(stream)))
+    if owned:
+        ws.raise_on_status(stream)
     return out
 
 
 def scan_topk_noalloc(corpus, dtype: int, dim: int, queries, k: int, *, scale: float = 1.0,
                       row_scales=None, mask=None, metric: int = METRIC_DOT, id_base: int = 0,
-                      out=None, stream=None):
+                      out=None, stream=None, check_status: bool = True):
     """zcgvs_scan_topk_noalloc: the fused search with the library's static scratch (no
-    workspace). Returns (indices int32 [B,k], scores fp32 [B,k])."""
+    workspace). Returns (indices int32 [B,k], scores fp32 [B,k]); with check_status (the
+    default) it reads the call's device status word and raises DeviceStatusError if non-zero."""
     import torch
 
     doc_count = corpus.shape[0]
@@ -195,6 +261,10 @@ def scan_topk_noalloc(corpus, dtype: int, dim: int, queries, k: int, *, scale: f
     check(lib().zcgvs_scan_topk_noalloc(_ptr(corpus), dtype, scale, _ptr(row_scales), doc_count, dim,
                                         _ptr(queries), batch, _ptr(mask), metric, k, id_base,
                                         _ptr(out[0]), _ptr(out[1]), _stream(stream)))
+    if check_status:
+        word = noalloc_status(stream)
+        if word:
+            raise DeviceStatusError(word)
     return out
 
 
@@ -272,13 +342,15 @@ def hybrid_topk(corpus, dtype: int, dim: int, queries, k: int, index: LexicalInd
     if out is None:
         out = (torch.empty((batch, k), dtype=torch.int32, device=queries.device),
                torch.empty((batch, k), dtype=torch.float32, device=queries.device))
-    ws = workspace or Workspace(queries.device)
+    ws, owned = _own_workspace(workspace, queries.device)
     nbytes = int(lib().zcgvs_hybrid_topk_workspace_bytes(dtype, doc_count, dim, batch, k))
     buf = ws.get(nbytes, stream)
     check(lib().zcgvs_hybrid_topk(_ptr(corpus), dtype, scale, _ptr(row_scales), doc_count, dim, _ptr(queries),
                                   batch, _ptr(mask), metric, _ptr(index.offsets), _ptr(index.docs),
                                   _ptr(index.weights), index.vocab, _ptr(terms), terms.shape[1], dense_weight, k,
                                   _ptr(out[0]), _ptr(out[1]), _ptr(buf), buf.numel(), _stream(stream)))
+    if owned:
+        ws.raise_on_status(stream)
     return out
 
 
@@ -325,12 +397,14 @@ def gemm_topk(corpus, dtype: int, dim: int, queries, k: int, *, row_scales=None,
     if out is None:
         out = (torch.empty((batch, k), dtype=torch.int32, device=queries.device),
                torch.empty((batch, k), dtype=torch.float32, device=queries.device))
-    ws = workspace or Workspace(queries.device)
+    ws, owned = _own_workspace(workspace, queries.device)
     nbytes = int(lib().zcgvs_gemm_topk_workspace_bytes(dtype, doc_count, dim, batch, k))
     buf = ws.get(nbytes, stream)
     check(lib().zcgvs_gemm_topk(_ptr(corpus), dtype, _ptr(row_scales), doc_count, dim, _ptr(queries), batch,
                                 _ptr(mask), metric, k, id_base, _ptr(out[0]), _ptr(out[1]), _ptr(buf), buf.numel(),
                                 _stream(stream)))
+    if owned:
+        ws.raise_on_status(stream)
     return out
 
 
@@ -344,11 +418,13 @@ def gemm_similarity(corpus, dtype: int, dim: int, queries, *, row_scales=None, m
     batch = queries.shape[0]
     if out is None:
         out = torch.empty((batch, doc_count), dtype=torch.float32, device=queries.device)
-    ws = workspace or Workspace(queries.device)
+    ws, owned = _own_workspace(workspace, queries.device)
     nbytes = int(lib().zcgvs_gemm_similarity_workspace_bytes(dtype, doc_count, dim, batch))
     buf = ws.get(nbytes, stream)
     check(lib().zcgvs_gemm_similarity(_ptr(corpus), dtype, _ptr(row_scales), doc_count, dim, _ptr(queries), batch,
                                       _ptr(mask), metric, _ptr(out), _ptr(buf), buf.numel(), _stream(stream)))
+    if owned:
+        ws.raise_on_status(stream)
     return out
 
 
