@@ -668,7 +668,7 @@ class Cfg4(Workload):
                                 id_base=id_base, workspace=self.ws)
 
         self.gemm_local = gemm_local
-        self.search = sharded.ShardedSearch(self.begin, gemm_local) if world > 1 else None
+        self.search = sharded.ShardedSearch(self.begin, self.end, gemm_local) if world > 1 else None
         self.h_queries = self.queries.cpu().pin_memory()
         self.d_q = torch.empty_like(self.queries)
 

@@ -2,9 +2,9 @@
 (python/zcgvs_tools/formats.py, imported read-only from the reference tree), stored as byte
 arrays beside the inputs they encode. The format tests check that this library's writer produces
 the same bytes and that its readers (Python and C++) decode them. Run in a container that has
-the reference tree (default /root/reference, override with ZCGVS_REFERENCE):
+the reference tree (its path in ZCGVS_REFERENCE):
 
-    python tests/golden/make_format_files.py
+    ZCGVS_REFERENCE=<reference checkout> python tests/golden/make_format_files.py
 """
 
 from __future__ import annotations
@@ -17,7 +17,9 @@ from pathlib import Path
 import numpy as np
 
 HERE = Path(__file__).resolve().parent
-REF = Path(os.environ.get("ZCGVS_REFERENCE", "/root/reference"))
+if not os.environ.get("ZCGVS_REFERENCE"):
+    sys.exit("set ZCGVS_REFERENCE to the reference checkout (the script imports its Python tools)")
+REF = Path(os.environ["ZCGVS_REFERENCE"])
 sys.path.insert(0, str(REF / "python"))
 
 from zcgvs_tools import formats  # noqa: E402

@@ -1,13 +1,13 @@
 """Generates tests/golden/*.npz from the reference's own code. Run in a container that has the
-reference tree (default /root/reference, override with ZCGVS_REFERENCE):
+reference tree (its path in ZCGVS_REFERENCE):
 
-    python tests/golden/make_golden.py
+    ZCGVS_REFERENCE=<reference checkout> python tests/golden/make_golden.py
 
 Sources of truth (nothing from the reference is copied; it is imported / linked read-only):
   * python/zcgvs_tools/formats.py  - sign packing, per-matrix int8 quantisation, row strides
   * tests/cpp/cpu_reference.hpp    - cpuCosineSimilarity, cpuTopKIndices,
     cpuQuantizeDequantizeInt8, cpuPackBinary, cpuHamming (through oracle/_ref/libzcgvs_refcpu.so,
-    built by `make -C oracle ref`)
+    built by `make -C oracle ref REF=<reference checkout>`)
 
 Inputs are regenerated from seeds with the oracle's std::mt19937 generators (oracle/gen.cpp),
 which reproduce the reference harnesses' randomMatrix; a CRC of every input is stored so a
@@ -26,7 +26,9 @@ import numpy as np
 
 HERE = Path(__file__).resolve().parent
 ROOT = HERE.parents[1]
-REF = Path(os.environ.get("ZCGVS_REFERENCE", "/root/reference"))
+if not os.environ.get("ZCGVS_REFERENCE"):
+    sys.exit("set ZCGVS_REFERENCE to the reference checkout (the script imports its Python tools)")
+REF = Path(os.environ["ZCGVS_REFERENCE"])
 sys.path.insert(0, str(ROOT / "oracle"))
 sys.path.insert(0, str(REF / "python"))
 
@@ -59,7 +61,7 @@ def main() -> None:
     oracle.build()
     ref = oracle.ref_lib()
     if ref is None:
-        raise SystemExit("oracle/_ref/libzcgvs_refcpu.so missing: run make -C oracle ref")
+        raise SystemExit("oracle/_ref/libzcgvs_refcpu.so missing: run make -C oracle ref REF=<reference checkout>")
 
     # 1. Format conventions from formats.py.
     fmt = {}

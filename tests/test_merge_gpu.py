@@ -115,7 +115,7 @@ def _nccl_worker(rank, world, port, result_path):
         b, e = sharded.shard_bounds(n, world, rank)
         local = sharded.scan_shard_search(torch.from_numpy(storage[b:e]).cuda(), 4, dim,
                                           row_scales=torch.from_numpy(row_scales[b:e]).cuda())
-        ids, scores = sharded.ShardedSearch(b, local).search(torch.from_numpy(queries).cuda(), k)
+        ids, scores = sharded.ShardedSearch(b, e, local).search(torch.from_numpy(queries).cuda(), k)
         torch.cuda.synchronize()
         np.savez(f"{result_path}.{rank}.npz", ids=ids.cpu().numpy(), scores=scores.cpu().numpy())
     finally:

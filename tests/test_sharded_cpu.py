@@ -69,7 +69,7 @@ def worker(rank, world, port, n, dim, batch, k, dtype, result_path):
                                     id_base=id_base)
             return torch.from_numpy(i), torch.from_numpy(s)
 
-        search = sharded.ShardedSearch(begin, local, merge=oracle_merge)
+        search = sharded.ShardedSearch(begin, end, local, merge=oracle_merge)
         ids, scores = search.search(queries, k)
         np.savez(f"{result_path}.{rank}.npz", ids=ids.numpy(), scores=scores.numpy())
     finally:
@@ -171,3 +171,14 @@ def test_sharded_rescore_rejects_candidates_beyond_a_shard():
     for m, k in [(101, 10), (50, 51), (50, 0)]:
         with pytest.raises(ValueError):
             search.search(None, m, k)
+
+
+def test_sharded_search_rejects_k_beyond_a_shard():
+    """A k that a one-GPU search over the whole corpus would accept but one shard cannot hold is
+    rejected before any exchange, with the shard's row count in the message."""
+    import sharded
+
+    search = sharded.ShardedSearch(100, 150, lambda *a: None, merge=lambda *a: None)
+    for k in (51, 0):
+        with pytest.raises(ValueError, match="rows per shard"):
+            search.search(None, k)

@@ -24,7 +24,7 @@ def shard_bounds(n: int, world: int, rank: int) -> tuple[int, int]:
 
 
 class ShardedSearch:
-    """One rank's part of a row-sharded top-k search.
+    """One rank's part of a row-sharded top-k search over rows [shard_begin, shard_end).
 
     local_search(queries, k, id_base) -> (ids int32 [B, k], scores fp32 [B, k]) searches this
     rank's shard; merge(ids [P, B, k], scores [P, B, k], k) -> ([B, k], [B, k]) merges. The
@@ -32,8 +32,9 @@ class ShardedSearch:
     through torch.distributed (NCCL on GPUs).
     """
 
-    def __init__(self, shard_begin: int, local_search, merge=None, group=None):
+    def __init__(self, shard_begin: int, shard_end: int, local_search, merge=None, group=None):
         self.shard_begin = shard_begin
+        self.shard_end = shard_end
         self.local_search = local_search
         if merge is None:
             import zcgvs_sm100 as zc
@@ -43,6 +44,11 @@ class ShardedSearch:
         self.group = group
 
     def search(self, queries, k: int):
+        # Every shard returns its own top-k, so k must fit the shard (a one-GPU search over the
+        # whole corpus would accept a larger k; say why it fails here).
+        if not 0 < k <= self.shard_end - self.shard_begin:
+            raise ValueError(f"sharded search needs 0 < k <= rows per shard; got k={k}, shard rows "
+                             f"{self.shard_end - self.shard_begin}")
         ids, scores = self.local_search(queries, k, self.shard_begin)
         return gather_merge(ids, scores, k, self.merge, self.group)
 
