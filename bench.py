@@ -61,6 +61,10 @@ def parse_args():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--docs", type=int, default=None,
                     help="corpus rows instead of the workload's (small cases for profiler captures)")
+    ap.add_argument("--no-sharded", action="store_true",
+                    help="skip the row-sharded config 4 measurement that follows the replica workloads")
+    ap.add_argument("--sharded-docs", type=int, default=None,
+                    help="corpus rows of the row-sharded measurement (default: config 4's 50,000,000)")
     return ap.parse_args()
 
 
@@ -273,6 +277,19 @@ def pack_signs(torch, x):
     weights = torch.ones(32, dtype=torch.int64, device=x.device) << torch.arange(32, device=x.device)
     words = (bits * weights).sum(dim=2)
     return torch.where(words >= 2 ** 31, words - 2 ** 32, words).to(torch.int32).contiguous()
+
+
+def native_sharded_searcher(torch, zc, world, rank, total_rows):
+    """This rank's zcgvs_sharded handle (NCCL communicator of its own); rank 0 makes the NCCL id
+    and the process group (when there is one) carries it to the others."""
+    nccl_id = zc.ShardedSearcher.unique_id() if rank == 0 else None
+    if world > 1:
+        import torch.distributed as dist
+
+        box = [nccl_id]
+        dist.broadcast_object_list(box, src=0)
+        nccl_id = box[0]
+    return zc.ShardedSearcher(nccl_id, world, rank, total_rows)
 
 
 # --------------------------------------------------------------------------------------------
@@ -540,6 +557,7 @@ class Cfg3(Workload):
     dominant = ("gemm_filter",)
     scaling = "strong"
     # prep, sample, threshold, 3 x (filter, bucket, select), rescore; sharded: two merges more
+    # (the two NCCL all-gathers are the library's kernels, not counted)
     launches = property(lambda self: 13 if self.world == 1 else 15)
 
     def setup(self, torch, zc, device, rank, world):
@@ -571,30 +589,26 @@ class Cfg3(Workload):
                       torch.empty((self.B, self.K), dtype=torch.float32).pin_memory())
         self.d_q = torch.empty((self.B, self.D), dtype=torch.float32, device=device)
         self.store_i16 = self.store.view(torch.int16)
-        self.search = None
-        if world > 1:
-            def coarse(q, m, id_base):
-                return zc.scan_topk(self.codes, zc.DTYPE_BINARY, self.D, q, m, id_base=id_base, workspace=self.ws)
+        self.search = native_sharded_searcher(torch, zc, world, rank, self.N) if world > 1 else None
 
-            def rescore(q, local, k):
-                return zc.rescore_topk(self.store_i16, zc.DTYPE_F16, self.D, q, local, k, metric=zc.METRIC_COSINE)
-
-            self.search = sharded.ShardedRescoreSearch(self.begin, self.end, coarse, rescore)
-
-    def _run(self, q, stream):
+    def _run(self, q, stream, graph=True):
         if self.search is not None:
-            ids, scores = self.search.search(q, self.M, self.K)
-            self.out[0].copy_(ids)
-            self.out[1].copy_(scores)
+            self.search.rescore_search(self.codes, self.zc.DTYPE_BINARY, self.store_i16, self.zc.DTYPE_F16, self.D, q,
+                                       self.M, self.K, metric=self.zc.METRIC_COSINE, graph=graph, out=self.out,
+                                       stream=stream)
             return
         self.zc.scan_topk(self.codes, self.zc.DTYPE_BINARY, self.D, q, self.M, workspace=self.ws, out=self.cand,
                           stream=stream)
         self.zc.rescore_topk(self.store_i16, self.zc.DTYPE_F16, self.D, q, self.cand[0], self.K,
                              metric=self.zc.METRIC_COSINE, out=self.out, stream=stream)
 
+    def step(self, i, stream):
+        j = (i % (self.NQ // self.B)) * self.B
+        self._run(self.queries[j:j + self.B], stream, graph=True)
+
     def step_direct(self, i, stream):
         j = (i % (self.NQ // self.B)) * self.B
-        self._run(self.queries[j:j + self.B], stream)
+        self._run(self.queries[j:j + self.B], stream, graph=False)
 
     def e2e_step(self, i, stream):
         j = (i % (self.NQ // self.B)) * self.B
@@ -668,20 +682,31 @@ class Cfg4(Workload):
                                 id_base=id_base, workspace=self.ws)
 
         self.gemm_local = gemm_local
-        self.search = sharded.ShardedSearch(self.begin, self.end, gemm_local) if world > 1 else None
+        self.search = native_sharded_searcher(torch, zc, world, rank, self.N) if (world > 1 or self.native) else None
+        self.out = (torch.empty((self.B, self.K), dtype=torch.int32, device=device),
+                    torch.empty((self.B, self.K), dtype=torch.float32, device=device))
         self.h_queries = self.queries.cpu().pin_memory()
         self.d_q = torch.empty_like(self.queries)
 
-    launches = property(lambda self: 12 if self.world == 1 else 13)
+    def __init__(self, native=False):
+        # native: search through the row-sharded handle even on one rank (the sharded key's
+        # one-GPU point uses the same code path as its N-GPU points).
+        self.native = native
+
+    launches = property(lambda self: 12 if self.search is None else 13)
     dominant = ("gemm_filter",)
 
-    def _run(self, q):
-        if self.world == 1:
+    def _run(self, q, graph=True):
+        if self.search is None:
             return self.gemm_local(q, self.K, 0)
-        return self.search.search(q, self.K)
+        return self.search.search(self.shard_i16, self.zc.DTYPE_F16, self.D, q, self.K, metric=self.zc.METRIC_COSINE,
+                                  tensor_f16=True, graph=graph, out=self.out)
+
+    def step(self, i, stream):
+        self._run(self.queries, graph=True)
 
     def step_direct(self, i, stream):
-        self._run(self.queries)
+        self._run(self.queries, graph=False)
 
     def e2e_step(self, i, stream):
         self.d_q.copy_(self.h_queries, non_blocking=True)
@@ -915,6 +940,73 @@ def run_reference_sampled(args, wl, steps, warmup):
     emit(json.dumps(line))
 
 
+def measure_sharded(args, torch, zc, device, rank, world):
+    """Row-sharded config 4 (fp16 50M x 768, batch 4,096, top-100) through the native sharded
+    handle, in the processes of the replica run: rank r holds rows shard_bounds(N, P, r), a step
+    is its tensor-core search with global ids, an NCCL all-gather of every rank's [4096, 100]
+    result and the device merge, replayed as one CUDA graph. Strong scaling (the corpus is fixed;
+    each rank scans N / P rows). Timed with CUDA events over the steps, max over ranks; a second,
+    direct pass with the library's kernel timing on splits the step into the local search, the
+    all-gather and the merge."""
+    import torch.distributed as dist
+
+    wl = Cfg4(native=True)
+    if args.sharded_docs:
+        wl.N = args.sharded_docs
+    wl.setup(torch, zc, device, rank, world)
+    stream = torch.cuda.current_stream()
+    steps, warmup = 5, 3
+    for i in range(warmup):  # the first step runs directly and captures the graph the rest replay
+        wl.step(i, stream)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    torch.cuda.synchronize()
+    with ClockSampler(device.index) as clocks:
+        t0, t1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for i in range(steps):
+            wl.step(i, stream)
+        t1.record(stream)
+        torch.cuda.synchronize()
+    elapsed_ms = t0.elapsed_time(t1)
+    tags = ("gemm_sample", "gemm_threshold", "gemm_filter", "gemm_bucket", "gemm_select", "gemm_retry", "allgather",
+            "merge")
+    zc.kernel_timing(True)
+    for i in range(steps):
+        wl.step_direct(i, stream)
+    torch.cuda.synchronize()
+    zc.kernel_timing(False)
+    kern = {t: zc.kernel_timing_read(t)[0] / steps for t in tags}
+    word, comm_error = wl.search.status()
+    local_ms = sum(v for t, v in kern.items() if t.startswith("gemm_"))
+    vals = [elapsed_ms, local_ms, kern["allgather"], kern["merge"], kern["gemm_filter"], float(word | comm_error)]
+    if world > 1:
+        t = torch.tensor(vals, device=device, dtype=torch.float64)
+        dist.all_reduce(t, op=dist.ReduceOp.MAX)
+        vals = [float(v) for v in t.tolist()]
+    elapsed_ms, local_ms, gather_ms, merge_ms, filter_ms, bad = vals
+    rows = wl.end - wl.begin
+    result = {
+        "workload": wl.name, "docs": wl.N, "rows_per_rank": rows, "dim": wl.D, "k": wl.K, "batch": wl.B,
+        "parallelism": f"rowshard{world}", "scaling": "strong", "launch": "one cuda graph per step",
+        "value": wl.B * steps / (elapsed_ms * 1e-3), "unit": UNIT, "steps": steps, "warmup": warmup,
+        "ms_per_step": elapsed_ms / steps,
+        "local_search_ms_per_step": local_ms, "filter_ms_per_step": filter_ms,
+        "allgather_ms_per_step": gather_ms, "merge_ms_per_step": merge_ms,
+        # the share of a step spent in the rank's own search: strong-scaling efficiency when the
+        # local search time is proportional to the rows (the driver's 1 -> N record has the rest)
+        "local_fraction": local_ms / (elapsed_ms / steps),
+        "filter_tflops": 2.0 * wl.B * rows * wl.D / (filter_ms * 1e-3) / 1e12 if filter_ms > 0 else None,
+        "gpu_launches": wl.launches * steps,
+        "clocks": clocks.summary(),
+        "device_status": int(bad),
+        "l2": "inputs larger than L2 (77 GB corpus)",
+    }
+    wl.search.close()
+    return result
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -996,26 +1088,46 @@ def run_ours(args):
     cpu = None
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         cpu = wl.cpu_baseline(12.0)
+    peaks, peak_kind = measured_peaks()
+    summary = {"scaling": wl.scaling, "units": wl.units, "dtype": wl.dtype, "config": wl.config(world),
+               "graphs": wl.graphs, "roofline": wl.roofline(kernel_ms, peaks, peak_kind),
+               "launches": wl.launches}
+    e2e_ranks = [e2e_s]
+    if world > 1:
+        # every rank's end-to-end seconds: shows whether one rank held back the max
+        t = torch.zeros(world, device=device)
+        t[rank] = e2e_s
+        dist.all_reduce(t, op=dist.ReduceOp.SUM)
+        e2e_ranks = [round(float(v), 4) for v in t.tolist()]
+    line_extra = {}
+    if wl.scaling == "weak" and not args.no_sharded:
+        # The replica workloads have no exchange on their data path; the row-sharded search does.
+        # Measure it in the same processes (config 4: the corpus split over the ranks).
+        wl = None
+        torch.cuda.empty_cache()
+        line_extra["sharded"] = measure_sharded(args, torch, zc, device, rank, world)
 
     if rank == 0:
         peaks, peak_kind = measured_peaks()
-        total_units = (1 if wl.scaling == "strong" else world) * wl.units
+        total_units = (1 if summary["scaling"] == "strong" else world) * summary["units"]
         line = {
             "metric": METRIC, "value": total_units * steps / (elapsed_ms * 1e-3), "unit": UNIT,
             "n_gpus": world, "steps": steps, "warmup": warmup,
             "ms_per_step": elapsed_ms / steps, "p50_ms": per_step[len(per_step) // 2],
-            "higher_is_better": True, "scaling": wl.scaling, "vs_baseline": None, "dtype": wl.dtype,
+            "higher_is_better": True, "scaling": summary["scaling"], "vs_baseline": None, "dtype": summary["dtype"],
             "data": "synthetic",
-            "config": dict(wl.config(world), launch="cuda-graph replay per query" if wl.graphs else "direct calls"),
-            "roofline": dict(wl.roofline(kernel_ms, peaks, peak_kind), kernel_ms=kernel_ms),
+            "config": dict(summary["config"], launch="cuda-graph replay per query" if summary["graphs"] else "direct calls"),
+            "roofline": dict(summary["roofline"], kernel_ms=kernel_ms),
             "kernels_ms_per_step": {t: v[0] / steps for t, v in kern.items() if v[1]},
             "e2e": {"value": total_units * e2e_steps / e2e_s, "unit": UNIT,
                     "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h},
-            "gpu_launches": wl.launches * steps,
+            "gpu_launches": summary["launches"] * steps,
             "clocks": clocks.summary(),
             "device_status": status,
+            "e2e_seconds_per_rank": e2e_ranks,
             "cpu_baseline": cpu,
         }
+        line.update(line_extra)
         emit(json.dumps(line))
     if world > 1:
         dist.barrier()

@@ -43,7 +43,8 @@ typedef enum zcgvs_status {
     ZCGVS_ERR_INVALID_ARG = 1,
     ZCGVS_ERR_CUDA = 2,
     ZCGVS_ERR_UNSUPPORTED = 3,
-    ZCGVS_ERR_DEVICE_STATUS = 4
+    ZCGVS_ERR_DEVICE_STATUS = 4,
+    ZCGVS_ERR_COMM = 5 /* an NCCL call of the sharded search failed, or NCCL is unavailable */
 } zcgvs_status;
 
 /* Storage precision of a corpus. Codes 0-3 equal the reference ScalarType
@@ -260,6 +261,85 @@ int zcgvs_gemm_similarity(const void* corpus, int dtype, const float* row_scales
  * --------------------------------------------------------------------------------------- */
 int zcgvs_merge_topk(const int* list_indices, const float* list_scores, int lists, int batch,
                      int k_in, int k, int* out_indices, float* out_scores, void* stream);
+
+/* The general form of zcgvs_merge_topk, which reads an all-gather's output in place and folds
+ * in the steps around the merge of a sharded search:
+ *   list p's entries are list_indices[p * list_stride + q * k_in + i] and the same offsets of
+ *   list_scores (an all-gather of packed [2, batch, k_in] int32 blocks, ids then score bits, is
+ *   read with list_stride = 2 * batch * k_in and list_scores = list_indices + batch * k_in);
+ *   list_id_offsets (optional, [lists] int32 on the device) is added to the ids of list p
+ *   (shard-local ids become global ids);
+ *   out_indices / out_scores (optional together) receive the merged [batch, k];
+ *   out_owned (optional) receives, per merged entry, id - own_begin when the id lies in
+ *   [own_begin, own_end) and -1 otherwise: the shard-local candidate list a rank rescores.
+ * At least one output must be given. */
+int zcgvs_merge_topk_lists(const int* list_indices, const float* list_scores, int64_t list_stride,
+                           int lists, int batch, int k_in, const int* list_id_offsets, int k,
+                           int* out_indices, float* out_scores, int own_begin, int own_end,
+                           int* out_owned, void* stream);
+
+/* ---------------------------------------------------------------------------------------
+ * Row-sharded search across the GPUs of one node, one process per GPU, over NCCL. No reference
+ * counterpart (the reference runs on one GPU). The corpus' rows are split evenly into `world`
+ * contiguous shards (zcgvs_shard_bounds); rank r holds rows [begin, end) of every store on its
+ * GPU. A search runs the local fused search with global ids, an NCCL all-gather of every
+ * rank's packed [batch, k] (id, score) list and zcgvs_merge_topk_lists on the device, so every
+ * rank ends with the global top-k, identical to a one-GPU search over the whole corpus (the
+ * union of the per-shard top-k lists contains the global top-k and the order is total). The
+ * rescore search follows the reference's pipeline semantics: global coarse top-M (exchange and
+ * merge), each rank rescoring the candidates it owns, exchange and merge of the top-k.
+ *
+ * NCCL is loaded at run time (libnccl.so.2; in a process that already loaded NCCL, such as one
+ * running torch.distributed, the loaded copy). A handle owns its communicator, its exchange
+ * buffers and workspace (allocated, and zero-filled, by the first search of a larger shape) and
+ * one CUDA graph: with ZCGVS_SHARDED_GRAPH the first search of a shape runs directly and is then
+ * captured, and later searches with the same arguments replay the whole step (local search,
+ * all-gathers, merges, rescoring) as one graph launch. Every rank must make the same calls in
+ * the same order. Not thread-safe: one handle per process and stream.
+ * --------------------------------------------------------------------------------------- */
+typedef struct zcgvs_sharded zcgvs_sharded;
+
+#define ZCGVS_SHARDED_GRAPH 0x1u       /* capture each search shape once, replay it after */
+#define ZCGVS_SHARDED_F16_TENSOR 0x2u  /* fp16 shards: local search on the tensor cores
+                                          (zcgvs_gemm_topk, fp16 queries) */
+
+/* Rows [*begin, *end) of shard `rank` when total_rows rows are split over `world` shards as
+ * evenly as possible (the first total_rows % world shards hold one row more). */
+int zcgvs_shard_bounds(int64_t total_rows, int world, int rank, int64_t* begin, int64_t* end);
+
+/* Bytes of an NCCL unique id (128). Rank 0 makes one with zcgvs_nccl_unique_id and sends it to
+ * the other ranks by any channel (a file, a TCP store, MPI). */
+size_t zcgvs_nccl_id_bytes(void);
+int zcgvs_nccl_unique_id(void* id);
+
+/* Creates the handle of rank `rank` of `world` on the current device (a collective: every rank
+ * must call it with the same id, world and total_rows). */
+int zcgvs_sharded_create(const void* nccl_id, int world, int rank, int64_t total_rows,
+                         zcgvs_sharded** out);
+int zcgvs_sharded_destroy(zcgvs_sharded* handle);
+
+/* Dense search: `shard` holds this rank's shard_rows rows (the arguments of zcgvs_scan_topk
+ * otherwise; ids in the result are global). k <= shard_rows. Writes [batch, k] on every rank. */
+int zcgvs_sharded_search(zcgvs_sharded* handle, const void* shard, int dtype, float scale,
+                         const float* row_scales, int64_t shard_rows, int dim, const float* queries,
+                         int batch, const uint8_t* mask, int metric, int k, unsigned flags,
+                         int* out_indices, float* out_scores, void* stream);
+
+/* Coarse search over this rank's codes (any dtype zcgvs_scan_topk takes, e.g. 1-bit), the
+ * global top-`candidates`, exact rescoring of the owned candidates against this rank's rows of
+ * `store` (as zcgvs_rescore_topk), and the global top-k. k <= candidates <= shard_rows. */
+int zcgvs_sharded_rescore_search(zcgvs_sharded* handle, const void* codes, int code_dtype,
+                                 float code_scale, const float* code_row_scales, const void* store,
+                                 int store_dtype, float store_scale, const float* store_row_scales,
+                                 int64_t shard_rows, int dim, const float* queries, int batch,
+                                 int metric, int candidates, int k, unsigned flags,
+                                 int* out_indices, float* out_scores, void* stream);
+
+/* The device status word of the handle's local-search workspace (ZCGVS_DEVICE_* bits; sticky)
+ * and the communicator's asynchronous NCCL error, after synchronising `stream`. A non-zero
+ * status or comm_error means the searches since the last clear may be incomplete. */
+int zcgvs_sharded_status(zcgvs_sharded* handle, uint32_t* status, int* comm_error, void* stream);
+int zcgvs_sharded_clear_status(zcgvs_sharded* handle, void* stream);
 
 /* ---------------------------------------------------------------------------------------
  * Hybrid lexical + dense search. Replaces the hybrid stages of Searcher::recordPipeline

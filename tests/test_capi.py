@@ -110,3 +110,38 @@ def test_device_status_text_names_every_bit(zc):
     text = zc.describe_device_status(zc.DEVICE_CANDIDATE_OVERFLOW | zc.DEVICE_TILE_WAIT_TIMEOUT)
     assert "0x9" in text and "corpus tile" in text and "more candidates" in text
     assert "unknown bits 0x20" in zc.describe_device_status(0x20)
+
+
+def test_shard_bounds_match_the_python_split(zc):
+    import sharded
+
+    for n, world in ((10, 3), (50_000_000, 8), (7, 7), (140_011, 2)):
+        spans = [zc.shard_bounds(n, world, r) for r in range(world)]
+        assert spans == [sharded.shard_bounds(n, world, r) for r in range(world)]
+        assert spans[0][0] == 0 and spans[-1][1] == n
+        assert all(a[1] == b[0] for a, b in zip(spans, spans[1:]))
+    lib = zc.lib()
+    b, e = ctypes.c_int64(), ctypes.c_int64()
+    assert lib.zcgvs_shard_bounds(10, 0, 0, ctypes.byref(b), ctypes.byref(e)) == zc.ERR_INVALID_ARG
+    assert lib.zcgvs_shard_bounds(10, 2, 2, ctypes.byref(b), ctypes.byref(e)) == zc.ERR_INVALID_ARG
+
+
+def test_sharded_entry_points_check_arguments_before_any_device_or_nccl_call(zc):
+    lib = zc.lib()
+    handle = ctypes.c_void_p()
+    nccl_id = ctypes.create_string_buffer(int(lib.zcgvs_nccl_id_bytes()))
+    assert lib.zcgvs_nccl_id_bytes() == 128
+    for world, rank, rows in ((0, 0, 10), (2, 2, 10), (4, 0, 3), (2, -1, 10)):
+        assert lib.zcgvs_sharded_create(nccl_id, world, rank, rows, ctypes.byref(handle)) == zc.ERR_INVALID_ARG
+    assert lib.zcgvs_sharded_create(None, 1, 0, 10, ctypes.byref(handle)) == zc.ERR_INVALID_ARG
+    fake = ctypes.c_void_p(16)
+    assert lib.zcgvs_sharded_search(None, fake, 4, 1.0, fake, 10, 8, fake, 1, None, 1, 5, 0, fake, fake,
+                                    None) == zc.ERR_INVALID_ARG
+    assert "null handle" in lib.zcgvs_last_error_message().decode()
+    assert lib.zcgvs_sharded_destroy(None) == zc.OK
+    # The list merge: no output at all, or a stride shorter than one list.
+    assert lib.zcgvs_merge_topk_lists(fake, fake, 100, 2, 2, 50, None, 10, None, None, 0, 0, None,
+                                      None) == zc.ERR_INVALID_ARG
+    assert lib.zcgvs_merge_topk_lists(fake, fake, 99, 2, 2, 50, None, 10, fake, fake, 0, 0, None,
+                                      None) == zc.ERR_INVALID_ARG
+    assert "list_stride" in lib.zcgvs_last_error_message().decode()

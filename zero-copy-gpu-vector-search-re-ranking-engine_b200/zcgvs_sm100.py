@@ -16,7 +16,8 @@ HERE = Path(__file__).resolve().parent
 LIB_PATH = HERE / "libzcgvs_sm100.so"
 HEADER_PATH = HERE.parent / "include" / "zcgvs_sm100.h"
 
-OK, ERR_INVALID_ARG, ERR_CUDA, ERR_UNSUPPORTED, ERR_DEVICE_STATUS = 0, 1, 2, 3, 4
+OK, ERR_INVALID_ARG, ERR_CUDA, ERR_UNSUPPORTED, ERR_DEVICE_STATUS, ERR_COMM = 0, 1, 2, 3, 4, 5
+SHARDED_GRAPH, SHARDED_F16_TENSOR = 1, 2
 # Bits of the device status word (the first 4 bytes of a workspace; ZCGVS_DEVICE_* in the header).
 DEVICE_TILE_WAIT_TIMEOUT, DEVICE_DRAIN_TIMEOUT, DEVICE_TMEM_WAIT_TIMEOUT, DEVICE_CANDIDATE_OVERFLOW = 1, 2, 4, 8
 _DEVICE_STATUS_TEXT = {
@@ -65,6 +66,18 @@ SIGNATURES = {
     "zcgvs_pack_binary": (_i32, [_P, _P, _i64, _i32, _P]),
     "zcgvs_remap_indices": (_i32, [_P, _P, _i32, _i32, _i32, _P, _P]),
     "zcgvs_merge_topk": (_i32, [_P, _P, _i32, _i32, _i32, _i32, _P, _P, _P]),
+    "zcgvs_merge_topk_lists": (_i32, [_P, _P, _i64, _i32, _i32, _i32, _P, _i32, _P, _P, _i32, _i32, _P, _P]),
+    "zcgvs_shard_bounds": (_i32, [_i64, _i32, _i32, _P, _P]),
+    "zcgvs_nccl_id_bytes": (_sz, []),
+    "zcgvs_nccl_unique_id": (_i32, [_P]),
+    "zcgvs_sharded_create": (_i32, [_P, _i32, _i32, _i64, _P]),
+    "zcgvs_sharded_destroy": (_i32, [_P]),
+    "zcgvs_sharded_search": (_i32, [_P, _P, _i32, _f32, _P, _i64, _i32, _P, _i32, _P, _i32, _i32, ctypes.c_uint,
+                                    _P, _P, _P]),
+    "zcgvs_sharded_rescore_search": (_i32, [_P, _P, _i32, _f32, _P, _P, _i32, _f32, _P, _i64, _i32, _P, _i32, _i32,
+                                            _i32, _i32, ctypes.c_uint, _P, _P, _P]),
+    "zcgvs_sharded_status": (_i32, [_P, _P, _P, _P]),
+    "zcgvs_sharded_clear_status": (_i32, [_P, _P]),
     "zcgvs_hybrid_topk_workspace_bytes": (_sz, [_i32, _i64, _i32, _i32, _i32]),
     "zcgvs_hybrid_topk": (_i32, [_P, _i32, _f32, _P, _i64, _i32, _P, _i32, _P, _i32, _P, _P, _P, _i32,
                                  _P, _i32, _f32, _i32, _P, _P, _P, _sz, _P]),
@@ -383,6 +396,95 @@ def merge_topk(list_indices, list_scores, k: int, out=None, stream=None):
     check(lib().zcgvs_merge_topk(_ptr(list_indices), _ptr(list_scores), lists, batch, k_in, k, _ptr(out[0]),
                                  _ptr(out[1]), _stream(stream)))
     return out
+
+
+def merge_topk_lists(list_indices, list_scores, list_stride: int, lists: int, batch: int, k_in: int, k: int, *,
+                     list_id_offsets=None, out=None, own_range=None, out_owned=None, stream=None):
+    """zcgvs_merge_topk_lists over flat device tensors (see the header for the layout)."""
+    check(lib().zcgvs_merge_topk_lists(_ptr(list_indices), _ptr(list_scores), list_stride, lists, batch, k_in,
+                                       _ptr(list_id_offsets), k, _ptr(out[0]) if out else None,
+                                       _ptr(out[1]) if out else None, own_range[0] if own_range else 0,
+                                       own_range[1] if own_range else 0, _ptr(out_owned), _stream(stream)))
+    return out, out_owned
+
+
+def shard_bounds(total_rows: int, world: int, rank: int) -> tuple[int, int]:
+    begin, end = ctypes.c_int64(0), ctypes.c_int64(0)
+    check(lib().zcgvs_shard_bounds(total_rows, world, rank, ctypes.byref(begin), ctypes.byref(end)))
+    return int(begin.value), int(end.value)
+
+
+class ShardedSearcher:
+    """Rank `rank`'s handle of a row-sharded search over `world` GPUs (zcgvs_sharded_*): the
+    local fused search, NCCL all-gathers and device merges, the whole step replayed as one CUDA
+    graph after the first search of a shape. Every rank must make the same calls in order."""
+
+    def __init__(self, nccl_id: bytes, world: int, rank: int, total_rows: int):
+        handle = ctypes.c_void_p()
+        buf = ctypes.create_string_buffer(bytes(nccl_id), len(nccl_id))
+        check(lib().zcgvs_sharded_create(buf, world, rank, total_rows, ctypes.byref(handle)))
+        self.handle = handle
+        self.world, self.rank, self.total_rows = world, rank, total_rows
+        self.begin, self.end = shard_bounds(total_rows, world, rank)
+
+    @staticmethod
+    def unique_id() -> bytes:
+        n = int(lib().zcgvs_nccl_id_bytes())
+        buf = ctypes.create_string_buffer(n)
+        check(lib().zcgvs_nccl_unique_id(buf))
+        return buf.raw
+
+    def _out(self, batch, k, device, out):
+        import torch
+
+        if out is None:
+            out = (torch.empty((batch, k), dtype=torch.int32, device=device),
+                   torch.empty((batch, k), dtype=torch.float32, device=device))
+        return out
+
+    def search(self, shard, dtype: int, dim: int, queries, k: int, *, scale: float = 1.0, row_scales=None,
+               mask=None, metric: int = METRIC_DOT, tensor_f16: bool = False, graph: bool = True, out=None,
+               stream=None):
+        queries = queries.reshape(-1, dim)
+        out = self._out(queries.shape[0], k, queries.device, out)
+        flags = (SHARDED_GRAPH if graph else 0) | (SHARDED_F16_TENSOR if tensor_f16 else 0)
+        check(lib().zcgvs_sharded_search(self.handle, _ptr(shard), dtype, scale, _ptr(row_scales), shard.shape[0], dim,
+                                         _ptr(queries), queries.shape[0], _ptr(mask), metric, k, flags, _ptr(out[0]),
+                                         _ptr(out[1]), _stream(stream)))
+        return out
+
+    def rescore_search(self, codes, code_dtype: int, store, store_dtype: int, dim: int, queries, candidates: int,
+                       k: int, *, code_scale: float = 1.0, code_row_scales=None, store_scale: float = 1.0,
+                       store_row_scales=None, metric: int = METRIC_DOT, graph: bool = True, out=None, stream=None):
+        queries = queries.reshape(-1, dim)
+        out = self._out(queries.shape[0], k, queries.device, out)
+        check(lib().zcgvs_sharded_rescore_search(self.handle, _ptr(codes), code_dtype, code_scale,
+                                                 _ptr(code_row_scales), _ptr(store), store_dtype, store_scale,
+                                                 _ptr(store_row_scales), codes.shape[0], dim, _ptr(queries),
+                                                 queries.shape[0], metric, candidates, k,
+                                                 SHARDED_GRAPH if graph else 0, _ptr(out[0]), _ptr(out[1]),
+                                                 _stream(stream)))
+        return out
+
+    def status(self, stream=None) -> tuple[int, int]:
+        """(device status word, NCCL asynchronous error) after synchronising `stream`."""
+        word, comm = ctypes.c_uint32(0), ctypes.c_int(0)
+        check(lib().zcgvs_sharded_status(self.handle, ctypes.byref(word), ctypes.byref(comm), _stream(stream)))
+        return int(word.value), int(comm.value)
+
+    def clear_status(self, stream=None) -> None:
+        check(lib().zcgvs_sharded_clear_status(self.handle, _stream(stream)))
+
+    def close(self) -> None:
+        if self.handle:
+            check(lib().zcgvs_sharded_destroy(self.handle))
+            self.handle = ctypes.c_void_p()
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:  # noqa: BLE001 - interpreter shutdown
+            pass
 
 
 def gemm_topk(corpus, dtype: int, dim: int, queries, k: int, *, row_scales=None, mask=None,
