@@ -27,6 +27,7 @@
 #include "zcgvs/data/embedding_store.hpp"
 #include "zcgvs/data/lexical_index.hpp"
 #include "zcgvs/search/searcher.hpp"
+#include "zcgvs/search/sharded_searcher.hpp"
 #include "zcgvs_sm100.h"
 
 namespace zcgvs {
@@ -761,6 +762,96 @@ HostTopK Searcher::copyResultToHost(const CudaStream& stream) {
     float elapsed_ms = 0.0f;
     ZCGVS_CUDA_CHECK(cudaEventElapsedTime(&elapsed_ms, ev_start_, ev_end_));
     last_gpu_ms_ = static_cast<double>(elapsed_ms);
+    return result;
+}
+
+// ------------------------------------------------------------------------------------------
+// ShardedSearcher
+// ------------------------------------------------------------------------------------------
+std::vector<char> ShardedSearcher::uniqueId() {
+    std::vector<char> id(zcgvs_nccl_id_bytes());
+    check(zcgvs_nccl_unique_id(id.data()), "zcgvs_nccl_unique_id");
+    return id;
+}
+
+void ShardedSearcher::shardBounds(std::int64_t total_rows, int world, int rank, std::int64_t* begin,
+                                  std::int64_t* end) {
+    check(zcgvs_shard_bounds(total_rows, world, rank, begin, end), "zcgvs_shard_bounds");
+}
+
+ShardedSearcher::ShardedSearcher(const std::vector<char>& nccl_id, int world, int rank, std::int64_t total_rows) {
+    if (nccl_id.size() != zcgvs_nccl_id_bytes()) throw std::invalid_argument("zcgvs: the NCCL id has the wrong size");
+    check(zcgvs_sharded_create(nccl_id.data(), world, rank, total_rows, &handle_), "zcgvs_sharded_create");
+    shardBounds(total_rows, world, rank, &begin_, &end_);
+}
+
+ShardedSearcher::~ShardedSearcher() { zcgvs_sharded_destroy(handle_); }
+
+void ShardedSearcher::setRescoreStore(const EmbeddingStore* shard_store) {
+    if (shard_store != nullptr) {
+        if (shard_store->dtype() == ScalarType::Binary) throw std::invalid_argument("zcgvs: rescore store must not be binary");
+        if (shard_store->docCount() != end_ - begin_) {
+            throw std::invalid_argument("zcgvs: the rescore store must hold this rank's shard rows");
+        }
+    }
+    rescore_store_ = shard_store;
+}
+
+void ShardedSearcher::search(const EmbeddingStore& shard, const float* host_queries, int dim, int batch,
+                             const SearchParams& params, const CudaStream& stream) {
+    if (dim != shard.dim()) throw std::invalid_argument("zcgvs: query dim does not match the shard");
+    if (batch <= 0 || params.k <= 0) throw std::invalid_argument("zcgvs: batch and k must be positive");
+    const bool rescore = rescore_store_ != nullptr && params.rescore_candidates > 0;
+    if (rescore && rescore_store_->dim() != dim) throw std::invalid_argument("zcgvs: rescore store dim differs");
+    const std::size_t elements = static_cast<std::size_t>(batch) * static_cast<std::size_t>(dim);
+    const std::size_t results = static_cast<std::size_t>(batch) * static_cast<std::size_t>(params.k);
+    grow(d_queries_, elements);
+    grow(h_queries_, elements);
+    grow(d_out_indices_, results);
+    grow(d_out_values_, results);
+    grow(h_out_indices_, results);
+    grow(h_out_values_, results);
+    std::memcpy(h_queries_.data(), host_queries, elements * sizeof(float));
+    d_queries_.copyFromHost(h_queries_.data(), elements, stream.get());
+    const unsigned flags = params.use_graph ? ZCGVS_SHARDED_GRAPH : 0u;
+    if (rescore) {
+        check(zcgvs_sharded_rescore_search(handle_, shard.deviceData(), static_cast<int>(shard.dtype()), shard.scale(),
+                                           shard.rowScales(), rescore_store_->deviceData(),
+                                           static_cast<int>(rescore_store_->dtype()), rescore_store_->scale(),
+                                           rescore_store_->rowScales(), shard.docCount(), dim, d_queries_.data(), batch,
+                                           static_cast<int>(params.metric), params.rescore_candidates, params.k, flags,
+                                           d_out_indices_.data(), d_out_values_.data(), stream.get()),
+              "zcgvs_sharded_rescore_search");
+    } else {
+        check(zcgvs_sharded_search(handle_, shard.deviceData(), static_cast<int>(shard.dtype()), shard.scale(),
+                                   shard.rowScales(), shard.docCount(), dim, d_queries_.data(), batch, params.d_mask,
+                                   static_cast<int>(params.metric), params.k, flags, d_out_indices_.data(),
+                                   d_out_values_.data(), stream.get()),
+              "zcgvs_sharded_search");
+    }
+    current_k_ = params.k;
+    current_batch_ = batch;
+}
+
+HostTopK ShardedSearcher::copyResultToHost(const CudaStream& stream) {
+    if (current_k_ == 0) throw std::runtime_error("zcgvs: copyResultToHost called before search");
+    const std::size_t elements = static_cast<std::size_t>(current_batch_) * static_cast<std::size_t>(current_k_);
+    d_out_indices_.copyToHost(h_out_indices_.data(), elements, stream.get());
+    d_out_values_.copyToHost(h_out_values_.data(), elements, stream.get());
+    std::uint32_t word = 0;
+    int comm_error = 0;
+    check(zcgvs_sharded_status(handle_, &word, &comm_error, stream.get()), "zcgvs_sharded_status");
+    if (comm_error != 0) throw std::runtime_error("zcgvs: NCCL reported asynchronous error " + std::to_string(comm_error));
+    if (word != 0u) {
+        check(zcgvs_sharded_clear_status(handle_, stream.get()), "zcgvs_sharded_clear_status");
+        stream.synchronize();
+        throw std::runtime_error("zcgvs: search incomplete, " + describeDeviceStatus(word));
+    }
+    HostTopK result;
+    result.batch = current_batch_;
+    result.k = current_k_;
+    result.indices.assign(h_out_indices_.data(), h_out_indices_.data() + elements);
+    result.scores.assign(h_out_values_.data(), h_out_values_.data() + elements);
     return result;
 }
 
