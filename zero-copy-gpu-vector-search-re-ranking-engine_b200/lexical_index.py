@@ -9,12 +9,18 @@ additions per document keep their order).
 
 ``build_csr`` computes the reference builder's BM25 weights from token counts
 (build_lexical.py:143-154): idf = ln(1 + (N - df + 0.5) / (df + 0.5)),
-w = idf * tf * (k1 + 1) / (tf + k1 * (1 - b + b * len / avgdl)), in float64, stored as fp32.
+w = idf * tf * (k1 + 1) / (tf + k1 * (1 - b + b * len / avgdl)), in float64, stored as fp32, with
+the builder's operation order and its average-length fallback (1 when the mean length is 0), so
+the weights equal the reference builder's bit for bit (tests/golden/lexical.npz holds indexes
+written by the reference builder itself). ``token_counts`` turns tokenised documents into its
+inputs the way the builder counts them.
 ``synthetic_corpus`` / ``synthetic_queries`` draw the seeded hybrid workload (Poisson document
 lengths, Zipf term frequencies) on any torch device.
 """
 
 from __future__ import annotations
+
+import math
 
 import numpy as np
 
@@ -41,12 +47,43 @@ def postings_sorted(offsets, docs) -> bool:
     return bool(starts[drops].all())
 
 
+def average_length(lengths) -> float:
+    """The builder's average document length (build_lexical.py:139-142): the float64 mean of the
+    token counts, 1.0 when it is not positive (an empty corpus, or only empty documents)."""
+    values = np.asarray(lengths.cpu() if hasattr(lengths, "cpu") else lengths, dtype=np.float64)
+    mean = float(values.mean()) if values.size else 0.0
+    return mean if mean > 0.0 else 1.0
+
+
+def token_counts(doc_tokens, vocab: int, max_doc_tokens: int = 512):
+    """(doc_ids, term_ids, tf, lengths) numpy int64 arrays from per-document token id lists, as
+    the builder counts them (build_lexical.py:127-137): each document cut to max_doc_tokens
+    tokens, its length the number kept, and one (doc, term, tf) entry per distinct in-vocabulary
+    term."""
+    docs, terms, counts, lengths = [], [], [], []
+    for d, tokens in enumerate(doc_tokens):
+        kept = np.asarray(tokens, dtype=np.int64)[:max_doc_tokens]
+        lengths.append(kept.size)
+        kept = kept[(kept >= 0) & (kept < vocab)]
+        uniq, tf = np.unique(kept, return_counts=True)
+        docs.append(np.full(uniq.size, d, dtype=np.int64))
+        terms.append(uniq)
+        counts.append(tf)
+    cat = (lambda parts: np.concatenate(parts) if parts else np.zeros(0, dtype=np.int64))
+    return cat(docs), cat(terms), cat(counts).astype(np.int64), np.asarray(lengths, dtype=np.int64)
+
+
 def build_csr(doc_ids, term_ids, tf, lengths, vocab: int, k1: float = 1.2, b: float = 0.75):
     """BM25 CSR index from unique (doc, term) pairs with term frequencies.
 
     doc_ids, term_ids, tf: torch int64 tensors of the pairs (any order); lengths: torch tensor
     [n_docs] of document token counts. Returns torch (offsets int64 [vocab + 1], docs int32,
     weights fp32) on the inputs' device, postings sorted by (term, doc).
+
+    The per-posting arithmetic runs as float64 torch operations on the inputs' device, each one
+    rounded on its own in the builder's order; the two values torch could round differently from
+    the builder are taken as the builder takes them: idf from Python's math.log once per
+    document frequency, and the mean length from numpy (average_length).
     """
     import torch
 
@@ -54,15 +91,17 @@ def build_csr(doc_ids, term_ids, tf, lengths, vocab: int, k1: float = 1.2, b: fl
     key = term_ids * n_docs + doc_ids
     order = torch.argsort(key)
     doc_ids, term_ids, tf = doc_ids[order], term_ids[order], tf[order].to(torch.float64)
-    df = torch.bincount(term_ids, minlength=vocab).to(torch.float64)
-    avgdl = float(lengths.to(torch.float64).mean()) if n_docs else 0.0
-    if avgdl <= 0.0:
-        avgdl = 1.0
-    idf = torch.log(1.0 + (n_docs - df + 0.5) / (df + 0.5))
+    df_count = torch.bincount(term_ids, minlength=vocab)
+    avgdl = average_length(lengths)
+    df_host = df_count.cpu().numpy()
+    idf_host = np.zeros(vocab, dtype=np.float64)
+    for value in np.unique(df_host[df_host > 0]):
+        idf_host[df_host == value] = math.log(1.0 + (n_docs - int(value) + 0.5) / (int(value) + 0.5))
+    idf = torch.from_numpy(idf_host).to(doc_ids.device)
     norm = k1 * (1.0 - b + b * lengths.to(torch.float64)[doc_ids] / avgdl)
     weights = (idf[term_ids] * (tf * (k1 + 1.0)) / (tf + norm)).to(torch.float32)
     offsets = torch.zeros(vocab + 1, dtype=torch.int64, device=doc_ids.device)
-    offsets[1:] = torch.cumsum(torch.bincount(term_ids, minlength=vocab), 0)
+    offsets[1:] = torch.cumsum(df_count, 0)
     return offsets, doc_ids.to(torch.int32), weights
 
 
