@@ -1,13 +1,14 @@
 // The search driver (the reference's Searcher, include/zcgvs/search/searcher.hpp:32-63), over the
 // fused kernels of this library: one zcgvs_scan_topk (or zcgvs_hybrid_topk with a lexical index)
 // per search, followed by zcgvs_rescore_topk when a rescore store is attached. Same public
-// interface and exceptions; optional CUDA-graph replay keyed by everything the launches capture.
+// interface and exceptions; optional CUDA-graph replay keyed by the launches' own argument list.
 // Not thread-safe (one Searcher per thread / stream / GPU), like the reference.
 #pragma once
 
 #include <cuda_runtime.h>
 
 #include <cstdint>
+#include <vector>
 
 #include "zcgvs/core/cuda_stream.hpp"
 #include "zcgvs/core/device_buffer.hpp"
@@ -49,27 +50,12 @@ public:
     bool hasLexicalIndex() const { return lexical_index_ != nullptr; }
 
 private:
-    struct GraphKey {
-        const void* corpus = nullptr;
-        const void* rescore_corpus = nullptr;
-        const void* lexical_index = nullptr;
-        const std::uint8_t* mask = nullptr;
-        std::uint64_t generation = 0;
-        std::int64_t doc_count = 0;
-        int k = 0;
-        int batch = 0;
-        int rescore_candidates = 0;
-        int lexical_stride = 0;
-        int metric = 0;
-        float dense_weight = 1.0f;
-
-        bool operator==(const GraphKey& other) const;
-    };
-
     void validate(int dim, int batch, const SearchParams& params, std::int64_t doc_count) const;
     void ensureCapacity(std::int64_t doc_count, int batch, const SearchParams& params);
-    void recordPipeline(std::int64_t doc_count, int batch, const SearchParams& params, cudaStream_t stream);
-    GraphKey makeKey(std::int64_t doc_count, int batch, const SearchParams& params) const;
+    // Launches one search on `stream`, or, with `key`, only lists the launches' arguments: the
+    // key of its CUDA graph, which replays only for searches with identical launches.
+    void recordPipeline(std::int64_t doc_count, int batch, const SearchParams& params, cudaStream_t stream,
+                        std::vector<std::uint64_t>* key = nullptr);
     bool lexicalEnabled(const SearchParams& params) const;
     bool rescoreEnabled(const SearchParams& params) const;
     void destroyGraph() noexcept;
@@ -95,9 +81,8 @@ private:
     cudaEvent_t ev_start_ = nullptr;
     cudaEvent_t ev_end_ = nullptr;
     cudaGraphExec_t graph_exec_ = nullptr;
-    GraphKey graph_key_{};
+    std::vector<std::uint64_t> graph_key_;
     bool graph_valid_ = false;
-    std::uint64_t generation_ = 0;
     std::uint64_t graph_captures_ = 0;
     std::uint64_t graph_launches_ = 0;
 

@@ -528,11 +528,27 @@ bool grow(Buffer& buffer, std::size_t required) {
 
 }  // namespace
 
-bool Searcher::GraphKey::operator==(const GraphKey& o) const {
-    return corpus == o.corpus && rescore_corpus == o.rescore_corpus && lexical_index == o.lexical_index &&
-           mask == o.mask && generation == o.generation && doc_count == o.doc_count && k == o.k && batch == o.batch &&
-           rescore_candidates == o.rescore_candidates && lexical_stride == o.lexical_stride && metric == o.metric &&
-           dense_weight == o.dense_weight;
+// The bit pattern of one launch argument, for the graph key.
+std::uint64_t argBits(const void* p) { return static_cast<std::uint64_t>(reinterpret_cast<std::uintptr_t>(p)); }
+std::uint64_t argBits(std::int64_t v) { return static_cast<std::uint64_t>(v); }
+std::uint64_t argBits(int v) { return static_cast<std::uint64_t>(static_cast<std::uint32_t>(v)); }
+std::uint64_t argBits(std::size_t v) { return static_cast<std::uint64_t>(v); }
+std::uint64_t argBits(float v) {
+    std::uint32_t bits = 0;
+    std::memcpy(&bits, &v, sizeof(bits));
+    return bits;
+}
+
+// Either launches fn(args..., stream) or, when `key` is given, appends the arguments' bits to it
+// instead: the graph key of a captured search is the exact argument list of its launches.
+template <typename Fn, typename... Args>
+void launchOrKey(std::vector<std::uint64_t>* key, const char* name, Fn fn, cudaStream_t stream, Args... args) {
+    if (key != nullptr) {
+        key->push_back(argBits(reinterpret_cast<const void*>(fn)));
+        (key->push_back(argBits(args)), ...);
+        return;
+    }
+    check(fn(args..., stream), name);
 }
 
 Searcher::Searcher(const EmbeddingStore& store) : store_(store), dim_(store.dim()) {
@@ -632,57 +648,37 @@ void Searcher::ensureCapacity(std::int64_t doc_count, int batch, const SearchPar
     grow(h_out_indices_, queries * static_cast<std::size_t>(params.k));
     grow(h_out_values_, queries * static_cast<std::size_t>(params.k));
     grow(h_status_, 1);
-    if (reallocated) {
-        ++generation_;
-        destroyGraph();
-    }
+    if (reallocated) destroyGraph();
 }
 
-void Searcher::recordPipeline(std::int64_t doc_count, int batch, const SearchParams& params, cudaStream_t stream) {
+void Searcher::recordPipeline(std::int64_t doc_count, int batch, const SearchParams& params, cudaStream_t stream,
+                              std::vector<std::uint64_t>* key) {
     const bool rescore = rescoreEnabled(params);
     const int width = rescore ? params.rescore_candidates : params.k;
     int* ids = rescore ? d_coarse_indices_.data() : d_out_indices_.data();
     float* scores = rescore ? d_coarse_values_.data() : d_out_values_.data();
     const int dtype = static_cast<int>(store_.dtype());
     const int metric = static_cast<int>(params.metric);
+    const std::int64_t n = doc_count;
     if (lexicalEnabled(params)) {
-        check(zcgvs_hybrid_topk(store_.deviceData(), dtype, store_.scale(), store_.rowScales(), doc_count, dim_, d_queries_.data(),
-                                batch, params.d_mask, metric, lexical_index_->deviceOffsets(),
-                                lexical_index_->devicePostingDocs(), lexical_index_->devicePostingWeights(),
-                                lexical_index_->vocabSize(), d_query_terms_.data(), params.lexical_stride,
-                                params.dense_weight, width, ids, scores, d_workspace_.data(), d_workspace_.bytes(), stream),
-              "zcgvs_hybrid_topk");
+        launchOrKey(key, "zcgvs_hybrid_topk", zcgvs_hybrid_topk, stream, store_.deviceData(), dtype, store_.scale(),
+                    store_.rowScales(), n, dim_, static_cast<const float*>(d_queries_.data()), batch, params.d_mask,
+                    metric, lexical_index_->deviceOffsets(), lexical_index_->devicePostingDocs(),
+                    lexical_index_->devicePostingWeights(), lexical_index_->vocabSize(),
+                    static_cast<const int*>(d_query_terms_.data()), params.lexical_stride, params.dense_weight, width,
+                    ids, scores, static_cast<void*>(d_workspace_.data()), d_workspace_.bytes());
     } else {
-        check(zcgvs_scan_topk(store_.deviceData(), dtype, store_.scale(), store_.rowScales(), doc_count, dim_, d_queries_.data(),
-                              batch, params.d_mask, metric, width, 0, ids, scores, d_workspace_.data(),
-                              d_workspace_.bytes(), stream),
-              "zcgvs_scan_topk");
+        launchOrKey(key, "zcgvs_scan_topk", zcgvs_scan_topk, stream, store_.deviceData(), dtype, store_.scale(),
+                    store_.rowScales(), n, dim_, static_cast<const float*>(d_queries_.data()), batch, params.d_mask,
+                    metric, width, 0, ids, scores, static_cast<void*>(d_workspace_.data()), d_workspace_.bytes());
     }
     if (rescore) {
-        check(zcgvs_rescore_topk(rescore_store_->deviceData(), static_cast<int>(rescore_store_->dtype()),
-                                 rescore_store_->scale(), rescore_store_->rowScales(), rescore_store_->docCount(), dim_,
-                                 d_queries_.data(),
-                                 batch, d_coarse_indices_.data(), width, metric, params.k, d_out_indices_.data(),
-                                 d_out_values_.data(), stream),
-              "zcgvs_rescore_topk");
+        launchOrKey(key, "zcgvs_rescore_topk", zcgvs_rescore_topk, stream, rescore_store_->deviceData(),
+                    static_cast<int>(rescore_store_->dtype()), rescore_store_->scale(), rescore_store_->rowScales(),
+                    rescore_store_->docCount(), dim_, static_cast<const float*>(d_queries_.data()), batch,
+                    static_cast<const int*>(d_coarse_indices_.data()), width, metric, params.k, d_out_indices_.data(),
+                    d_out_values_.data());
     }
-}
-
-Searcher::GraphKey Searcher::makeKey(std::int64_t doc_count, int batch, const SearchParams& params) const {
-    GraphKey key;
-    key.corpus = store_.deviceData();
-    key.rescore_corpus = rescoreEnabled(params) ? rescore_store_->deviceData() : nullptr;
-    key.lexical_index = lexicalEnabled(params) ? static_cast<const void*>(lexical_index_) : nullptr;
-    key.mask = params.d_mask;
-    key.generation = generation_;
-    key.doc_count = doc_count;
-    key.k = params.k;
-    key.batch = batch;
-    key.rescore_candidates = rescoreEnabled(params) ? params.rescore_candidates : 0;
-    key.lexical_stride = lexicalEnabled(params) ? params.lexical_stride : 0;
-    key.metric = static_cast<int>(params.metric);
-    key.dense_weight = lexicalEnabled(params) ? params.dense_weight : 1.0f;
-    return key;
 }
 
 void Searcher::search(const float* host_queries, int dim, int batch, const SearchParams& params, const CudaStream& stream) {
@@ -702,8 +698,9 @@ void Searcher::search(const float* host_queries, int dim, int batch, const Searc
 
     const bool graph_path = params.use_graph;
     if (graph_path) {
-        const GraphKey key = makeKey(doc_count, batch, params);
-        if (!graph_valid_ || !(graph_key_ == key)) {
+        std::vector<std::uint64_t> key;
+        recordPipeline(doc_count, batch, params, stream.get(), &key);
+        if (!graph_valid_ || graph_key_ != key) {
             // Capture outside the timed region; the uploads above are drained first so the graph
             // holds the search and nothing else.
             stream.synchronize();
@@ -722,7 +719,7 @@ void Searcher::search(const float* host_queries, int dim, int batch, const Searc
             cudaGraphDestroy(graph);
             ZCGVS_CUDA_CHECK(status);
             graph_valid_ = true;
-            graph_key_ = key;
+            graph_key_ = std::move(key);
             ++graph_captures_;
         }
     }
