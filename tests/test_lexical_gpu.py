@@ -194,3 +194,142 @@ def test_hybrid_sorted_postings_with_runs_and_ragged_tail(zc, orc):
                                        row_scales=row_scales)
     np.testing.assert_array_equal(idx.cpu().numpy(), ref_idx)
     np.testing.assert_array_equal(val.cpu().numpy(), ref_val)
+
+
+def _launch_counts(zc, fn):
+    """Runs fn with the library's kernel timing on; returns (scan, lexical, hybrid_select) launch counts."""
+    import torch
+
+    zc.kernel_timing(True)
+    try:
+        fn()
+        torch.cuda.synchronize()
+        return tuple(zc.kernel_timing_read(t)[1] for t in ("scan", "lexical", "hybrid_select"))
+    finally:
+        zc.kernel_timing(False)
+
+
+@pytest.mark.parametrize("k", [1, 10, 32, 33, 150, 300])
+def test_hybrid_one_query_edge_cases_bit_exact(zc, orc, k):
+    """One query per call takes the hybrid scan (dense rows and BM25 accumulated in the same
+    CTAs) and the blend + top-k kernel for k <= 192, the lexical kernel and the blending scan
+    above: masked documents, padding / out-of-vocabulary / repeated term ids and a query without
+    terms, bit-exact against the oracle on the per-row int8 store (exact integer dot products)."""
+    import torch
+
+    n, dim, vocab, batch = 20000, 512, 2000, 4
+    offsets, docs, weights, terms, corpus, queries = zipf_case(orc, n, dim, vocab, batch, 21)
+    terms[1, :] = -1
+    terms[2, 0] = vocab + 5
+    terms[3, 1] = terms[3, 0]
+    mask = np.ones(n, dtype=np.uint8)
+    mask[::3] = 0
+    storage, _, row_scales = orc.encode(corpus, 4)
+    index = zc.LexicalIndex(offsets, docs, weights)
+    d_storage, d_scales, d_mask, d_queries, d_terms = (dev(storage), dev(row_scales), dev(mask), dev(queries),
+                                                       dev(terms))
+    ws = zc.Workspace()
+    fused = k <= 192
+    for w in (0.0, 0.3, 1.0):
+        for use_mask in (False, True):
+            ref_idx, ref_val = orc.hybrid_topk(storage, 4, dim, queries, k, offsets, docs, weights, vocab, terms, w,
+                                               row_scales=row_scales, mask=mask if use_mask else None)
+            for q in range(batch):
+                out = []
+                counts = _launch_counts(zc, lambda: out.append(zc.hybrid_topk(
+                    d_storage, 4, dim, d_queries[q:q + 1], k, index, d_terms[q:q + 1], w, row_scales=d_scales,
+                    mask=d_mask if use_mask else None, workspace=ws)))
+                assert counts == ((1, 0, 1) if fused else (1, 1, 0))
+                idx, val = out[0]
+                np.testing.assert_array_equal(idx.cpu().numpy()[0], ref_idx[q])
+                np.testing.assert_array_equal(val.cpu().numpy()[0], ref_val[q])
+    assert ws.status() == 0
+
+
+@pytest.mark.parametrize("n", [1, 63, 64, 1000, 9473, 150000])
+def test_hybrid_one_query_corpus_sizes(zc, orc, n):
+    """Corpora of one document, less than one tile, one tile, fewer tiles than SMs, a ragged last
+    tile and more tiles than SMs: the hybrid scan's CTA ranges (its BM25 accumulator spans the
+    CTA's tiles) and the select kernel's ranges (n split evenly over the CTAs) differ, and every
+    document must be scored once."""
+    import torch
+
+    dim, vocab = 768, 500
+    k = min(10, n)
+    offsets, docs, weights, terms, corpus, queries = zipf_case(orc, n, dim, vocab, 2, 41)
+    storage, _, row_scales = orc.encode(corpus, 4)
+    index = zc.LexicalIndex(offsets, docs, weights)
+    for w in (0.0, 0.5):
+        ref_idx, ref_val = orc.hybrid_topk(storage, 4, dim, queries, k, offsets, docs, weights, vocab, terms, w,
+                                           row_scales=row_scales)
+        for q in range(2):
+            out = []
+            counts = _launch_counts(zc, lambda: out.append(zc.hybrid_topk(
+                dev(storage), 4, dim, dev(queries[q:q + 1]), k, index, dev(terms[q:q + 1]), w,
+                row_scales=dev(row_scales))))
+            assert counts == (1, 0, 1)
+            idx, val = out[0]
+            np.testing.assert_array_equal(idx.cpu().numpy()[0], ref_idx[q])
+            np.testing.assert_array_equal(val.cpu().numpy()[0], ref_val[q])
+
+
+@pytest.mark.parametrize("name,dtype,dim", [("f16", 1, 384), ("f32", 0, 256), ("i8row", 4, 768)])
+def test_hybrid_one_query_runs_and_ragged_tail(zc, orc, name, dtype, dim):
+    """The hand-made index with runs of equal documents and odd list lengths, one query per call
+    (the hybrid scan's lexical warps): with w = 0 the result is lexical / max alone, a sequential
+    sum on both sides, bit-exact for every storage type."""
+    import torch
+
+    n, vocab, k, batch = 7000, 40, 50, 5
+    rng = np.random.default_rng(78)
+    lists = []
+    for t in range(vocab):
+        df = int(rng.integers(1, 900)) | 1
+        lists.append(np.sort(rng.integers(0, n, size=df)).astype(np.int32))
+    offsets = np.zeros(vocab + 1, dtype=np.int64)
+    offsets[1:] = np.cumsum([len(x) for x in lists])
+    docs = np.concatenate(lists)
+    weights = rng.uniform(0.1, 3.0, size=docs.shape[0]).astype(np.float32)
+    terms = np.full((batch, 6), -1, dtype=np.int32)
+    for q in range(batch):
+        terms[q, :3 + q % 3] = rng.choice(vocab, size=3 + q % 3, replace=False)
+    corpus = orc.normal_rows(n, dim, 33)
+    queries = orc.normal_rows(batch, dim, 34)
+    storage, scale, row_scales = orc.encode(corpus, dtype)
+    st = dev(storage.view(np.int16) if storage.dtype == np.uint16 else storage)
+    index = zc.LexicalIndex(offsets, docs, weights)
+    ref_idx, ref_val = orc.hybrid_topk(storage, dtype, dim, queries, k, offsets, docs, weights, vocab, terms, 0.0,
+                                       scale=scale, row_scales=row_scales, metric=0)
+    for q in range(batch):
+        out = []
+        counts = _launch_counts(zc, lambda: out.append(zc.hybrid_topk(
+            st, dtype, dim, dev(queries[q:q + 1]), k, index, dev(terms[q:q + 1]), 0.0, scale=scale,
+            row_scales=None if row_scales is None else dev(row_scales), metric=0)))
+        assert counts == (1, 0, 1)
+        idx, val = out[0]
+        np.testing.assert_array_equal(idx.cpu().numpy()[0], ref_idx[q])
+        np.testing.assert_array_equal(val.cpu().numpy()[0], ref_val[q])
+
+
+def test_hybrid_one_query_windowed_accumulator(zc, orc):
+    """1.3M documents: a CTA's documents no longer fit the BM25 accumulator beside a four-stage
+    ring, so the hybrid scan's lexical warps score them in two windows (two rounds of posting
+    searches); bit-exact against the oracle on the per-row int8 store."""
+    import torch
+
+    n, dim, vocab = 1_300_000, 768, 5000
+    offsets, docs, weights, terms, corpus, queries = zipf_case(orc, n, dim, vocab, 2, 51)
+    storage, _, row_scales = orc.encode(corpus, 4)
+    index = zc.LexicalIndex(offsets, docs, weights)
+    d_storage, d_scales = dev(storage), dev(row_scales)
+    for w in (0.0, 0.5):
+        ref_idx, ref_val = orc.hybrid_topk(storage, 4, dim, queries, 10, offsets, docs, weights, vocab, terms, w,
+                                           row_scales=row_scales)
+        for q in range(2):
+            out = []
+            counts = _launch_counts(zc, lambda: out.append(zc.hybrid_topk(
+                d_storage, 4, dim, dev(queries[q:q + 1]), 10, index, dev(terms[q:q + 1]), w, row_scales=d_scales)))
+            assert counts == (1, 0, 1)
+            idx, val = out[0]
+            np.testing.assert_array_equal(idx.cpu().numpy()[0], ref_idx[q])
+            np.testing.assert_array_equal(val.cpu().numpy()[0], ref_val[q])

@@ -4,23 +4,11 @@
 // every posting weight into a [N] score vector with float atomicAdd, so the order of the
 // additions (and the low bits of the result) changes from run to run; its own test compares
 // with a tolerance (tests/cpp/test_lexical.cu:118-126). Here the document space is cut into
-// contiguous ranges, one per CTA, and each CTA walks the query's term slots in order:
-//
-//   * For every slot a warp finds the CTA's slice of that term's posting list with a 32-way
-//     search (about log32(df) dependent loads instead of log2(df)); posting lists are sorted by
-//     document within each term, as the reference builder writes them
-//     (python/zcgvs_tools/build_lexical.py:143-162).
-//   * The slice is added into a shared-memory accumulator of the CTA's documents. A run of
-//     equal document ids (possible in hand-made indexes) is summed by one thread in posting
-//     order, and slots are separated by a barrier, so every document's score is the exact
-//     sequential sum in (slot, posting) order: the CPU loop of tests/cpp/test_lexical.cu:71-80.
-//   * Each CTA writes its documents' scores and its max(0, max score) to the workspace; the
-//     scan kernel reduces those partial maxima (src/cuda/lexical.cu:44-64 does it with a float
-//     atomicMax) and blends lexical and dense scores before its top-k.
-//   * Indexes whose postings are in any order (the reference launcher's contract, used by
-//     zcgvs_bm25) take a second path with the same sums: one warp per CTA walks each term's whole
-//     list in posting order, grouping equal documents of a 32-posting step (match_any) and adding
-//     them in lane order. It reads every posting once per CTA, so it is the slow path.
+// contiguous ranges, one per CTA, and each CTA walks the query's term slots in order with the
+// accumulation of lexical_device.cuh (every document's score is the exact sequential sum in
+// (slot, posting) order). Each CTA writes its documents' scores and its max(0, max score) to the
+// workspace; the scan kernel reduces those partial maxima (src/cuda/lexical.cu:44-64 does it
+// with a float atomicMax) and blends lexical and dense scores before its top-k.
 #include <cuda_runtime.h>
 
 #include <algorithm>
@@ -30,6 +18,7 @@
 
 #include "host_common.h"
 #include "lexical.h"
+#include "lexical_device.cuh"
 #include "zcgvs_sm100.h"
 
 namespace zc {
@@ -38,61 +27,17 @@ namespace {
 
 constexpr int kLexThreads = 512;
 constexpr int kLexWarps = kLexThreads / 32;
-constexpr int kLexSlots = 128;          // term slots searched per round
 constexpr int kLexMaxDocsPerCta = 32768;  // 128 KB accumulator
 
 struct LexParams {
-    const long long* offsets;
-    const int* docs;
-    const float* weights;
-    int vocab;
+    LexIndex index;
     const int* terms;       // [batch, stride]
     int stride;
-    long long n;
     int docs_per_cta;
     const float* init;      // [batch, n] scores to add onto, or nullptr (start at 0)
     float* out;             // [batch, n]
     float* part_max;        // [batch, gridDim.x] or nullptr
-    int sorted;             // postings sorted by document within each term (else: any order)
-    int vec;                // sorted, docs and weights 16-byte aligned: 16-byte posting loads
 };
-
-// First index in [lo, hi) whose document id is >= target (hi if none), for sorted docs[].
-// Whole warp; 32 probes per step.
-__device__ long long lower_bound_warp(const int* __restrict__ docs, long long lo, long long hi, int target,
-                                      int lane) {
-    while (hi - lo > 32) {
-        const long long step = (hi - lo + 31) / 32;
-        const long long pos = lo + lane * step;
-        const bool less = pos < hi && __ldg(docs + pos) < target;
-        const int c = __popc(__ballot_sync(0xffffffffu, less));
-        if (c == 0) return lo;
-        const long long next_hi = lo + static_cast<long long>(c) * step;
-        lo += static_cast<long long>(c - 1) * step + 1;
-        hi = min(hi, next_hi);
-    }
-    const long long pos = lo + lane;
-    const bool less = pos < hi && __ldg(docs + pos) < target;
-    return lo + __popc(__ballot_sync(0xffffffffu, less));
-}
-
-// lower_bound_warp with a first round of 32 probes `step` apart around `guess` (where the target
-// would sit if the list's documents were spread evenly over [0, n)); the answer's side of that
-// window is then searched as usual. Exact for any sorted list; for evenly spread lists the
-// window holds the answer and about two dependent loads are saved per search.
-__device__ long long lower_bound_hint(const int* __restrict__ docs, long long lo, long long hi, int target,
-                                      long long guess, long long step, int lane) {
-    if (hi - lo > 64) {
-        const long long pos = min(max(guess + static_cast<long long>(lane - 16) * step, lo), hi - 1);
-        const bool less = __ldg(docs + pos) < target;  // a prefix of the lanes (positions ascend)
-        const int c = __popc(__ballot_sync(0xffffffffu, less));
-        const long long below = __shfl_sync(0xffffffffu, pos, max(c - 1, 0));
-        const long long at = __shfl_sync(0xffffffffu, pos, min(c, 31));
-        if (c > 0) lo = below + 1;   // docs[below] < target
-        if (c < 32) hi = at + 1;     // docs[at] >= target
-    }
-    return lower_bound_warp(docs, lo, hi, target, lane);
-}
 
 __global__ void __launch_bounds__(kLexThreads) lexical_kernel(const LexParams p) {
     extern __shared__ __align__(16) float acc[];
@@ -104,185 +49,20 @@ __global__ void __launch_bounds__(kLexThreads) lexical_kernel(const LexParams p)
     const int lane = tid & 31;
     const int warp = tid >> 5;
     const int q = blockIdx.y;
+    const long long n = p.index.n;
     const long long d0 = static_cast<long long>(blockIdx.x) * p.docs_per_cta;
-    const int count = static_cast<int>(min(static_cast<long long>(p.docs_per_cta), p.n - d0));
-    const size_t row = static_cast<size_t>(q) * p.n;
+    const int count = static_cast<int>(min(static_cast<long long>(p.docs_per_cta), n - d0));
+    const size_t row = static_cast<size_t>(q) * n;
     const int* terms = p.terms + static_cast<size_t>(q) * p.stride;
     // Postings in the index (CSR end): the 16-byte loads never reach past it.
-    const long long total = p.vec ? __ldg(p.offsets + p.vocab) : 0;
+    const long long total = p.index.vec ? __ldg(p.index.offsets + p.index.vocab) : 0;
 
     for (int i = tid; i < count; i += kLexThreads) acc[i] = p.init != nullptr ? p.init[row + d0 + i] : 0.0f;
-
     for (int t0 = 0; t0 < p.stride; t0 += kLexSlots) {
-        const int slots = min(kLexSlots, p.stride - t0);
-        __syncthreads();  // the previous round's slices are consumed
-        for (int t = warp; t < slots; t += kLexWarps) {
-            const int term = __ldg(terms + t0 + t);
-            long long lo = 0, hi = 0;
-            if (term >= 0 && term < p.vocab) {
-                const long long begin = __ldg(p.offsets + term);
-                const long long end = __ldg(p.offsets + term + 1);
-                if (p.sorted) {
-                    // Interpolated first probes: a window of +-16 steps covers about three standard
-                    // deviations of a randomly spread list's position (sqrt(df) / 2 at most).
-                    const long long df = end - begin;
-                    const double per_doc = static_cast<double>(df) / static_cast<double>(p.n);
-                    const long long step = 1 + static_cast<long long>(0.1 * sqrt(static_cast<double>(df)));
-                    lo = lower_bound_hint(p.docs, begin, end, static_cast<int>(d0),
-                                          begin + static_cast<long long>(per_doc * static_cast<double>(d0)), step, lane);
-                    hi = lower_bound_hint(p.docs, lo, end, static_cast<int>(d0 + count),
-                                          begin + static_cast<long long>(per_doc * static_cast<double>(d0 + count)), step,
-                                          lane);
-                } else {
-                    lo = begin;
-                    hi = end;
-                }
-            }
-            if (lane == 0) {
-                s_lo[t] = lo;
-                s_hi[t] = hi;
-            }
-        }
-        __syncthreads();
-        if (!p.sorted) {
-            // Any posting order: warp 0 walks each term's whole list in posting order, 32 at a time.
-            // Postings of one document inside a step are grouped (match_any) and added in lane
-            // order, so every sum keeps the sequential (slot, posting) order.
-            if (warp == 0) {
-                for (int t = 0; t < slots; ++t) {
-                    const long long lo = s_lo[t];
-                    const long long hi = s_hi[t];
-                    for (long long base = lo; base < hi; base += 32) {
-                        const long long i = base + lane;
-                        const int doc = i < hi ? __ldg(p.docs + i) : -1;
-                        const bool mine = doc >= d0 && doc < d0 + count;
-                        const float w = mine ? __ldg(p.weights + i) : 0.0f;
-                        const uint32_t peers = __match_any_sync(0xffffffffu, mine ? doc : -1 - lane);
-                        const int rank = __popc(peers & ((1u << lane) - 1u));
-                        int rounds = mine ? __popc(peers) : 0;
-#pragma unroll
-                        for (int off = 16; off > 0; off >>= 1) rounds = max(rounds, __shfl_xor_sync(0xffffffffu, rounds, off));
-                        for (int r = 0; r < rounds; ++r) {
-                            if (mine && rank == r) acc[doc - d0] = __fadd_rn(acc[doc - d0], w);
-                            __syncwarp();
-                        }
-                    }
-                }
-            }
-            __syncthreads();
-            continue;
-        }
-        if (p.vec) {
-            // 16-byte posting groups, software-pipelined across slots. A step is one group per
-            // thread of one slot (thread tid owns group g0 + tid); the loads of the next two steps
-            // are in flight while a step's additions run, across the barrier that closes a slot
-            // (loads never touch the accumulator), so a slot's memory latency overlaps the work
-            // of the slots before it. Slots without postings here are skipped. A posting is the
-            // head of its run unless the posting before it (the same thread's, the previous
-            // lane's last one, or for lane 0 a load) holds the same document.
-            struct Step {
-                int t;
-                long long g0;
-            };
-            struct Group {
-                int4 dv;
-                float4 wv;
-                int before;
-            };
-            auto g_lo = [&](int t) { return s_lo[t] >> 2; };
-            auto g_hi = [&](int t) { return (s_hi[t] + 3) >> 2; };
-            auto first_from = [&](int t) {
-                while (t < slots && g_lo(t) >= g_hi(t)) ++t;
-                return Step{t, t < slots ? g_lo(t) : 0};
-            };
-            auto advance = [&](Step c) {
-                if (c.t >= slots) return c;
-                const long long g0 = c.g0 + kLexThreads;
-                return g0 < g_hi(c.t) ? Step{c.t, g0} : first_from(c.t + 1);
-            };
-            auto load = [&](Step c, Group& b) {
-                b.dv = make_int4(-1, -1, -1, -1);
-                b.wv = make_float4(0.f, 0.f, 0.f, 0.f);
-                b.before = -1;
-                if (c.t >= slots) return;
-                const long long g = c.g0 + tid;
-                if (g >= g_hi(c.t)) return;
-                if (4 * g + 3 < total) {
-                    b.dv = __ldg(reinterpret_cast<const int4*>(p.docs) + g);
-                    b.wv = __ldg(reinterpret_cast<const float4*>(p.weights) + g);
-                } else {
-                    // The index's last partial group: element loads.
-                    int dd[4] = {-1, -1, -1, -1};
-                    float ww[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        if (4 * g + e < total) {
-                            dd[e] = __ldg(p.docs + 4 * g + e);
-                            ww[e] = __ldg(p.weights + 4 * g + e);
-                        }
-                    }
-                    b.dv = make_int4(dd[0], dd[1], dd[2], dd[3]);
-                    b.wv = make_float4(ww[0], ww[1], ww[2], ww[3]);
-                }
-                if (lane == 0 && 4 * g > s_lo[c.t]) b.before = __ldg(p.docs + 4 * g - 1);
-            };
-            auto process = [&](Step c, const Group& b) {
-                const long long lo = s_lo[c.t];
-                const long long hi = s_hi[c.t];
-                const long long g = c.g0 + tid;
-                const int up = __shfl_up_sync(0xffffffffu, b.dv.w, 1);
-                if (g >= g_hi(c.t)) return;
-                const int d[4] = {b.dv.x, b.dv.y, b.dv.z, b.dv.w};
-                const float w[4] = {b.wv.x, b.wv.y, b.wv.z, b.wv.w};
-                int prev = lane == 0 ? b.before : up;
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                    const long long i = 4 * g + e;
-                    const int doc = d[e];
-                    const bool head = i >= lo && i < hi && (i == lo || prev != doc);
-                    prev = doc;
-                    if (!head) continue;
-                    float a = __fadd_rn(acc[doc - d0], w[e]);
-                    // The rest of a run of equal documents, in posting order (rare).
-                    for (long long j = i + 1; j < hi && __ldg(p.docs + j) == doc; ++j) {
-                        a = __fadd_rn(a, __ldg(p.weights + j));
-                    }
-                    acc[doc - d0] = a;
-                }
-            };
-            Step s0 = first_from(0);
-            Step s1 = advance(s0);
-            Group b0, b1, b2;
-            load(s0, b0);
-            load(s1, b1);
-            while (s0.t < slots) {
-                const Step s2 = advance(s1);
-                load(s2, b2);
-                process(s0, b0);
-                if (s1.t != s0.t) __syncthreads();  // slot s0.t's additions land before the next slot's
-                s0 = s1;
-                s1 = s2;
-                b0 = b1;
-                b1 = b2;
-            }
-        } else {
-            for (int t = 0; t < slots; ++t) {
-                const long long lo = s_lo[t];
-                const long long hi = s_hi[t];
-                for (long long i = lo + tid; i < hi; i += kLexThreads) {
-                    const int doc = __ldg(p.docs + i);
-                    if (i > lo && __ldg(p.docs + i - 1) == doc) continue;  // not the head of its run
-                    float a = acc[doc - d0];
-                    a = __fadd_rn(a, __ldg(p.weights + i));
-                    for (long long j = i + 1; j < hi && __ldg(p.docs + j) == doc; ++j) {
-                        a = __fadd_rn(a, __ldg(p.weights + j));
-                    }
-                    acc[doc - d0] = a;
-                }
-                __syncthreads();  // slot t's additions land before slot t + 1's
-            }
-        }
+        lex_round<kLexThreads, 0>(p.index, terms + t0, min(kLexSlots, p.stride - t0), d0, count, acc, s_lo, s_hi,
+                                  total, tid);
     }
+    __syncthreads();
 
     float best = 0.0f;
     for (int i = tid; i < count; i += kLexThreads) {
@@ -332,6 +112,22 @@ __global__ void fuse_scores_kernel(float* __restrict__ dense, const float* __res
 
 }  // namespace
 
+LexIndex lex_index(const long long* offsets, const int* docs, const float* weights, int vocab, long long n,
+                   bool sorted) {
+    LexIndex x{};
+    x.offsets = offsets;
+    x.docs = docs;
+    x.weights = weights;
+    x.vocab = vocab;
+    x.n = n;
+    x.sorted = sorted ? 1 : 0;
+    x.vec = (sorted && vocab != INT_MAX && reinterpret_cast<uintptr_t>(docs) % 16 == 0 &&
+             reinterpret_cast<uintptr_t>(weights) % 16 == 0)
+                ? 1
+                : 0;
+    return x;
+}
+
 int lexical_parts(long long n) {
     const long long sms = device_sm_count();
     long long per = (n + 2 * sms - 1) / (2 * sms);
@@ -346,22 +142,13 @@ int launch_lexical(const long long* offsets, const int* docs, const float* weigh
     const int parts = lexical_parts(n);
     const long long per = (n + parts - 1) / parts;
     LexParams p{};
-    p.offsets = offsets;
-    p.docs = docs;
-    p.weights = weights;
-    p.vocab = vocab;
+    p.index = lex_index(offsets, docs, weights, vocab, n, sorted);
     p.terms = terms;
     p.stride = stride;
-    p.n = n;
     p.docs_per_cta = static_cast<int>(per);
     p.init = init;
     p.out = out;
     p.part_max = part_max;
-    p.sorted = sorted ? 1 : 0;
-    p.vec = (sorted && vocab != INT_MAX && reinterpret_cast<uintptr_t>(docs) % 16 == 0 &&
-             reinterpret_cast<uintptr_t>(weights) % 16 == 0)
-                ? 1
-                : 0;
     const size_t smem = static_cast<size_t>(per) * sizeof(float);
     cudaError_t e = ensure_smem_optin(reinterpret_cast<const void*>(lexical_kernel));
     if (e != cudaSuccess) return fail_cuda(e, "cudaFuncSetAttribute(lexical_kernel)");

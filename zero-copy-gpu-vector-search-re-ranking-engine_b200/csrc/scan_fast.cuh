@@ -17,6 +17,14 @@
 //     candidates and is always a valid lower bound of the CTA's true k-th key.
 //   * After the last tile: every candidate at or above the threshold is selected into the CTA
 //     list (workspace), and the last CTA of the pass merges the CTA lists (as scan_kernel).
+//
+// Hybrid variant (LEX = true, one query): the selector's place goes to kFusedLexWarps lexical
+// warps that accumulate the BM25 scores of the CTA's documents (lexical_device.cuh, a named
+// barrier among themselves) while the producer and consumers stream the dense rows; consumers
+// write each row's dense score instead of selecting. The blend needs the lexical maximum over
+// every document, so it and the top-k run in the next kernel (hybrid_select.cu), which this one
+// lets start early (griddepcontrol). The posting lists are read while HBM streams the rows, so
+// the lexical pass costs no time of its own.
 #pragma once
 
 #include "scan_kernel.cuh"
@@ -35,8 +43,14 @@ constexpr int kCandCap = kFastConsumers * kRegionCap;
 constexpr int kSelE = 8;
 constexpr int kSelCap = 32 * kSelE;
 
-template <int MODE, int JC>
-__global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanParams p) {
+// Hybrid variant: lexical warps after the producer (warps kFusedLexWarp0 ...).
+constexpr int kFusedLexWarps = 3;
+constexpr int kFusedLexWarp0 = kFastConsumers + 1;
+constexpr int kFusedLexThreads = kFusedLexWarps * 32;
+constexpr int kFusedThreads = (kFastConsumers + 1 + kFusedLexWarps) * 32;
+
+template <int MODE, int JC, bool LEX = false>
+__global__ void __launch_bounds__(LEX ? kFusedThreads : kFastThreads, 1) scan_fast_kernel(const ScanParams p) {
     using Traits = ModeTraits<MODE>;
     constexpr int EPC = Traits::kEpc;
     constexpr bool kInt = (MODE == kModeI8R);
@@ -46,7 +60,8 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
     constexpr int kRowsPerWarp = RPW * RW;
     constexpr int kRowsPerStep = kFastConsumers * kRowsPerWarp;
     constexpr int kGroupShift = 3;                // log2(LPR) - log2(RW)
-    constexpr int kWarpsAll = kFastThreads / 32;
+    constexpr int kThreads = LEX ? kFusedThreads : kFastThreads;
+    constexpr int kWarpsAll = kThreads / 32;
     using QElem = typename std::conditional<kInt, int, float>::type;
 
     extern __shared__ __align__(128) uint8_t smem[];
@@ -106,8 +121,13 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
         s_sel_complete = 0;
         s_inv = (p.lex != nullptr) ? hybrid_inverse(p, pass) : 0.0f;
     }
-    for (int i = tid; i < kCandCap; i += kFastThreads) cbuf[i] = 0ull;
-    stage_queries<MODE, 1, kFastThreads>(p, qsmem, s_qscale, pass, 1, s_red);
+    if constexpr (LEX) {
+        // The select kernel only reads this kernel's outputs after griddepcontrol.wait.
+        asm volatile("griddepcontrol.launch_dependents;");
+    } else {
+        for (int i = tid; i < kCandCap; i += kFastThreads) cbuf[i] = 0ull;
+    }
+    stage_queries<MODE, 1, kThreads>(p, qsmem, s_qscale, pass, 1, s_red);
     __syncthreads();
 
     if (warp == kFastProducerWarp) {
@@ -172,7 +192,7 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
                 mbar_wait_bounded(&full[i % S], static_cast<uint32_t>((i / S) & 1), p.status, kStatusDrainTimeout);
             }
         }
-    } else if (warp == kFastSelectorWarp) {
+    } else if (!LEX && warp == kFastSelectorWarp) {
         // ---------------- selector warp ----------------
         // Follows the shared buffer and keeps the best keys it has seen in sbuf (kSelCap
         // slots). When sbuf fills it sorts it in registers, keeps k and publishes the k-th key.
@@ -220,6 +240,47 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
         // sbuf[0, scount) holds the best keys the selector saw (its top k among them, unsorted):
         // the whole CTA ranks them once the scan is over.
         if (lane == 0) s_sel_count = scount;
+    } else if (LEX && warp >= kFusedLexWarp0) {
+        // ---------------- lexical warps (hybrid variant) ----------------
+        if constexpr (LEX) {
+            __shared__ long long s_lo[kLexSlots];
+            __shared__ long long s_hi[kLexSlots];
+            __shared__ float s_lmax[kFusedLexWarps];
+            const int ltid = tid - kFusedLexWarp0 * 32;
+            float* acc = reinterpret_cast<float*>(smem + p.smem_lex_off);
+            const long long d_begin = static_cast<long long>(t_begin) * R;
+            const int count = static_cast<int>(min(static_cast<long long>(my_tiles) * R, p.n - d_begin));
+            const long long total = p.lexi.vec ? __ldg(p.lexi.offsets + p.lexi.vocab) : 0;
+            const int* terms = p.lex_terms + static_cast<size_t>(pass) * p.lex_stride;
+            float* out = p.lex_out + static_cast<size_t>(pass) * p.n;
+            float best = 0.0f;
+            // The CTA's documents, lex_window at a time (the accumulator's size).
+            for (int w0 = 0; w0 < count; w0 += p.lex_window) {
+                const long long d0 = d_begin + w0;
+                const int wc = min(p.lex_window, count - w0);
+                for (int i = ltid; i < wc; i += kFusedLexThreads) acc[i] = 0.0f;
+                for (int t0 = 0; t0 < p.lex_stride; t0 += kLexSlots) {
+                    lex_round<kFusedLexThreads, 1>(p.lexi, terms + t0, min(kLexSlots, p.lex_stride - t0), d0, wc, acc,
+                                                   s_lo, s_hi, total, ltid);
+                }
+                lex_sync<kFusedLexThreads, 1>();
+                for (int i = ltid; i < wc; i += kFusedLexThreads) {
+                    const float v = acc[i];
+                    out[d0 + i] = v;
+                    best = fmaxf(best, v);
+                }
+                lex_sync<kFusedLexThreads, 1>();  // read out before the next window clears it
+            }
+#pragma unroll
+            for (int off = 16; off > 0; off >>= 1) best = fmaxf(best, __shfl_xor_sync(0xffffffffu, best, off));
+            if (lane == 0) s_lmax[ltid >> 5] = best;
+            lex_sync<kFusedLexThreads, 1>();
+            if (ltid == 0) {
+                float m = 0.0f;
+                for (int w = 0; w < kFusedLexWarps; ++w) m = fmaxf(m, s_lmax[w]);
+                atomicMax(p.lex_peak, __float_as_uint(m > 0.0f ? m : 0.0f));
+            }
+        }
     } else {
         // ---------------- consumer warps ----------------
         const int grp = lane / LPR;
@@ -296,14 +357,19 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
                         score = acc[0];
                     }
                     if (p.mask != nullptr && side_mask[r] == 0) score = -FLT_MAX;
-                    if (lex_row != nullptr) score = hybrid_blend(score, lexv, p.dense_weight, inv);
-                    // Cheap float pre-check; only candidates at or above the threshold's score
-                    // pay for the exact 64-bit key comparison.
-                    if (!(score < thr_score) || thr == 0ull) {
-                        key = make_key(score, id0 + r);
-                        take = key > thr;
+                    if constexpr (LEX) {
+                        p.out_matrix[static_cast<size_t>(pass) * p.n + row0 + r] = score;
+                    } else {
+                        if (lex_row != nullptr) score = hybrid_blend(score, lexv, p.dense_weight, inv);
+                        // Cheap float pre-check; only candidates at or above the threshold's
+                        // score pay for the exact 64-bit key comparison.
+                        if (!(score < thr_score) || thr == 0ull) {
+                            key = make_key(score, id0 + r);
+                            take = key > thr;
+                        }
                     }
                 }
+                if constexpr (LEX) continue;
                 const uint32_t ballot = __ballot_sync(0xffffffffu, take);
                 if (take) {
                     const int slot = wcount + __popc(ballot & ((1u << lane) - 1u));
@@ -328,6 +394,7 @@ __global__ void __launch_bounds__(kFastThreads, 1) scan_fast_kernel(const ScanPa
             atomicAdd(&s_done, 1);
         }
     }
+    if constexpr (LEX) return;
     __syncthreads();
 
     // The stage ring (free now) holds the merge buffer.

@@ -255,13 +255,8 @@ int check_alignment(int dtype, const void* corpus, const void* row_scales, const
     return ZCGVS_OK;
 }
 
-int launch(const ScanPlan& plan, ScanParams& params, cudaStream_t stream) {
-    const ScanKernelFn kernel = plan.fast ? scan_lookup_fast(plan.mode, plan.jc) : lookup(plan);
-    if (kernel == nullptr) {
-        return fail(ZCGVS_ERR_UNSUPPORTED, "zcgvs: no scan kernel variant for this configuration");
-    }
-    cudaError_t status = ensure_smem_optin(reinterpret_cast<const void*>(kernel));
-    if (status != cudaSuccess) return fail_cuda(status, "cudaFuncSetAttribute(scan_kernel)");
+// The plan's tile, stage and shared-memory layout fields of the kernel arguments.
+void fill_params(const ScanPlan& plan, ScanParams& params) {
     params.rows_per_tile = plan.rows_per_tile;
     params.ntiles = plan.ntiles;
     params.use_tma = plan.use_tma ? 1 : 0;
@@ -287,6 +282,16 @@ int launch(const ScanPlan& plan, ScanParams& params, cudaStream_t stream) {
     params.smem_query_off = plan.fast ? plan.fast_query_off : plan.smem_query_off;
     params.smem_topk_off = plan.fast ? plan.fast_topk_off : plan.smem_topk_off;
     params.smem_bar_off = plan.fast ? plan.fast_bar_off : plan.smem_bar_off;
+}
+
+int launch(const ScanPlan& plan, ScanParams& params, cudaStream_t stream) {
+    const ScanKernelFn kernel = plan.fast ? scan_lookup_fast(plan.mode, plan.jc) : lookup(plan);
+    if (kernel == nullptr) {
+        return fail(ZCGVS_ERR_UNSUPPORTED, "zcgvs: no scan kernel variant for this configuration");
+    }
+    cudaError_t status = ensure_smem_optin(reinterpret_cast<const void*>(kernel));
+    if (status != cudaSuccess) return fail_cuda(status, "cudaFuncSetAttribute(scan_kernel)");
+    fill_params(plan, params);
     const dim3 grid(static_cast<unsigned>(plan.passes), static_cast<unsigned>(plan.grid_rows));
     const int threads = plan.fast ? kFastThreads : kScanThreads;
     const int smem = plan.fast ? plan.fast_smem : plan.smem_total;
@@ -440,20 +445,135 @@ int run_scan_topk(const ScanPlan& plan, const void* corpus, float scale, const f
     return launch(plan, params, stream);
 }
 
-// Hybrid workspace: the scan's, then lexical scores [batch][n], then partial maxima.
+// Hybrid workspace: the scan's, then lexical scores [batch][n], then the lexical kernel's
+// partial maxima, then for one query the dense scores [n] of the hybrid scan, the select
+// kernel's global candidates (k per CTA, one CTA per SM) and its cross-CTA state.
 struct HybridLayout {
-    size_t scan = 0, lex = 0, part = 0, total = 0;
+    size_t scan = 0, lex = 0, part = 0, dense = 0, select = 0, state = 0, total = 0;
     int parts = 0;
+    int select_ctas = 0;
 };
 
-HybridLayout hybrid_layout(size_t scan_ws, long long n, int batch) {
+HybridLayout hybrid_layout(size_t scan_ws, long long n, int batch, int k) {
     HybridLayout h;
     h.parts = lexical_parts(n);
+    const int sms = device_sm_count();
     h.scan = round_up(scan_ws, kWorkspaceAlign);
     h.lex = round_up(static_cast<size_t>(batch) * static_cast<size_t>(n) * 4, kWorkspaceAlign);
     h.part = round_up(static_cast<size_t>(batch) * h.parts * 4, kWorkspaceAlign);
-    h.total = h.scan + h.lex + h.part;
+    if (batch == 1) {
+        h.dense = round_up(static_cast<size_t>(n) * 4, kWorkspaceAlign);
+        h.select_ctas = static_cast<int>(std::min<long long>(sms, (n + 3) / 4));
+        h.select = round_up(static_cast<size_t>(h.select_ctas) * static_cast<size_t>(k) * 8, kWorkspaceAlign);
+        h.state = round_up(sizeof(HybridSelectState), kWorkspaceAlign);
+    }
+    h.total = h.scan + h.lex + h.part + h.dense + h.select + h.state;
     return h;
+}
+
+// Shared-memory layout of the hybrid scan with lexical warps (scan_fast_kernel<MODE, JC, true>):
+// the stage ring, the query, the CTA's BM25 accumulator, the ring's barriers.
+struct FusedPlan {
+    int stages = 0;
+    int query_off = 0;
+    int lex_off = 0;
+    int bar_off = 0;
+    int smem = 0;
+    int lex_window = 0;
+};
+
+// The hybrid scan runs one query on the single-query fast-path tiles (bulk copies), with an
+// index whose postings are sorted and 16-byte aligned. Its BM25 accumulator covers the CTA's
+// documents in as few windows as keep the stage ring as deep as it would be without it (at most
+// four stages: a shallower ring costs the dense stream more than a second window of posting
+// searches costs the lexical warps). Otherwise the lexical kernel and the blending scan run one
+// after the other.
+bool plan_fused(const ScanPlan& plan, long long n, int batch, int k, const LexIndex& lexi, FusedPlan& f) {
+    if (batch != 1 || plan.jc == 0 || !plan.use_tma || !lexi.vec || k > kSelCap - 64) return false;
+    if (scan_lookup_fused(plan.mode, plan.jc) == nullptr) return false;
+    const long long per_cta = (plan.ntiles + plan.grid_rows - 1) / plan.grid_rows * plan.rows_per_tile;
+    const long long span = std::min(per_cta, n);
+    const long long query = static_cast<long long>(round_up(static_cast<size_t>(plan.query_bytes), 128));
+    // The kernel's static shared memory (slot bounds, reductions) stays under 4 KB.
+    const long long budget = device_max_smem() - 4096;
+    const long long base = query + 2 * kMaxStages * 8 + 128;
+    auto stages_with = [&](long long lex_bytes) {
+        return base + lex_bytes >= budget ? 0LL
+                                          : std::min<long long>(kMaxStages, (budget - base - lex_bytes) / plan.stage_bytes);
+    };
+    const long long wanted = std::min<long long>(4, stages_with(0));
+    long long window = 0, lex_bytes = 0, stages = 0;
+    for (int windows = 1; windows <= 8; ++windows) {
+        window = (span + windows - 1) / windows;
+        lex_bytes = static_cast<long long>(round_up(static_cast<size_t>(window) * 4, 128));
+        stages = stages_with(lex_bytes);
+        if (stages >= wanted) break;
+    }
+    if (stages < 2) return false;
+    f.stages = static_cast<int>(stages);
+    f.lex_window = static_cast<int>(window);
+    f.query_off = static_cast<int>(round_up(static_cast<size_t>(stages * plan.stage_bytes), 128));
+    f.lex_off = f.query_off + static_cast<int>(query);
+    f.bar_off = f.lex_off + static_cast<int>(lex_bytes);
+    f.smem = f.bar_off + 2 * kMaxStages * 8;
+    return f.smem <= budget;
+}
+
+// One query: the hybrid scan writes the dense scores, the lexical scores and one lexical
+// maximum per CTA; the select kernel (a programmatic dependent launch) blends and selects.
+int run_hybrid_fused(const ScanPlan& plan, const FusedPlan& f, const HybridLayout& h, const LexIndex& lexi,
+                     const void* corpus, float scale, const float* row_scales, int64_t doc_count, int dim,
+                     const float* queries, const uint8_t* mask, const int* query_terms, int term_stride,
+                     float dense_weight, int k, int* out_indices, float* out_scores, uint8_t* ws,
+                     cudaStream_t stream) {
+    const ScanKernelFn kernel = scan_lookup_fused(plan.mode, plan.jc);
+    cudaError_t status = ensure_smem_optin(reinterpret_cast<const void*>(kernel));
+    if (status != cudaSuccess) return fail_cuda(status, "cudaFuncSetAttribute(scan_fast_kernel<lexical>)");
+    float* lex = reinterpret_cast<float*>(ws + h.scan);
+    float* dense = reinterpret_cast<float*>(ws + h.scan + h.lex + h.part);
+    unsigned long long* select_cand = reinterpret_cast<unsigned long long*>(ws + h.scan + h.lex + h.part + h.dense);
+    HybridSelectState* state =
+        reinterpret_cast<HybridSelectState*>(ws + h.scan + h.lex + h.part + h.dense + h.select);
+    unsigned int* counters = reinterpret_cast<unsigned int*>(ws + 16);
+    unsigned long long* lists = reinterpret_cast<unsigned long long*>(ws + plan.ws_header);
+    ScanParams params{};
+    params.corpus = static_cast<const uint8_t*>(corpus);
+    params.row_scales = row_scales;
+    params.scale = scale;
+    params.n = doc_count;
+    params.dim = dim;
+    params.queries = queries;
+    params.batch = 1;
+    params.mask = mask;
+    params.k = k;
+    params.status = reinterpret_cast<unsigned int*>(ws);
+    params.counters = counters;
+    params.lists = lists;
+    params.out_idx = out_indices;
+    params.out_scores = out_scores;
+    params.out_matrix = dense;
+    params.lexi = lexi;
+    params.lex_terms = query_terms;
+    params.lex_stride = term_stride;
+    params.lex_out = lex;
+    params.lex_peak = &state->peak;
+    fill_params(plan, params);
+    params.stages = f.stages;
+    params.spill_stride = 0;
+    params.smem_query_off = f.query_off;
+    params.smem_topk_off = 0;
+    params.smem_bar_off = f.bar_off;
+    params.smem_lex_off = f.lex_off;
+    params.lex_window = f.lex_window;
+    const dim3 grid(1u, static_cast<unsigned>(plan.grid_rows));
+    {
+        KernelTimer timer("scan", stream);
+        kernel<<<grid, kFusedThreads, f.smem, stream>>>(params);
+    }
+    status = cudaGetLastError();
+    if (status != cudaSuccess) return fail_cuda(status, "scan_fast_kernel<lexical> launch");
+    return launch_hybrid_select(dense, lex, state, dense_weight, doc_count, k, 0u, select_cand, out_indices,
+                                out_scores, h.select_ctas, stream);
 }
 
 }  // namespace
@@ -489,7 +609,7 @@ int zcgvs_scan_topk(const void* corpus, int dtype, float scale, const float* row
 size_t zcgvs_hybrid_topk_workspace_bytes(int dtype, int64_t doc_count, int dim, int batch, int k) {
     if (doc_count <= 0 || dim <= 0 || batch <= 0 || k <= 0) return 0;
     const size_t scan = zcgvs_scan_topk_workspace_bytes(dtype, doc_count, dim, batch, k);
-    return zc::hybrid_layout(scan, doc_count, batch).total;
+    return zc::hybrid_layout(scan, doc_count, batch, k).total;
 }
 
 int zcgvs_hybrid_topk(const void* corpus, int dtype, float scale, const float* row_scales, int64_t doc_count,
@@ -508,13 +628,22 @@ int zcgvs_hybrid_topk(const void* corpus, int dtype, float scale, const float* r
         return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs_hybrid_topk: null or empty lexical index");
     }
     const HybridLayout h = hybrid_layout(zcgvs_scan_topk_workspace_bytes(dtype, doc_count, dim, batch, k),
-                                         doc_count, batch);
+                                         doc_count, batch, k);
     if (workspace == nullptr || workspace_bytes < h.total) {
         return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: workspace smaller than zcgvs_hybrid_topk_workspace_bytes()");
     }
     if (!aligned16(workspace)) return fail(ZCGVS_ERR_INVALID_ARG, "zcgvs: workspace must be 16-byte aligned");
     uint8_t* ws = static_cast<uint8_t*>(workspace);
     const cudaStream_t st = static_cast<cudaStream_t>(stream);
+    if (lexical) {
+        const LexIndex lexi = lex_index(reinterpret_cast<const long long*>(offsets), posting_docs, posting_weights,
+                                        vocab_size, doc_count, true);
+        FusedPlan f;
+        if (plan_fused(plan, doc_count, batch, k, lexi, f)) {
+            return run_hybrid_fused(plan, f, h, lexi, corpus, scale, row_scales, doc_count, dim, queries, mask,
+                                    query_terms, term_stride, dense_weight, k, out_indices, out_scores, ws, st);
+        }
+    }
     HybridArgs hy;
     if (lexical) {
         hy.lex = reinterpret_cast<float*>(ws + h.scan);

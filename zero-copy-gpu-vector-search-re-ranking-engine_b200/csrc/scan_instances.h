@@ -15,6 +15,8 @@ ScanKernelFn scan_lookup_i8(int mode, int qb, int jc, bool l2, bool emit);
 ScanKernelFn scan_lookup_bin(int qb, bool emit);
 // Warp-specialised single-query kernel (scan_fast.cuh), 16 lanes per row, `jc` sweeps.
 ScanKernelFn scan_lookup_fast(int mode, int jc);
+// Its hybrid variant with lexical warps (dense scores and BM25 scores out, no selection).
+ScanKernelFn scan_lookup_fused(int mode, int jc);
 
 }  // namespace zc
 

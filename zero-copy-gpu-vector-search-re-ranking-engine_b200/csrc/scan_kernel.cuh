@@ -26,6 +26,7 @@
 #include <type_traits>
 
 #include "common.cuh"
+#include "lexical_device.cuh"
 #include "topk_cta.cuh"
 
 namespace zc {
@@ -79,6 +80,19 @@ struct ScanParams {
     const float* lex_part;
     int lex_parts;
     float dense_weight;
+    // Hybrid scan with lexical warps (scan_fast_kernel<MODE, JC, true>, one query): the CSR
+    // index, the query terms [lex_stride], the lexical scores out [n] and their maximum, raised
+    // with an unsigned atomicMax on the bits of each CTA's max(0, max) (valid for non-negative
+    // floats); the dense scores go to out_matrix [n]. The BM25 accumulator (lex_window
+    // documents) sits at smem_lex_off of the dynamic shared memory; a CTA scores its documents
+    // lex_window at a time.
+    LexIndex lexi;
+    const int* lex_terms;
+    int lex_stride;
+    float* lex_out;
+    unsigned int* lex_peak;
+    int smem_lex_off;
+    int lex_window;
 };
 
 // Convex blend of a dense score with a max-normalised lexical score in the reference's

@@ -44,9 +44,9 @@ __device__ __forceinline__ bool topk_offer_check(const TopkSmem& t, int q, u64 k
 
 // Warp-cooperative descending bitonic sort of 32 * E keys held in registers, element index
 // lane * E + i. Strides below E swap registers inside a lane; larger strides exchange the
-// same register with the partner lane (lane ^ stride / E).
-template <int E>
-__device__ __forceinline__ void warp_sort_desc_regs(u64 (&v)[E], int lane) {
+// same register with the partner lane (lane ^ stride / E). T: any unsigned key type.
+template <int E, typename T = u64>
+__device__ __forceinline__ void warp_sort_desc_regs(T (&v)[E], int lane) {
 #pragma unroll
     for (int size = 2; size <= 32 * E; size <<= 1) {
 #pragma unroll
@@ -58,8 +58,8 @@ __device__ __forceinline__ void warp_sort_desc_regs(u64 (&v)[E], int lane) {
                     if (j > i) {
                         const int e = lane * E + i;
                         const bool descending = (e & size) == 0;
-                        const u64 a = v[i];
-                        const u64 b = v[j];
+                        const T a = v[i];
+                        const T b = v[j];
                         const bool swap = descending ? (a < b) : (a > b);
                         v[i] = swap ? b : a;
                         v[j] = swap ? a : b;
@@ -72,9 +72,9 @@ __device__ __forceinline__ void warp_sort_desc_regs(u64 (&v)[E], int lane) {
                 for (int i = 0; i < E; ++i) {
                     const int e = lane * E + i;
                     const bool descending = (e & size) == 0;
-                    const u64 other = __shfl_xor_sync(0xffffffffu, v[i], lane_mask);
-                    const u64 hi = v[i] > other ? v[i] : other;
-                    const u64 lo = v[i] > other ? other : v[i];
+                    const T other = __shfl_xor_sync(0xffffffffu, v[i], lane_mask);
+                    const T hi = v[i] > other ? v[i] : other;
+                    const T lo = v[i] > other ? other : v[i];
                     v[i] = (lower == descending) ? hi : lo;
                 }
             }
