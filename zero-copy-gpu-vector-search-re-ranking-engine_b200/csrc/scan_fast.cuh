@@ -44,7 +44,7 @@ constexpr int kSelE = 8;
 constexpr int kSelCap = 32 * kSelE;
 
 // Hybrid variant: lexical warps after the producer (warps kFusedLexWarp0 ...).
-constexpr int kFusedLexWarps = 3;
+constexpr int kFusedLexWarps = 7;
 constexpr int kFusedLexWarp0 = kFastConsumers + 1;
 constexpr int kFusedLexThreads = kFusedLexWarps * 32;
 constexpr int kFusedThreads = (kFastConsumers + 1 + kFusedLexWarps) * 32;
