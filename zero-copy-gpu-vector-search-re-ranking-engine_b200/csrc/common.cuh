@@ -175,6 +175,17 @@ __device__ __forceinline__ u64 l2_policy_evict_first() {
     return policy;
 }
 
+__device__ __forceinline__ u64 l2_policy_evict_last() {
+    u64 policy;
+    asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(policy));
+    return policy;
+}
+
+// A 4-byte global store with an L2 cache policy (data the next kernel reads back soon).
+__device__ __forceinline__ void st_global_hint(float* ptr, float value, u64 policy) {
+    asm volatile("st.global.L2::cache_hint.f32 [%0], %1, %2;" ::"l"(ptr), "f"(value), "l"(policy) : "memory");
+}
+
 // bulk_copy_g2s with an L2 cache policy from createpolicy.
 __device__ __forceinline__ void bulk_copy_g2s_hint(void* dst_smem, const void* src_gmem, uint32_t bytes,
                                                    u64* bar, u64 policy) {

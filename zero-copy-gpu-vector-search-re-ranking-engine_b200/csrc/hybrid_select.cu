@@ -117,10 +117,12 @@ __global__ void __launch_bounds__(kSelectThreads, 1) hybrid_select_kernel(const 
             }
         }
     };
+    // The peak's load goes out before the score loads, so it does not queue behind them.
+    const unsigned int peak_bits = tid == 0 ? __ldcg(&p.state->peak) : 0u;
     fetch(0);
     if (tid == 0) {
         // max(0, max lexical score): raised as the bits of non-negative floats.
-        const float peak = __uint_as_float(__ldcg(&p.state->peak));
+        const float peak = __uint_as_float(peak_bits);
         s_inv = peak > 0.0f ? __fdiv_rn(1.0f, peak) : 0.0f;
         s_floor = 0u;
         s_count = 0;

@@ -247,6 +247,7 @@ __global__ void __launch_bounds__(LEX ? kFusedThreads : kFastThreads, 1) scan_fa
             __shared__ long long s_hi[kLexSlots];
             __shared__ float s_lmax[kFusedLexWarps];
             const int ltid = tid - kFusedLexWarp0 * 32;
+            const u64 keep_policy = l2_policy_evict_last();
             float* acc = reinterpret_cast<float*>(smem + p.smem_lex_off);
             const long long d_begin = static_cast<long long>(t_begin) * R;
             const int count = static_cast<int>(min(static_cast<long long>(my_tiles) * R, p.n - d_begin));
@@ -266,7 +267,7 @@ __global__ void __launch_bounds__(LEX ? kFusedThreads : kFastThreads, 1) scan_fa
                 lex_sync<kFusedLexThreads, 1>();
                 for (int i = ltid; i < wc; i += kFusedLexThreads) {
                     const float v = acc[i];
-                    out[d0 + i] = v;
+                    st_global_hint(out + d0 + i, v, keep_policy);  // kept in L2 for the select kernel
                     best = fmaxf(best, v);
                 }
                 lex_sync<kFusedLexThreads, 1>();  // read out before the next window clears it
@@ -295,6 +296,7 @@ __global__ void __launch_bounds__(LEX ? kFusedThreads : kFastThreads, 1) scan_fa
         }
         const float qscale = s_qscale[0];
         const float inv = s_inv;
+        const u64 keep_policy = LEX ? l2_policy_evict_last() : 0ull;
         const float* lex_row = p.lex != nullptr ? p.lex + static_cast<size_t>(pass) * p.n : nullptr;
         u64* region = cbuf + warp * kRegionCap;
         unsigned long long* wspill = spill + warp * warp_rows;
@@ -358,7 +360,8 @@ __global__ void __launch_bounds__(LEX ? kFusedThreads : kFastThreads, 1) scan_fa
                     }
                     if (p.mask != nullptr && side_mask[r] == 0) score = -FLT_MAX;
                     if constexpr (LEX) {
-                        p.out_matrix[static_cast<size_t>(pass) * p.n + row0 + r] = score;
+                        // Kept in L2 for the select kernel that reads it next.
+                        st_global_hint(p.out_matrix + static_cast<size_t>(pass) * p.n + row0 + r, score, keep_policy);
                     } else {
                         if (lex_row != nullptr) score = hybrid_blend(score, lexv, p.dense_weight, inv);
                         // Cheap float pre-check; only candidates at or above the threshold's
