@@ -293,13 +293,28 @@ __device__ inline bool topk_merge_lists_small(const TopkSmem& t, int q_local, co
     return true;
 }
 
-// How many of the n distinct keys in keys[] are larger than key (its rank, 0 = largest). All
-// lanes of a warp read the same entry at once (a broadcast).
+// How many of the n distinct keys in keys[] (shared memory) are larger than key (its rank, 0 =
+// largest). All lanes of a warp read the same entries at once (broadcasts). Eight keys per step
+// in four 16-byte loads (when keys[] is 16-byte aligned) into independent counters, so the loads
+// of a step are in flight together instead of one shared-memory latency per key.
 __device__ __forceinline__ int key_rank(const u64* keys, int n, u64 key) {
-    int r = 0;
-#pragma unroll 4
-    for (int j = 0; j < n; ++j) r += keys[j] > key ? 1 : 0;
-    return r;
+    int r[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+    int j = 0;
+    if ((reinterpret_cast<uintptr_t>(keys) & 15u) == 0) {
+        const ulonglong2* k2 = reinterpret_cast<const ulonglong2*>(keys);
+        for (; j + 8 <= n; j += 8) {
+            ulonglong2 v[4];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) v[u] = k2[j / 2 + u];
+#pragma unroll
+            for (int u = 0; u < 4; ++u) {
+                r[2 * u] += v[u].x > key ? 1 : 0;
+                r[2 * u + 1] += v[u].y > key ? 1 : 0;
+            }
+        }
+    }
+    for (; j < n; ++j) r[0] += keys[j] > key ? 1 : 0;
+    return ((r[0] + r[1]) + (r[2] + r[3])) + ((r[4] + r[5]) + (r[6] + r[7]));
 }
 
 // Lists at least as many as k: the floor F is the k-th largest list head (found by counting
