@@ -344,10 +344,14 @@ int zcgvs_sharded_clear_status(zcgvs_sharded* handle, void* stream);
 /* ---------------------------------------------------------------------------------------
  * Hybrid lexical + dense search. Replaces the hybrid stages of Searcher::recordPipeline
  * (src/search/searcher.cpp:236-263: per query launchBm25, launchMaxPositive and
- * launchFuseScores over [batch, N] score matrices, then launchTopK) with two kernels: a BM25
- * kernel that writes each query's lexical scores and partial maxima to the workspace, and the
- * fused scan, which blends score = w * dense + ((1 - w) * lex) * (1 / max(lex)) (0 when the max
- * is not positive; src/cuda/lexical.cu:66-72) before its top-k.
+ * launchFuseScores over [batch, N] score matrices, then launchTopK) with two kernels, blending
+ * score = w * dense + ((1 - w) * lex) * (1 / max(lex)) (0 when the max is not positive;
+ * src/cuda/lexical.cu:66-72) before the top-k. One query (batch 1, k <= 192, a dense dtype and
+ * dimension of the single-query scan, 16-byte aligned posting arrays): a scan whose CTAs also
+ * accumulate the BM25 scores of their own documents, writing both score vectors to the
+ * workspace, then a blend + top-k kernel launched as its programmatic dependent. Otherwise: a
+ * BM25 kernel that writes each query's lexical scores and partial maxima, then the scan that
+ * blends before its top-k. Both give the same results, bit for bit.
  *
  *   offsets / posting_docs / posting_weights : the CSR index of the reference LexicalIndex
  *                     (include/zcgvs/data/lexical_index.hpp:14-46): offsets [vocab_size + 1]
