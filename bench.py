@@ -65,6 +65,8 @@ def parse_args():
                     help="skip the row-sharded config 4 measurement that follows the replica workloads")
     ap.add_argument("--sharded-docs", type=int, default=None,
                     help="corpus rows of the row-sharded measurement (default: config 4's 50,000,000)")
+    ap.add_argument("--no-searcher", action="store_true",
+                    help="skip the end-to-end rate through the C++ Searcher (one-query workloads, one GPU)")
     return ap.parse_args()
 
 
@@ -309,6 +311,11 @@ class Workload:
     def kernel_ms(self, kern, steps):
         return sum(kern[t][0] for t in self.dominant) / steps
 
+    # Arguments of the package's searcher_e2e program for this workload's shape (one-query
+    # workloads), or None: the end-to-end rate through the C++ drop-in Searcher.
+    def searcher_args(self):
+        return None
+
     # Batch-1 workloads replay CUDA graphs, as a serving loop does (the reference's Searcher
     # captures its pipeline the same way): one graph per query of a pool for the device-resident
     # steps, and one over the device staging buffers for the end-to-end steps. The graphs hold
@@ -407,6 +414,11 @@ class Cfg2(Workload):
         if batch >= 64:
             self.steps, self.warmup = 20, 3
 
+    def searcher_args(self):
+        if self.B != 1:
+            return None
+        return [f"docs={self.N}", f"dim={self.D}", "dtype=4", f"k={self.K}", "metric=0"]
+
     units = property(lambda self: self.B)
     launches = property(lambda self: 12 if self.B >= 64 else 1)
 
@@ -485,6 +497,9 @@ class Cfg1(Workload):
     units = 1
     launches = 1
     steps, warmup = 300, 10
+
+    def searcher_args(self):
+        return [f"docs={self.N}", f"dim={self.D}", "dtype=0", f"k={self.K}", "metric=0"]
 
     def setup(self, torch, zc, device, rank, world):
         self.torch, self.zc = torch, zc
@@ -744,6 +759,12 @@ class Cfg5(Workload):
     3-12 Zipf terms, de-duplicated; score = 0.5 * dense + 0.5 * lex / max(lex)."""
 
     N, D, K, V, NQ = 2_000_000, 384, 10, 30_000, 1000
+
+    def searcher_args(self):
+        # The Searcher's hybrid path with a synthetic index of the same statistics (Zipf(1.1)
+        # terms, 200 token draws per document, queries of 3-12 terms), built by the program.
+        return [f"docs={self.N}", f"dim={self.D}", "dtype=1", f"k={self.K}", "metric=0", f"vocab={self.V}",
+                "mean_len=200", "terms=12", "weight=0.5"]
     name = "cfg5_hybrid_bm25_f16_2Mx384_top10_b1"
     dtype = "f16 + f32"
     units = 1
@@ -946,6 +967,27 @@ def run_reference_sampled(args, wl, steps, warmup):
     emit(json.dumps(line))
 
 
+def searcher_e2e(wl):
+    """End-to-end rate through the C++ drop-in layer: the package's searcher_e2e program runs
+    zcgvs::Searcher::search on a host query + copyResultToHost per query (graph replay once
+    captured), on this workload's shape, in its own process on this GPU."""
+    argv = wl.searcher_args()
+    if argv is None:
+        return None
+    exe = PKG / "searcher_e2e"
+    if not exe.exists():
+        return {"unavailable": f"{exe.name} is not built (make -C {PKG.name})"}
+    res = subprocess.run([str(exe)] + argv + ["steps=1000", "warmup=30"], capture_output=True, text=True,
+                         timeout=600)
+    if res.returncode != 0:
+        return {"unavailable": (res.stderr.strip().splitlines() or ["exit status %d" % res.returncode])[-1]}
+    out = json.loads(res.stdout.strip().splitlines()[-1])
+    return {"value": out["queries_per_s"], "unit": UNIT, "h2d_bytes_per_step": out["h2d_bytes_per_step"],
+            "d2h_bytes_per_step": out["d2h_bytes_per_step"], "ms_per_query": out["ms_per_query"],
+            "search_gpu_ms_mean": out["search_gpu_ms_mean"], "steps": out["steps"], "graph": out["graph"],
+            "api": "zcgvs::Searcher::search (host query) + copyResultToHost, C++ (" + exe.name + ")"}
+
+
 def measure_sharded(args, torch, zc, device, rank, world):
     """Row-sharded config 4 (fp16 50M x 768, batch 4,096, top-100) through the native sharded
     handle, in the processes of the replica run: rank r holds rows shard_bounds(N, P, r), a step
@@ -1106,6 +1148,8 @@ def run_ours(args):
         dist.all_reduce(t, op=dist.ReduceOp.SUM)
         e2e_ranks = [round(float(v), 4) for v in t.tolist()]
     line_extra = {}
+    if rank == 0 and world == 1 and not args.no_searcher:
+        line_extra["e2e_searcher"] = searcher_e2e(wl)
     if wl.scaling == "weak" and not args.no_sharded:
         # The replica workloads have no exchange on their data path; the row-sharded search does.
         # Measure it in the same processes (config 4: the corpus split over the ranks).
