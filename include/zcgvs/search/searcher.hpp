@@ -86,6 +86,11 @@ private:
     std::uint64_t graph_captures_ = 0;
     std::uint64_t graph_launches_ = 0;
 
+    // Results of at most kHostResultMax (id, score) pairs are written by the search's last
+    // kernel straight into the pinned host buffers (device-accessible under unified addressing),
+    // saving the two device-to-host copies; larger ones go through device buffers and copies.
+    static constexpr long long kHostResultMax = 16384;
+    bool host_out_ = false;
     int current_k_ = 0;
     int current_batch_ = 0;
     double last_gpu_ms_ = 0.0;

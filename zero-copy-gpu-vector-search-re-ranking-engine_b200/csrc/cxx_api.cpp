@@ -655,8 +655,12 @@ void Searcher::recordPipeline(std::int64_t doc_count, int batch, const SearchPar
                               std::vector<std::uint64_t>* key) {
     const bool rescore = rescoreEnabled(params);
     const int width = rescore ? params.rescore_candidates : params.k;
-    int* ids = rescore ? d_coarse_indices_.data() : d_out_indices_.data();
-    float* scores = rescore ? d_coarse_values_.data() : d_out_values_.data();
+    // The final results go to the pinned host buffers themselves when they are small (host_out_):
+    // the last kernel writes them across the bus, so copyResultToHost has no copy to make.
+    int* out_ids = host_out_ ? h_out_indices_.data() : d_out_indices_.data();
+    float* out_scores = host_out_ ? h_out_values_.data() : d_out_values_.data();
+    int* ids = rescore ? d_coarse_indices_.data() : out_ids;
+    float* scores = rescore ? d_coarse_values_.data() : out_scores;
     const int dtype = static_cast<int>(store_.dtype());
     const int metric = static_cast<int>(params.metric);
     const std::int64_t n = doc_count;
@@ -676,8 +680,7 @@ void Searcher::recordPipeline(std::int64_t doc_count, int batch, const SearchPar
         launchOrKey(key, "zcgvs_rescore_topk", zcgvs_rescore_topk, stream, rescore_store_->deviceData(),
                     static_cast<int>(rescore_store_->dtype()), rescore_store_->scale(), rescore_store_->rowScales(),
                     rescore_store_->docCount(), dim_, static_cast<const float*>(d_queries_.data()), batch,
-                    static_cast<const int*>(d_coarse_indices_.data()), width, metric, params.k, d_out_indices_.data(),
-                    d_out_values_.data());
+                    static_cast<const int*>(d_coarse_indices_.data()), width, metric, params.k, out_ids, out_scores);
     }
 }
 
@@ -696,6 +699,7 @@ void Searcher::search(const float* host_queries, int dim, int batch, const Searc
         d_query_terms_.copyFromHost(h_query_terms_.data(), terms, stream.get());
     }
 
+    host_out_ = static_cast<long long>(batch) * params.k <= kHostResultMax;
     const bool graph_path = params.use_graph;
     if (graph_path) {
         std::vector<std::uint64_t> key;
@@ -740,8 +744,10 @@ void Searcher::search(const float* host_queries, int dim, int batch, const Searc
 HostTopK Searcher::copyResultToHost(const CudaStream& stream) {
     if (current_k_ == 0 || current_batch_ == 0) throw std::runtime_error("zcgvs: copyResultToHost called before search");
     const std::size_t elements = static_cast<std::size_t>(current_batch_) * static_cast<std::size_t>(current_k_);
-    d_out_indices_.copyToHost(h_out_indices_.data(), elements, stream.get());
-    d_out_values_.copyToHost(h_out_values_.data(), elements, stream.get());
+    if (!host_out_) {
+        d_out_indices_.copyToHost(h_out_indices_.data(), elements, stream.get());
+        d_out_values_.copyToHost(h_out_values_.data(), elements, stream.get());
+    }
     // The device status word (first 4 bytes of the workspace) travels with the result.
     ZCGVS_CUDA_CHECK(cudaMemcpyAsync(h_status_.data(), d_workspace_.data(), sizeof(std::uint32_t),
                                      cudaMemcpyDeviceToHost, stream.get()));
