@@ -143,6 +143,11 @@ int zcgvs_kernel_timing_read(const char* tag, double* total_ms, int* launches);
  *   id_base     : added to every row index (global ids of a row shard); 0 for a whole corpus.
  *   out_indices : [batch, k] int32 document ids, descending by score.
  *   out_scores  : [batch, k] fp32 scores.
+ *   Outputs may be device memory or pinned host memory (cudaHostAlloc / cudaMallocHost, which
+ *   kernels can address under unified addressing): the last kernel then writes the result
+ *   across the bus itself and no device-to-host copy is needed (worth it for small results;
+ *   the same holds for zcgvs_hybrid_topk and zcgvs_rescore_topk). Inputs and the workspace
+ *   stay in device memory.
  * --------------------------------------------------------------------------------------- */
 size_t zcgvs_scan_topk_workspace_bytes(int dtype, int64_t doc_count, int dim, int batch, int k);
 
