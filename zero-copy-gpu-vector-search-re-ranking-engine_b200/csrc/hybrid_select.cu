@@ -267,9 +267,7 @@ __global__ void __launch_bounds__(kSelectThreads, 1) hybrid_select_kernel(const 
     __syncthreads();
     for (int c = tid; c < G; c += kSelectThreads) {
         const u64 mine = heads[c];
-        int rank = 0;
-#pragma unroll 8
-        for (int j = 0; j < G; ++j) rank += heads[j] > mine ? 1 : 0;
+        const int rank = key_rank(heads, G, mine);  // heads is 16-byte aligned: eight keys a step
         if (rank == p.k - 1 && mine != 0ull) atomicMax(&s_floor_key, mine);
     }
     __syncthreads();
